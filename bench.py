@@ -1,0 +1,402 @@
+"""MoE-layer benchmark (Mixtral-8x7B shape, 4096 prefill tokens per GPU).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--config NAME]
+
+One step = one full MoE-layer forward (router -> permute -> grouped gated GEMM
+-> grouped down GEMM -> combine) over one batch of synthetic tokens.  Inputs
+are resident in HBM for ``value``; ``e2e`` goes through the public API
+(``FusedMoE.forward``) with the tokens copied in from pinned host memory and
+the output copied back inside the timed region.  With N > 1 GPUs (torchrun)
+the layer is expert-parallel (``EPFusedMoE``: experts sharded, tokens
+all-to-all over NCCL), each rank bringing its own 4096 tokens (weak scaling);
+time = max over ranks.
+
+``--impl reference`` times the CPU restatement of the reference's torch path
+(oracle/moe_oracle.py, the reference's per-call expert restack included) on
+the host cores over a bounded token sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "MoE-layer tokens/s at Mixtral-8x7B shape (H4096 E8 top2 I14336, 4096 prefill tokens per GPU)"
+UNIT = "tokens/s"
+DATA = "synthetic: seeded N(0,0.02) weights, N(0,1) activations, N(0,1) per-expert router bias (fp32 router)"
+L2_NOTE = "L2 flushed (256 MB write) before every timed step; weights 2.8 GB > 126 MB L2"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def committed_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))
+        except Exception:
+            return {}
+    return {}
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (SM clock, reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, path):
+        self.path = path
+        self.proc = None
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self, gpus):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in gpus:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        loaded = [s for s in sm if s > 0.5 * (mx or max(sm))] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------- GPU arm
+def build_layer(cfg, d, device):
+    from reframework_b200.moe import FusedMoE
+    moe = FusedMoE(cfg.experts, cfg.top_k, cfg.hidden, cfg.inter, dtype=cfg.dtype,
+                   router_dtype=torch.float32, device=device)
+    with torch.no_grad():
+        moe.gate.copy_(d["gate"])
+        w1b, w2b = moe._resident_banks()
+        w1b.copy_(d["w1"])
+        w2b.copy_(d["w2"])
+    if d["bias"] is not None:
+        moe.set_router_bias(d["bias"][0])
+    return moe
+
+
+def staged_forward(moe, x, ev):
+    """FusedMoE.forward (resident, no shared experts) with an event between stages."""
+    from reframework_b200 import kernels as K
+    ev[0].record()
+    w, ids32, _, _, _ = moe._router(x, ids32=True, ids64=False)
+    ev[1].record()
+    p = K.permute(ids32, moe.num_experts, x=x)
+    ev[2].record()
+    w1b, w2b = moe._resident_banks()
+    h = torch.empty(p.rows_cap, moe.intermediate_size, dtype=x.dtype, device=x.device)
+    K.grouped_gemm_gated(p.x_perm, w1b, p.offsets, p.counts, h, activation=moe.activation)
+    ev[3].record()
+    y = torch.empty(p.rows_cap, moe.hidden_size, dtype=x.dtype, device=x.device)
+    K.grouped_gemm_down(h, w2b, p.offsets, p.counts, y)
+    ev[4].record()
+    out = torch.empty_like(x)
+    K.combine(y, p.row_of_slot, w, out)
+    ev[5].record()
+    return out
+
+
+LAUNCHES_PER_FORWARD = 7  # router, permute x3 (histogram, scatter, gather), gated GEMM, down GEMM, combine
+
+
+def run_gpu(args):
+    from reframework_b200.workloads import CONFIGS, generate
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg = CONFIGS[args.config]
+    T = cfg.tokens
+    d = generate(cfg, device=str(dev), with_x=False)
+    gx = torch.Generator(device=dev).manual_seed(cfg.seed + 101 + rank)
+    x = torch.randn(T, cfg.hidden, generator=gx, device=dev, dtype=cfg.dtype)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    if world > 1:
+        from reframework_b200.parallel.ep import EPFusedMoE
+        full = build_layer(cfg, d, dev)
+        layer = EPFusedMoE.from_full(full, world, rank, token_sharded=True)
+        del full
+        torch.cuda.empty_cache()
+
+        def fwd(inp):
+            return layer(inp)
+        stage_fn = None
+    else:
+        layer = build_layer(cfg, d, dev)
+        fwd = layer
+        stage_fn = staged_forward
+    del d
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    nev = 6
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            if stage_fn:
+                stage_fn(layer, x, [torch.cuda.Event(enable_timing=True) for _ in range(nev)])
+            else:
+                fwd(x)
+        barrier()
+        clocks = Clocks(os.path.join(ROOT, "gpurun_out", f"clocks_bench_r{rank}.csv")
+                        if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/clocks_r{rank}.csv")
+        if rank == 0:
+            clocks.start()
+        step_ms, stage_ms = [], []
+        for _ in range(args.steps):
+            flush.zero_()
+            if stage_fn:
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(nev)]
+                stage_fn(layer, x, ev)
+                stage_ms.append(ev)
+            else:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fwd(x)
+                e1.record()
+                stage_ms.append([e0, e1])
+        barrier()
+        for ev in stage_ms:
+            step_ms.append(ev[0].elapsed_time(ev[-1]))
+        # ---- e2e through the public API with host buffers
+        xh = x.to("cpu").pin_memory()
+        oh = torch.empty_like(xh).pin_memory()
+        for _ in range(max(1, args.warmup)):
+            oh.copy_(fwd(xh.to(dev, non_blocking=True)), non_blocking=True)
+        barrier()
+        e2e_ms = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            xd = xh.to(dev, non_blocking=True)
+            o = fwd(xd)
+            oh.copy_(o, non_blocking=True)
+            e1.record()
+            e2e_ms.append((e0, e1))
+        barrier()
+        clk = clocks.stop(list(range(world))) if rank == 0 else None
+    e2e_step = [a.elapsed_time(b) for a, b in e2e_ms]
+
+    def maxrank(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = maxrank(sum(step_ms) / len(step_ms))
+    ms_e2e = maxrank(sum(e2e_step) / len(e2e_step))
+    tokens = T * world
+    res = {
+        "metric": METRIC, "value": tokens / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
+        "config": {"workload": cfg.name, "hidden": cfg.hidden, "experts": cfg.experts, "top_k": cfg.top_k,
+                   "inter": cfg.inter, "tokens_per_gpu": T, "global_tokens": tokens,
+                   "router": "fp32 logits + N(0,1) bias", "parallelism": f"ep{world}" if world > 1 else "single",
+                   "l2": L2_NOTE},
+        "e2e": {"value": tokens / (ms_e2e / 1e3), "unit": UNIT,
+                "h2d_bytes_per_step": x.numel() * x.element_size(),
+                "d2h_bytes_per_step": x.numel() * x.element_size(),
+                "ms_per_step": ms_e2e, "api": "FusedMoE.forward" if world == 1 else "EPFusedMoE.forward"},
+        "gpu_launches": LAUNCHES_PER_FORWARD * args.steps if world == 1 else None,
+        "clocks": clk,
+    }
+    if stage_fn:
+        names = ["router", "permute", "gemm_gated", "gemm_down", "combine"]
+        per = {n: statistics.mean(ev[i].elapsed_time(ev[i + 1]) for ev in stage_ms) for i, n in enumerate(names)}
+        res["stages_ms"] = per
+        bf16_peak, hbm_peak, src = peaks()
+        rows = T * cfg.top_k
+        flop_g = 2.0 * rows * cfg.hidden * 2 * cfg.inter
+        flop_d = 2.0 * rows * cfg.inter * cfg.hidden
+        ach = flop_g / (per["gemm_gated"] / 1e3) / 1e12
+        tr = committed_traffic().get("gemm_gated_bytes_per_launch")
+        res["roofline"] = {"kernel": "tc_grouped_gemm<bf16, gated> (K3)", "bound": "tensor",
+                           "achieved": ach, "peak": bf16_peak, "unit": "TFLOP/s", "frac": ach / bf16_peak,
+                           "peak_source": f"{src} bf16 (burst)", "traffic": tr,
+                           "algorithmic_flop_per_launch": flop_g}
+        tot_ms = per["gemm_gated"] + per["gemm_down"]
+        res["gemms_tflops"] = (flop_g + flop_d) / (tot_ms / 1e3) / 1e12
+        res["layer_tflops"] = cfg.flops / (ms / 1e3) / 1e12
+        byt_perm = rows * cfg.hidden * 2 * 2
+        res["hbm"] = {"permute_gbs": byt_perm / (per["permute"] / 1e3) / 1e9,
+                      "combine_gbs": (rows + T) * cfg.hidden * 2 / (per["combine"] / 1e3) / 1e9,
+                      "peak_gbs": hbm_peak}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(cfg, layer, budget_s=args.cpu_budget)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res))
+
+
+# ------------------------------------------------------------ CPU reference arm
+def _cpu_info():
+    info = {"cores": os.cpu_count()}
+    try:
+        flags = open("/proc/cpuinfo").read()
+        info["amx"] = "amx_bf16" in flags
+        for line in flags.splitlines():
+            if line.startswith("model name"):
+                info["cpu"] = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return info
+
+
+def _cpu_layer_forward(x, gate, w1_list, w2_list, bias, top_k):
+    """The reference's resident FusedMoE.forward on the CPU: restack every expert
+    (moe_layer.py:444-445), fp32 router + bias, torch_fused_topk, fused_experts."""
+    from oracle import moe_oracle as O
+    w1 = torch.stack(w1_list, 0)
+    w2 = torch.stack(w2_list, 0)
+    w, ids = O.route(x, gate, top_k, True, bias=bias)
+    return O.fused_experts(x, w1, w2, w, ids)
+
+
+def cpu_baseline(cfg, layer, budget_s=25.0, sample_tokens=1024):
+    """Time the oracle port of the reference layer on the host cores (rank 0, N=1)."""
+    torch.set_num_threads(os.cpu_count())
+    w1b, w2b = layer._resident_banks()
+    w1 = [w.cpu() for w in w1b]
+    w2 = [w.cpu() for w in w2b]
+    gate = layer.gate.detach().cpu()
+    bias = layer.router_bias.cpu() if layer.router_bias is not None else None
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(sample_tokens, cfg.hidden, generator=g).to(cfg.dtype)
+    _cpu_layer_forward(x[:64], gate, w1, w2, bias, cfg.top_k)  # warm-up (thread pool, allocator)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while not times or (time.perf_counter() < t_end and len(times) < 5):
+        t0 = time.perf_counter()
+        _cpu_layer_forward(x, gate, w1, w2, bias, cfg.top_k)
+        times.append(time.perf_counter() - t0)
+    s = statistics.median(times)
+    info = _cpu_info()
+    return {"value": sample_tokens / s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{sample_tokens} of the {cfg.tokens} tokens per call, {len(times)} timed calls "
+                      f"(median {s:.2f} s); restack + fp32 router + torch bf16 experts on the CPU",
+            "cpu": info.get("cpu"), "amx": info.get("amx")}
+
+
+def run_reference(args):
+    """--impl reference: the reference path's CPU restatement on the host cores."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from reframework_b200.workloads import CONFIGS, generate
+    cfg = CONFIGS[args.config]
+    torch.set_num_threads(os.cpu_count())
+    d = generate(cfg, with_x=False)
+    w1 = list(d["w1"])
+    w2 = list(d["w2"])
+    bias = d["bias"][0] if d["bias"] is not None else None
+    sample = args.ref_tokens
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(sample, cfg.hidden, generator=g).to(cfg.dtype)
+    for _ in range(args.warmup):
+        _cpu_layer_forward(x, d["gate"], w1, w2, bias, cfg.top_k)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        _cpu_layer_forward(x, d["gate"], w1, w2, bias, cfg.top_k)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    v = sample / (ms / 1e3)
+    info = _cpu_info()
+    res = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
+        "config": {"workload": cfg.name, "hidden": cfg.hidden, "experts": cfg.experts, "top_k": cfg.top_k,
+                   "inter": cfg.inter, "tokens_per_gpu": cfg.tokens, "sample_tokens_per_step": sample,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{sample} tokens per step (of {cfg.tokens}), reference restack + "
+                                   "fp32 router + per-expert torch bf16 GEMMs",
+                         "cpu": info.get("cpu"), "amx": info.get("amx")},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(res))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--config", default="c2_mixtral_bf16")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=25.0)
+    ap.add_argument("--ref-tokens", type=int, default=512)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,197 @@
+/*
+ * rf_moe.h — C ABI of the B200 (sm_100a) MoE-layer forward.
+ *
+ * One entry point per stage of the MoE layer.  Every call takes raw device
+ * pointers owned by the caller (the library never allocates or frees tensor
+ * memory), int64 sizes, and a CUDA stream; it enqueues work on that stream and
+ * returns an rf_status.  No call synchronises the stream, and no C++
+ * exception crosses this boundary.  rf_moe_last_error() returns the message
+ * of the calling thread's most recent failure.
+ *
+ * Row layout shared by the stages: the T*K (token, slot) pairs are grouped by
+ * expert ("permuted rows").  Expert e owns rows
+ *     [expert_offsets[e], expert_offsets[e] + expert_counts[e])
+ * and every expert_offsets[e] is a multiple of the `align` given to
+ * rf_moe_permute (128 for the grouped GEMMs, 1 for a compact layout).
+ * Within an expert, rows are in ascending flat order t*K+k — the order of the
+ * reference's per-expert boolean selection.  Pad rows (between an expert's
+ * last row and the next expert's first) hold src_slot = -1 and zero inputs.
+ * A buffer of permuted rows needs rf_moe_rows_capacity(T*K, E, align) rows.
+ *
+ * Reference interfaces replaced (paths relative to the Reframework root):
+ *   rf_moe_router_topk      reframework/moe/moe_layer.py:320-344 (FusedMoE.route)
+ *                           reframework/moe/fused.py:32-46 (torch_fused_topk)
+ *   rf_moe_permute          reframework/moe/fused.py:71-80 (bincount + per-expert
+ *                           select + hidden_states[tok] gather)
+ *   rf_moe_gather_rows      reframework/moe/fused.py:80 (hidden_states[tok]);
+ *                           reframework/parallel/dist.py:194-206 (all_to_all
+ *                           chunk packing, for EP dispatch/combine)
+ *   rf_moe_grouped_gemm_gated  reframework/moe/fused.py:81-82 (x @ w1[e].t(),
+ *                           gated_act_and_mul) + reframework/layers/activation.py:15-59
+ *   rf_moe_grouped_gemm_down   reframework/moe/fused.py:83 (inter @ w2[e].t())
+ *   rf_moe_combine          reframework/moe/fused.py:84-86 (y * w, index_add_)
+ *                           + reframework/layers/norm.py:43-53 (residual add, opt-in)
+ */
+#ifndef RF_MOE_H
+#define RF_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void *rf_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+typedef enum {
+  RF_F32 = 0,
+  RF_F16 = 1,
+  RF_BF16 = 2
+} rf_dtype;
+
+typedef enum {
+  RF_ACT_SILU = 0,      /* silu(gate) * up            (activation.py:15-24) */
+  RF_ACT_GELU = 1,      /* gelu(gate) * up, erf form  (activation.py:27-35) */
+  RF_ACT_GELU_TANH = 2  /* gelu_tanh(gate) * up       (activation.py:38-46) */
+} rf_activation;
+
+typedef enum {
+  RF_OK = 0,
+  RF_ERR_ARG = 1,          /* invalid argument (message says which) */
+  RF_ERR_UNSUPPORTED = 2,  /* valid but not implemented for these sizes/dtypes */
+  RF_ERR_CUDA = 3,         /* a CUDA runtime call failed */
+  RF_ERR_DEVICE = 4        /* a kernel reported an error (see rf_moe_device_status) */
+} rf_status;
+
+/* Device-side error codes reported by rf_moe_device_status. */
+#define RF_DEV_OK 0
+#define RF_DEV_BAD_EXPERT_ID 1   /* a routed id was outside [0, E) */
+#define RF_DEV_WAIT_TIMEOUT 2    /* a pipeline wait ran out of time and gave up */
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char *rf_moe_last_error(void);
+
+/* ABI version (major*100 + minor). */
+int rf_moe_version(void);
+
+/* Reads and clears the device-side error word of the current device
+ * (synchronises the device).  *code gets one of RF_DEV_*. */
+int rf_moe_device_status(int *code);
+
+/* Rows needed for the permuted layout of n_pairs = T*K pairs over E experts. */
+int64_t rf_moe_rows_capacity(int64_t n_pairs, int64_t num_experts, int64_t align);
+
+/* Workspace bytes rf_moe_permute needs (caller-allocated device memory). */
+size_t rf_moe_permute_workspace_size(int64_t n_pairs, int64_t num_experts);
+
+/*
+ * K1 — router.  For each token t:
+ *   logit[e] = sum_h x[t,h] * gate[e,h]   (fp32 accumulation, fixed order)
+ *   if round_dtype >= 0: logit rounded to that dtype (the reference runs the
+ *                        router GEMM in the layer dtype, moe_layer.py:324)
+ *   if bias:             logit += bias[e]  (fp32 router with load bias)
+ *   p = softmax(logit) in fp32; top-k by p (descending, ties -> lower id);
+ *   weights = p / sum(top-k p) when renormalize, else p.
+ * entropy_k_min > 0 selects the entropy-adaptive branch of moe_layer.py:327-342
+ * (slots past k_dyn get weight 0; weights always renormalised).
+ * shared_gate (optional, [H] in gate_dtype) also writes
+ *   shared_scale[t] = sigmoid(sum_h x[t,h] * shared_gate[h]).
+ * Outputs: topk_weights [T,K] fp32; topk_ids32 [T,K] and/or topk_ids64 [T,K]
+ * (either may be NULL, not both); logits [T,E] fp32 (NULL to skip).
+ * Requires 1 <= K <= min(E, 16), E <= 1024, H % 8 == 0.
+ * gate == NULL means x already holds the [T,E] logits (H must equal E): the
+ * call is then torch_fused_topk alone.
+ */
+int rf_moe_router_topk(const void *x, int x_dtype, const void *gate, int gate_dtype,
+                       const float *bias, int64_t T, int64_t H, int64_t E, int64_t K,
+                       int renormalize, int round_dtype, int entropy_k_min,
+                       const void *shared_gate, float *shared_scale,
+                       float *topk_weights, int32_t *topk_ids32, int64_t *topk_ids64,
+                       float *logits, rf_stream_t stream);
+
+/*
+ * K2 — counting-sort permute of the T*K pairs by expert (stable), plus the
+ * gather of the activation rows.  Inputs: topk_ids [T,K] int32.
+ * Outputs (device):
+ *   expert_offsets [E+1] int32   first row of each expert (multiple of align);
+ *                                expert_offsets[E] = rows used
+ *   expert_counts  [E]   int32
+ *   row_of_slot    [T*K] int32   permuted row of pair t*K+k (-1 if its id was invalid)
+ *   src_slot       [rows_capacity] int32  pair t*K+k feeding each row, -1 for pads
+ *   x_perm         [rows_capacity, H] (optional; NULL skips the gather):
+ *                  x_perm[row] = x[src_slot[row] / K], zero on pad rows
+ * workspace: rf_moe_permute_workspace_size(T*K, E) bytes.
+ * align is one of 1, 64, 128, 256; E <= 1024.
+ */
+int rf_moe_permute(const int32_t *topk_ids, int64_t T, int64_t K, int64_t E, int64_t align,
+                   const void *x, int dtype, int64_t H,
+                   int32_t *expert_offsets, int32_t *expert_counts, int32_t *row_of_slot,
+                   int32_t *src_slot, void *x_perm, void *workspace, size_t workspace_bytes,
+                   rf_stream_t stream);
+
+/*
+ * Row gather: dst[r] = src[index[r] / index_div] for r < n_rows (n_rows read
+ * from *n_rows_dev when non-NULL, else n_rows_max), zero rows where index < 0.
+ * Rows are `row_bytes` long (a multiple of 16); src/dst 16-byte aligned.
+ */
+int rf_moe_gather_rows(const void *src, const int32_t *index, int64_t index_div,
+                       int64_t n_rows_max, const int32_t *n_rows_dev, int64_t row_bytes,
+                       void *dst, rf_stream_t stream);
+
+/*
+ * K3 — grouped GEMM with the gated activation fused into the epilogue:
+ *   for every expert e in the group list and every row r of expert e:
+ *     h[r, j] = act(sum_k a[r,k] * w1[s,j,k]) * (sum_k a[r,k] * w1[s,I+j,k])
+ *   with s = expert_slot ? expert_slot[e] : e, j in [0, I).
+ * a [rows_capacity, H], w1 [num_slots, 2I, H] (rows 0..I-1 gate, I..2I-1 up),
+ * h [rows_capacity, I]; all in `dtype`; fp32 accumulation.  bf16/fp16 run on
+ * tcgen05 tensor cores (TMA-fed, TMEM accumulators) and need H % 8 == 0,
+ * I % 8 == 0 and align 128; fp32 (and other shapes) run on CUDA cores.
+ * groups: expert ids to compute (NULL = all E experts, n_groups ignored).
+ */
+int rf_moe_grouped_gemm_gated(const void *a, const void *w1, void *h,
+                              const int32_t *expert_offsets, const int32_t *expert_counts,
+                              const int32_t *expert_slot, const int32_t *groups, int64_t n_groups,
+                              int64_t E, int64_t num_slots, int64_t rows_capacity,
+                              int64_t H, int64_t I, int dtype, int activation,
+                              rf_stream_t stream);
+
+/*
+ * Selects the grouped-GEMM implementation for subsequent calls of this
+ * process: 0 = automatic (tensor cores whenever the shape allows), 1 = CUDA
+ * cores only (used by tests to cross-check the two implementations).
+ * No reference counterpart (the reference has a single torch matmul path).
+ */
+int rf_moe_set_gemm_impl(int impl);
+
+/*
+ * K4 — grouped down-projection GEMM:
+ *   y[r, n] = sum_j h[r,j] * w2[s,n,j]      for rows r of each listed expert
+ * h [rows_capacity, I], w2 [num_slots, H, I], y [rows_capacity, H].
+ * Same dtype / group / slot rules as K3.
+ */
+int rf_moe_grouped_gemm_down(const void *h, const void *w2, void *y,
+                             const int32_t *expert_offsets, const int32_t *expert_counts,
+                             const int32_t *expert_slot, const int32_t *groups, int64_t n_groups,
+                             int64_t E, int64_t num_slots, int64_t rows_capacity,
+                             int64_t H, int64_t I, int dtype, rf_stream_t stream);
+
+/*
+ * K5 — weighted combine (fp32 accumulation, one rounding):
+ *   out[t] = sum_k topk_weights[t,k] * y[row_of_slot[t*K+k]]     (rows < 0 skipped)
+ *          + (shared_y ? (shared_scale ? shared_scale[t] : 1) * shared_y[t] : 0)
+ *          + (residual ? residual[t] : 0)
+ *          + (accumulate ? out[t] : 0)
+ * y [rows, H], shared_y/residual/out [T, H], all in `dtype`.
+ */
+int rf_moe_combine(const void *y, const int32_t *row_of_slot, const float *topk_weights,
+                   int64_t T, int64_t K, int64_t H, int dtype,
+                   const void *shared_y, const float *shared_scale, const void *residual,
+                   int accumulate, void *out, rf_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RF_MOE_H */

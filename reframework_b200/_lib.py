@@ -1,0 +1,119 @@
+"""ctypes binding of the rf_moe C ABI (include/rf_moe.h).
+
+Loads ``reframework_b200/_rf_moe.so`` (built in-tree by
+``python -m reframework_b200.csrc.build``).  There is no fallback: if the
+library is missing or a call fails, an :class:`RfMoeError` is raised with the
+library's message.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_rf_moe.so")
+
+RF_F32, RF_F16, RF_BF16 = 0, 1, 2
+ACTIVATIONS = {"silu": 0, "gelu": 1, "gelu_tanh": 2}
+DEV_ERRORS = {0: "ok", 1: "routed expert id out of range", 2: "pipeline wait timed out"}
+
+_c_void_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+
+# name -> (restype, argtypes) — mirrors include/rf_moe.h
+_SIGNATURES = {
+    "rf_moe_last_error": (ctypes.c_char_p, []),
+    "rf_moe_version": (_int, []),
+    "rf_moe_device_status": (_int, [ctypes.POINTER(_int)]),
+    "rf_moe_rows_capacity": (_i64, [_i64, _i64, _i64]),
+    "rf_moe_permute_workspace_size": (ctypes.c_size_t, [_i64, _i64]),
+    "rf_moe_router_topk": (_int, [_c_void_p, _int, _c_void_p, _int, _c_void_p, _i64, _i64, _i64, _i64,
+                                  _int, _int, _int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                  _c_void_p, _c_void_p, _c_void_p]),
+    "rf_moe_permute": (_int, [_c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _int, _i64, _c_void_p,
+                              _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t,
+                              _c_void_p]),
+    "rf_moe_gather_rows": (_int, [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p,
+                                  _c_void_p]),
+    "rf_moe_set_gemm_impl": (_int, [_int]),
+    "rf_moe_grouped_gemm_gated": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                         _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64,
+                                         _int, _int, _c_void_p]),
+    "rf_moe_grouped_gemm_down": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                        _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64,
+                                        _int, _c_void_p]),
+    "rf_moe_combine": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p,
+                              _c_void_p, _c_void_p, _int, _c_void_p, _c_void_p]),
+}
+
+
+class RfMoeError(RuntimeError):
+    """A call into the rf_moe CUDA library failed."""
+
+
+_lib: Optional[ctypes.CDLL] = None
+_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (raises RfMoeError if it has not been built)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RfMoeError(
+                        f"rf_moe CUDA library not found at {LIB_PATH}; build it with "
+                        "`python -m reframework_b200.csrc.build` (needs nvcc)")
+                h = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in _SIGNATURES.items():
+                    fn = getattr(h, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = h
+    return _lib
+
+
+def exported_symbols():
+    return list(_SIGNATURES)
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = lib().rf_moe_last_error().decode(errors="replace")
+        raise RfMoeError(f"{what} failed (status {rc}): {msg}")
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.float32:
+        return RF_F32
+    if dt == torch.float16:
+        return RF_F16
+    if dt == torch.bfloat16:
+        return RF_BF16
+    raise RfMoeError(f"unsupported dtype {dt}")
+
+
+def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def device_status() -> int:
+    """Read and clear the device error word (synchronises the device)."""
+    code = ctypes.c_int(0)
+    check(lib().rf_moe_device_status(ctypes.byref(code)), "rf_moe_device_status")
+    return code.value
+
+
+def set_gemm_impl(impl: int) -> None:
+    check(lib().rf_moe_set_gemm_impl(int(impl)), "rf_moe_set_gemm_impl")

@@ -1,0 +1,29 @@
+// Internal interface between the grouped-GEMM entry points (gemm_tc.cu) and
+// the CUDA-core implementation (gemm_simt.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace rf {
+
+struct GroupedGemmArgs {
+  const void *a;                 // [rows_capacity, Kdim]
+  const void *w;                 // gated: [S, 2*N, Kdim]; down: [S, N, Kdim]
+  void *out;                     // [rows_capacity, N]
+  const int32_t *offsets;        // [E+1]
+  const int32_t *counts;         // [E]
+  const int32_t *slot;           // [E] or NULL
+  const int32_t *groups;         // [G] or NULL (all experts)
+  int n_groups;                  // G
+  int E;
+  int num_slots;
+  int64_t rows_capacity;
+  int Kdim;                      // reduction length (H for gated, I for down)
+  int N;                         // output columns (I for gated, H for down)
+  int dtype;
+  int act;
+};
+
+int launch_simt_grouped_gemm(const GroupedGemmArgs &g, bool gated, cudaStream_t st);
+
+}  // namespace rf

@@ -1,0 +1,637 @@
+// K3/K4 — grouped expert GEMMs on the sm_100a tensor cores (tcgen05).
+//
+// Restates the per-expert matmuls of reframework/moe/fused.py:81-83
+// (`x @ w1[e].t()`, gated activation, `inter @ w2[e].t()`) as two persistent
+// grouped GEMMs over all experts at once:
+//   gated: h[r, j] = act(a[r] . w1[s, j]) * (a[r] . w1[s, I + j])
+//   down:  y[r, n] = h[r] . w2[s, n]
+// for the rows r of every listed expert (s = the expert's weight slot).
+//
+// Design (one CTA per SM, 192 threads, warp-specialised):
+//   warp 0      TMA producer: per 64-deep k-block loads the 128-row A tile
+//               and the 256-row B tile (gated: 128 gate rows + the matching
+//               128 up rows, so one accumulator holds both halves) into a
+//               4-stage shared-memory ring (128-byte swizzle, no multicast).
+//   warp 1      allocates 512 TMEM columns and issues tcgen05.mma (M=128,
+//               N=256, K=16, bf16/fp16 in, fp32 accumulate) from one thread;
+//               two accumulators (2 x 256 columns) let the epilogue of tile i
+//               overlap the main loop of tile i+1.
+//   warps 2-5   epilogue: tcgen05.ld of their 32-lane TMEM quadrant, gated
+//               activation (gated kernel), rounding, 16-byte global stores of
+//               the valid rows.
+// Tiles: per listed expert ceil(count/128) m-blocks x n-blocks, ordered
+// n-major / m-minor inside an expert so concurrently running CTAs share the
+// weight tile through L2; CTAs stride over the tile list.  The tile table is
+// built on the device from expert_counts, so no host synchronisation.
+// Every mbarrier wait is bounded (2 s): on expiry the CTA sets the device
+// error word, stops issuing, waits for its own in-flight MMAs and copies and
+// releases TMEM before returning.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "gemm.cuh"
+
+RF_DEVICE_ERROR_WORD();
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, NTHREADS = 192;
+constexpr int A_BYTES = BM * BK * 2;      // 16 KB
+constexpr int B_BYTES = BN * BK * 2;      // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t TMEM_COLS = 512;       // 2 accumulators x 256 fp32 columns
+constexpr int MAX_GROUPS = 1024;
+constexpr int NUM_BARS = 2 * STAGES + 5;  // full, empty, tmem full x2, tmem empty x2, drain
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 +
+                              (size_t)(MAX_GROUPS + 1) * 4 + (size_t)3 * MAX_GROUPS * 4;
+
+struct TcArgs {
+  const int32_t *offsets, *counts, *slot, *groups;
+  int n_groups, E, num_slots;
+  int Kdim;       // reduction length
+  int N;          // output columns
+  int n_tiles_n;  // n-blocks per expert
+  void *out;
+  int act;
+};
+
+// ------------------------------------------------------------------ PTX
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for the phase of `parity` to complete.  Gives up (false) when another
+// role of this CTA aborted, or after WAIT_LIMIT_NS (then flags the abort).
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = rf::globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 63) == 0) {
+      if (*abort_flag) return false;
+      if (rf::globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+        *abort_flag = 1;
+        rf_report(RF_DEV_WAIT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+// Wait used on the teardown path only: bounded, ignores the abort flag.
+__device__ void mbar_wait_teardown(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = rf::globaltimer_ns();
+  while (!mbar_try(bar, parity)) {
+    if (rf::globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+      rf_report(RF_DEV_WAIT_TIMEOUT);
+      return;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t holder, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(holder),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 TMEM lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
+// 128 bytes grouped by 8 (1024 B between groups), sm_100 descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu)   // start address (16-byte units)
+         | ((uint64_t)1 << 16)                // leading byte offset (unused for SW128 K-major)
+         | ((uint64_t)(1024 >> 4) << 32)      // stride byte offset: 8-row group pitch
+         | ((uint64_t)1 << 46)                // descriptor version (sm_100)
+         | ((uint64_t)2 << 61);               // layout: 128-byte swizzle
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulator, A/B K-major,
+// M = 128, N = 256; operand format 0 = f16, 1 = bf16 (A and B always equal).
+template <typename T>
+__host__ __device__ constexpr uint32_t instr_desc() {
+  return (1u << 4) | ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 7) |
+         ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 10) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+
+template <typename T, bool GATED>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const TcArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + STAGES * A_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * B_BYTES);
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + NUM_BARS);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  int *tile_prefix = reinterpret_cast<int *>(tmem_holder + 4);  // [G+1]
+  int *g_row0 = tile_prefix + MAX_GROUPS + 1;                      // [G]
+  int *g_cnt = g_row0 + MAX_GROUPS;                                // [G]
+  int *g_slot = g_cnt + MAX_GROUPS;                                // [G]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.n_groups;
+  const uint32_t bar0 = smem_u32(bars);
+#define FULL(s) (bar0 + 8u * (uint32_t)(s))
+#define EMPTY(s) (bar0 + 8u * (uint32_t)(STAGES + (s)))
+#define TFULL(a) (bar0 + 8u * (uint32_t)(2 * STAGES + (a)))
+#define TEMPTY(a) (bar0 + 8u * (uint32_t)(2 * STAGES + 2 + (a)))
+  const uint32_t DRAIN = bar0 + 8u * (uint32_t)(2 * STAGES + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(FULL(s), 1);
+      mbar_init(EMPTY(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(TFULL(a), 1);
+      mbar_init(TEMPTY(a), 4);  // one arrival per epilogue warp
+    }
+    mbar_init(DRAIN, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (threadIdx.x == 32) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
+  }
+  // per-group table: first row, row count, weight slot, tile count
+  for (int g = threadIdx.x; g < G; g += NTHREADS) {
+    int e = p.groups ? p.groups[g] : g;
+    int tiles = 0, row0 = 0, cnt = 0, s = 0;
+    if (e >= 0 && e < p.E) {
+      s = p.slot ? p.slot[e] : e;
+      if (s >= 0 && s < p.num_slots) {
+        row0 = p.offsets[e];
+        cnt = p.counts[e];
+        tiles = ((cnt + BM - 1) / BM) * p.n_tiles_n;
+      } else {
+        rf_report(RF_DEV_BAD_EXPERT_ID);
+      }
+    } else {
+      rf_report(RF_DEV_BAD_EXPERT_ID);
+    }
+    g_row0[g] = row0;
+    g_cnt[g] = tiles ? cnt : 0;
+    g_slot[g] = s;
+    tile_prefix[g + 1] = tiles;
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  if (warp == 2) {  // inclusive scan of tile counts -> tile_prefix
+    int carry = 0;
+    for (int c = 0; c < G; c += 32) {
+      int v = (c + lane < G) ? tile_prefix[c + lane + 1] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      if (c + lane < G) tile_prefix[c + lane + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) tile_prefix[0] = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int total = tile_prefix[G];
+  const int num_kb = (p.Kdim + BK - 1) / BK;
+
+  // tile -> (group, n-block, m-block); groups with zero tiles are skipped by
+  // taking the last group whose prefix is <= t
+  auto decode = [&](int t, int &row0, int &rows, int &nb, int &s) {
+    int lo = 0, hi = G - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tile_prefix[mid] <= t) lo = mid;
+      else hi = mid - 1;
+    }
+    const int cnt = g_cnt[lo];
+    const int mt = (cnt + BM - 1) / BM;
+    const int local = t - tile_prefix[lo];
+    nb = local / mt;
+    const int mb = local - nb * mt;
+    row0 = g_row0[lo] + mb * BM;
+    rows = min(BM, cnt - mb * BM);
+    s = g_slot[lo];
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int row0, rows, nb, s;
+        decode(t, row0, rows, nb, s);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(EMPTY(stage), phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(FULL(stage), STAGE_BYTES);
+          const uint32_t a_dst = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_dst = smem_u32(sB + stage * B_BYTES);
+          tma_load_2d(a_dst, &tmA, FULL(stage), kb * BK, row0);
+          if (GATED) {
+            tma_load_3d(b_dst, &tmB, FULL(stage), kb * BK, nb * (BN / 2), 2 * s);
+            tma_load_3d(b_dst + B_BYTES / 2, &tmB, FULL(stage), kb * BK, nb * (BN / 2), 2 * s + 1);
+          } else {
+            tma_load_3d(b_dst, &tmB, FULL(stage), kb * BK, nb * BN, s);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // let the copies already issued land before the CTA can exit
+        const int first = issued > STAGES ? issued - STAGES : 0;
+        for (int j = first; j < issued; ++j)
+          mbar_wait_teardown(FULL(j % STAGES), (uint32_t)((j / STAGES) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = instr_desc<T>();
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t aph = (uint32_t)((it >> 1) & 1);
+        if (!mbar_wait(TEMPTY(acc), aph ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(FULL(stage), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            tc_mma(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC,
+                   (kb | k) ? 1u : 0u);
+          tc_commit(EMPTY(stage));  // frees the stage once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) tc_commit(TFULL(acc));
+      }
+      // no MMA may still be running when TMEM is released
+      tc_commit(DRAIN);
+      mbar_wait_teardown(DRAIN, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int wq = warp & 3;  // TMEM lane quadrant this warp may access
+    const int r = wq * 32 + lane;
+    T *out = reinterpret_cast<T *>(p.out);
+    int it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+      int row0, rows, nb, s;
+      decode(t, row0, rows, nb, s);
+      const int acc = it & 1;
+      const uint32_t aph = (uint32_t)((it >> 1) & 1);
+      // one lane waits, the warp re-converges on the broadcast before the
+      // warp-collective (.sync.aligned) TMEM loads
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(TFULL(acc), aph, abort_flag) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + ((uint32_t)(wq * 32) << 16) + (uint32_t)(acc * BN);
+      const bool row_ok = r < rows;
+      T *orow = out + (int64_t)(row0 + r) * p.N;
+      if (GATED) {
+        const int n0 = nb * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tb + c, g);
+          tmem_ld32(tb + BN / 2 + c, u);
+          tmem_ld_wait();
+          if (row_ok) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float h0 = rf::act_gate(p.act, __uint_as_float(g[2 * j])) * __uint_as_float(u[2 * j]);
+              const float h1 =
+                  rf::act_gate(p.act, __uint_as_float(g[2 * j + 1])) * __uint_as_float(u[2 * j + 1]);
+              pk[j] = rf::pack2<T>(h0, h1);
+            }
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int col = n0 + c + 8 * v;
+              if (col < p.N)
+                *reinterpret_cast<uint4 *>(orow + col) =
+                    make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+            }
+          }
+        }
+      } else {
+        const int n0 = nb * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v32[32];
+          tmem_ld32(tb + c, v32);
+          tmem_ld_wait();
+          if (row_ok) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              pk[j] = rf::pack2<T>(__uint_as_float(v32[2 * j]), __uint_as_float(v32[2 * j + 1]));
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int col = n0 + c + 8 * v;
+              if (col < p.N)
+                *reinterpret_cast<uint4 *>(orow + col) =
+                    make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(TEMPTY(acc));
+    }
+  }
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+#undef FULL
+#undef EMPTY
+#undef TFULL
+#undef TEMPTY
+}
+
+// ----------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int g_gemm_impl = 0;  // 0 = auto, 1 = CUDA cores only
+
+bool encode(CUtensorMap *m, int dtype, int rank, const void *base, const cuuint64_t *dims,
+            const cuuint64_t *strides, const cuuint32_t *box) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == RF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(m, dt, (cuuint32_t)rank, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <typename T, bool GATED>
+int launch_tc_t(const rf::GroupedGemmArgs &g, const CUtensorMap &ma, const CUtensorMap &mb,
+                cudaStream_t st) {
+  auto kern = tc_grouped_gemm<T, GATED>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess)
+    return rf::fail(RF_ERR_CUDA, std::string("tensor-core GEMM: ") + cudaGetErrorString(attr_err));
+  TcArgs p;
+  p.offsets = g.offsets;
+  p.counts = g.counts;
+  p.slot = g.slot;
+  p.groups = g.groups;
+  p.n_groups = g.n_groups;
+  p.E = g.E;
+  p.num_slots = g.num_slots;
+  p.Kdim = g.Kdim;
+  p.N = g.N;
+  p.n_tiles_n = GATED ? (g.N + BN / 2 - 1) / (BN / 2) : (g.N + BN - 1) / BN;
+  p.out = g.out;
+  p.act = g.act;
+  kern<<<rf::num_sms(), NTHREADS, SMEM_BYTES, st>>>(ma, mb, p);
+  return rf::check_launch(GATED ? "tensor-core gated GEMM" : "tensor-core down GEMM");
+}
+
+// Returns 1 if the tensor-core path took the call (status in *rc), 0 if the
+// shape or dtype is outside what it handles (the CUDA-core kernel runs then).
+int try_tc(const rf::GroupedGemmArgs &g, bool gated, cudaStream_t st, int *rc) {
+  if (g_gemm_impl == 1) return 0;
+  if (g.dtype != RF_BF16 && g.dtype != RF_F16) return 0;
+  if (g.Kdim % 8 || g.N % 8 || g.n_groups > MAX_GROUPS) return 0;
+  if ((uintptr_t)g.a % 16 || (uintptr_t)g.w % 16 || (uintptr_t)g.out % 16) return 0;
+  *rc = RF_OK;
+  if (!encode_fn()) {
+    *rc = rf::fail(RF_ERR_CUDA, "tensor-core GEMM: cuTensorMapEncodeTiled is unavailable");
+    return 1;
+  }
+  CUtensorMap ma, mb;
+  const cuuint64_t dA[2] = {(cuuint64_t)g.Kdim, (cuuint64_t)g.rows_capacity};
+  const cuuint64_t sAs[1] = {(cuuint64_t)g.Kdim * 2};
+  const cuuint32_t bA[2] = {BK, BM};
+  bool ok = encode(&ma, g.dtype, 2, g.a, dA, sAs, bA);
+  if (gated) {
+    // w1 [S, 2N, K] viewed as [2S][N][K]: half 0 = gate rows, half 1 = up rows
+    const cuuint64_t dB[3] = {(cuuint64_t)g.Kdim, (cuuint64_t)g.N, (cuuint64_t)(2 * g.num_slots)};
+    const cuuint64_t sB[2] = {(cuuint64_t)g.Kdim * 2, (cuuint64_t)g.N * g.Kdim * 2};
+    const cuuint32_t bB[3] = {BK, BN / 2, 1};
+    ok = ok && encode(&mb, g.dtype, 3, g.w, dB, sB, bB);
+  } else {
+    const cuuint64_t dB[3] = {(cuuint64_t)g.Kdim, (cuuint64_t)g.N, (cuuint64_t)g.num_slots};
+    const cuuint64_t sB[2] = {(cuuint64_t)g.Kdim * 2, (cuuint64_t)g.N * g.Kdim * 2};
+    const cuuint32_t bB[3] = {BK, BN, 1};
+    ok = ok && encode(&mb, g.dtype, 3, g.w, dB, sB, bB);
+  }
+  if (!ok) {
+    *rc = rf::fail(RF_ERR_CUDA, "tensor-core GEMM: cuTensorMapEncodeTiled rejected the operands");
+    return 1;
+  }
+  if (g.dtype == RF_BF16)
+    *rc = gated ? launch_tc_t<__nv_bfloat16, true>(g, ma, mb, st)
+                : launch_tc_t<__nv_bfloat16, false>(g, ma, mb, st);
+  else
+    *rc = gated ? launch_tc_t<__half, true>(g, ma, mb, st) : launch_tc_t<__half, false>(g, ma, mb, st);
+  return 1;
+}
+
+int grouped_gemm(const void *a, const void *w, void *out, const int32_t *offsets,
+                 const int32_t *counts, const int32_t *slot, const int32_t *groups,
+                 int64_t n_groups, int64_t E, int64_t num_slots, int64_t rows_capacity,
+                 int64_t Kdim, int64_t N, int dtype, int act, bool gated, rf_stream_t stream,
+                 const char *name) {
+  const std::string nm(name);
+  RF_CHECK_ARG(rf::valid_dtype(dtype), nm + ": unknown dtype");
+  RF_CHECK_ARG(act == RF_ACT_SILU || act == RF_ACT_GELU || act == RF_ACT_GELU_TANH,
+               nm + ": unknown activation");
+  RF_CHECK_ARG(E >= 1 && E <= 65535 && num_slots >= 1 && rows_capacity >= 0 && Kdim >= 1 && N >= 1,
+               nm + ": bad sizes");
+  RF_CHECK_ARG(Kdim < (1 << 30) && N < (1 << 30) && rows_capacity < ((int64_t)1 << 31),
+               nm + ": sizes exceed int32");
+  RF_CHECK_ARG(a && w && out && offsets && counts, nm + ": null pointer");
+  const int64_t G = groups ? n_groups : E;
+  RF_CHECK_ARG(G >= 0 && G <= 65535, nm + ": bad group count");
+  if (G == 0 || rows_capacity == 0) return RF_OK;
+  rf::GroupedGemmArgs g;
+  g.a = a;
+  g.w = w;
+  g.out = out;
+  g.offsets = offsets;
+  g.counts = counts;
+  g.slot = slot;
+  g.groups = groups;
+  g.n_groups = (int)G;
+  g.E = (int)E;
+  g.num_slots = (int)num_slots;
+  g.rows_capacity = rows_capacity;
+  g.Kdim = (int)Kdim;
+  g.N = (int)N;
+  g.dtype = dtype;
+  g.act = act;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = RF_OK;
+  if (try_tc(g, gated, st, &rc)) return rc;
+  return rf::launch_simt_grouped_gemm(g, gated, st);
+}
+
+}  // namespace
+
+extern "C" int rf_moe_set_gemm_impl(int impl) {
+  if (impl != 0 && impl != 1) return rf::fail(RF_ERR_ARG, "rf_moe_set_gemm_impl: 0 or 1");
+  g_gemm_impl = impl;
+  return RF_OK;
+}
+
+extern "C" int rf_moe_grouped_gemm_gated(const void *a, const void *w1, void *h,
+                                         const int32_t *expert_offsets,
+                                         const int32_t *expert_counts, const int32_t *expert_slot,
+                                         const int32_t *groups, int64_t n_groups, int64_t E,
+                                         int64_t num_slots, int64_t rows_capacity, int64_t H,
+                                         int64_t I, int dtype, int activation, rf_stream_t stream) {
+  return grouped_gemm(a, w1, h, expert_offsets, expert_counts, expert_slot, groups, n_groups, E,
+                      num_slots, rows_capacity, H, I, dtype, activation, true, stream,
+                      "rf_moe_grouped_gemm_gated");
+}
+
+extern "C" int rf_moe_grouped_gemm_down(const void *h, const void *w2, void *y,
+                                        const int32_t *expert_offsets, const int32_t *expert_counts,
+                                        const int32_t *expert_slot, const int32_t *groups,
+                                        int64_t n_groups, int64_t E, int64_t num_slots,
+                                        int64_t rows_capacity, int64_t H, int64_t I, int dtype,
+                                        rf_stream_t stream) {
+  return grouped_gemm(h, w2, y, expert_offsets, expert_counts, expert_slot, groups, n_groups, E,
+                      num_slots, rows_capacity, I, H, dtype, RF_ACT_SILU, false, stream,
+                      "rf_moe_grouped_gemm_down");
+}

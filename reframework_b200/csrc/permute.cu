@@ -1,0 +1,277 @@
+// K2 — stable counting-sort permute of the (token, slot) pairs by expert, and
+// the row gather that builds the expert-contiguous activation buffer.
+//
+// Restates the grouping of reframework/moe/fused.py:71-80 (bincount, then per
+// active expert the rows `flat_expert == e` in ascending flat index t*K+k, and
+// `hidden_states[tok]`).  Three launches:
+//   1. permute_hist     per-block expert histograms of the flat ids
+//   2. permute_scatter  per-expert totals -> padded exclusive scan (offsets),
+//                       then a stable in-block ranking (warp match + per-warp
+//                       running cursors) that assigns every pair its row
+//   3. gather_rows      x_perm[row] = x[src_slot[row] / K] (zero on pad rows),
+//                       one warp per row with 16-byte vector copies
+// The first two kernels touch only 4-byte ids; the gather is the HBM-bound part
+// (reads and writes T*K*H elements).
+#include "common.cuh"
+
+RF_DEVICE_ERROR_WORD();
+
+namespace {
+
+constexpr int PT = 256;        // threads per block (8 warps)
+constexpr int PW = PT / 32;
+constexpr int CHUNK = 4096;    // pairs per block
+constexpr int SUB = CHUNK / PW;  // pairs per warp
+
+__global__ void __launch_bounds__(PT) permute_hist(const int32_t *ids, int64_t n, int E,
+                                                   int32_t *block_counts) {
+  extern __shared__ int s_hist[];
+  for (int e = threadIdx.x; e < E; e += PT) s_hist[e] = 0;
+  __syncthreads();
+  const int64_t b0 = (int64_t)blockIdx.x * CHUNK;
+  const int64_t b1 = min(n, b0 + CHUNK);
+  for (int64_t i = b0 + threadIdx.x; i < b1; i += PT) {
+    const int e = ids[i];
+    if (e >= 0 && e < E) atomicAdd(&s_hist[e], 1);
+    else rf_report(RF_DEV_BAD_EXPERT_ID);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += PT) block_counts[(int64_t)blockIdx.x * E + e] = s_hist[e];
+}
+
+// Block-wide exclusive scan of v[0..E) in place (E <= 1024, PT threads);
+// returns the total.  Uses s_tmp[PW] scratch.
+__device__ int block_exclusive_scan(int *v, int E, int *s_tmp) {
+  const int per = (E + PT - 1) / PT;
+  const int beg = threadIdx.x * per;
+  const int end = min(E, beg + per);
+  int local = 0;
+  for (int i = beg; i < end; ++i) local += v[i];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int inc = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += u;
+  }
+  if (lane == 31) s_tmp[warp] = inc;
+  __syncthreads();
+  int warp_base = 0, total = 0;
+  for (int w = 0; w < PW; ++w) {
+    if (w < warp) warp_base += s_tmp[w];
+    total += s_tmp[w];
+  }
+  int run = warp_base + inc - local;
+  __syncthreads();
+  for (int i = beg; i < end; ++i) {
+    const int c = v[i];
+    v[i] = run;
+    run += c;
+  }
+  __syncthreads();
+  return total;
+}
+
+__global__ void __launch_bounds__(PT) permute_scatter(const int32_t *ids, int64_t n, int K, int E,
+                                                      int align, const int32_t *block_counts,
+                                                      int nblk, int32_t *offsets_out,
+                                                      int32_t *counts_out, int32_t *row_of_slot,
+                                                      int32_t *src_slot) {
+  extern __shared__ int smem[];
+  int *s_tot = smem;                 // [E]
+  int *s_off = s_tot + E;            // [E]   padded exclusive offsets
+  int *s_wc = s_off + E;             // [PW][E] per-warp cursors
+  int *s_tmp = s_wc + PW * E;        // [PW]
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  // 1. per-expert totals and this block's base within each expert
+  for (int e = threadIdx.x; e < E; e += PT) {
+    int tot = 0, before = 0;
+    for (int bb = 0; bb < nblk; ++bb) {
+      const int c = block_counts[(int64_t)bb * E + e];
+      if (bb < b) before += c;
+      tot += c;
+    }
+    s_tot[e] = tot;
+    s_off[e] = (tot + align - 1) / align * align;
+    s_wc[e] = before;  // stash in warp-0 row for now
+  }
+  __syncthreads();
+  const int used = block_exclusive_scan(s_off, E, s_tmp);
+  if (b == 0) {
+    for (int e = threadIdx.x; e < E; e += PT) {
+      offsets_out[e] = s_off[e];
+      counts_out[e] = s_tot[e];
+    }
+    if (threadIdx.x == 0) offsets_out[E] = used;
+  }
+  // pad rows of the experts owned (e % nblk == b) by this block
+  for (int e = b; e < E; e += nblk) {
+    const int p0 = s_off[e] + s_tot[e];
+    const int p1 = s_off[e] + (s_tot[e] + align - 1) / align * align;
+    for (int r = p0 + threadIdx.x; r < p1; r += PT) src_slot[r] = -1;
+  }
+  // 2. per-warp histograms of this block's chunk
+  const int64_t c0 = (int64_t)b * CHUNK;
+  const int64_t w0 = c0 + (int64_t)warp * SUB;
+  const int64_t w1 = min(n, w0 + SUB);
+  __syncthreads();
+  int *base = s_tmp;  // unused from here; keep names readable
+  (void)base;
+  // move the block base out of s_wc[0..E) before zeroing the warp rows
+  for (int e = threadIdx.x; e < E; e += PT) s_tot[e] = s_off[e] + s_wc[e];  // block's first row per expert
+  __syncthreads();
+  for (int i = threadIdx.x; i < PW * E; i += PT) s_wc[i] = 0;
+  __syncthreads();
+  int *wc = s_wc + warp * E;
+  for (int64_t i0 = w0; i0 < w1; i0 += 32) {
+    const int64_t i = i0 + lane;
+    int e = -1;
+    if (i < w1) {
+      e = ids[i];
+      if (e < 0 || e >= E) e = -1;
+    }
+    const unsigned grp = __match_any_sync(0xffffffffu, e);
+    const int leader = __ffs(grp) - 1;
+    if (lane == leader && e >= 0 && i < w1) wc[e] += __popc(grp);
+    __syncwarp();
+  }
+  __syncthreads();
+  // 3. exclusive prefix over warps, seeded with the block base
+  for (int e = threadIdx.x; e < E; e += PT) {
+    int run = s_tot[e];
+    for (int w = 0; w < PW; ++w) {
+      const int c = s_wc[w * E + e];
+      s_wc[w * E + e] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  // 4. stable scatter: rank inside each 32-pair group, groups in order
+  const unsigned lt = (1u << lane) - 1u;
+  for (int64_t i0 = w0; i0 < w1; i0 += 32) {
+    const int64_t i = i0 + lane;
+    int e = -1;
+    if (i < w1) {
+      e = ids[i];
+      if (e < 0 || e >= E) e = -1;
+    }
+    const unsigned grp = __match_any_sync(0xffffffffu, e);
+    const int leader = __ffs(grp) - 1;
+    int row = -1;
+    if (e >= 0) row = wc[e] + __popc(grp & lt);
+    __syncwarp();
+    if (lane == leader && e >= 0) wc[e] += __popc(grp);
+    __syncwarp();
+    if (i < w1) {
+      row_of_slot[i] = row;
+      if (row >= 0) src_slot[row] = (int32_t)i;
+    }
+  }
+  (void)K;
+}
+
+template <int UNROLL>
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint8_t *src, const int32_t *index,
+                                                          int64_t index_div, int64_t n_max,
+                                                          const int32_t *n_dev, int64_t row_bytes,
+                                                          uint8_t *dst) {
+  const int64_t n = n_dev ? min((int64_t)*n_dev, n_max) : n_max;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * 8;
+  const int64_t vecs = row_bytes / 16;
+  for (int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); r < n; r += warps) {
+    const int32_t s = index[r];
+    uint4 *d = reinterpret_cast<uint4 *>(dst + r * row_bytes);
+    if (s < 0) {
+      for (int64_t v = lane; v < vecs; v += 32) d[v] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const uint4 *q = reinterpret_cast<const uint4 *>(src + (int64_t)(s / index_div) * row_bytes);
+    int64_t v = lane;
+    for (; v + 32 * (UNROLL - 1) < vecs; v += 32 * UNROLL) {
+      uint4 t[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) t[u] = __ldg(q + v + 32 * u);
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) d[v + 32 * u] = t[u];
+    }
+    for (; v < vecs; v += 32) d[v] = __ldg(q + v);
+  }
+}
+
+int launch_gather(const void *src, const int32_t *index, int64_t index_div, int64_t n_max,
+                  const int32_t *n_dev, int64_t row_bytes, void *dst, cudaStream_t st) {
+  if (n_max <= 0) return RF_OK;
+  int64_t blocks = (n_max + 7) / 8;
+  const int64_t cap = (int64_t)rf::num_sms() * 8;
+  if (blocks > cap) blocks = cap;
+  gather_rows_kernel<4><<<(int)blocks, 256, 0, st>>>((const uint8_t *)src, index, index_div, n_max,
+                                                      n_dev, row_bytes, (uint8_t *)dst);
+  return rf::check_launch("rf_moe_gather_rows");
+}
+
+}  // namespace
+
+extern "C" size_t rf_moe_permute_workspace_size(int64_t n_pairs, int64_t num_experts) {
+  const int64_t nblk = n_pairs > 0 ? (n_pairs + CHUNK - 1) / CHUNK : 1;
+  return (size_t)(nblk * num_experts * 4 + 256);
+}
+
+extern "C" int rf_moe_gather_rows(const void *src, const int32_t *index, int64_t index_div,
+                                  int64_t n_rows_max, const int32_t *n_rows_dev, int64_t row_bytes,
+                                  void *dst, rf_stream_t stream) {
+  RF_CHECK_ARG(row_bytes > 0 && row_bytes % 16 == 0, "rf_moe_gather_rows: row_bytes % 16 != 0");
+  RF_CHECK_ARG(index_div >= 1, "rf_moe_gather_rows: index_div must be >= 1");
+  RF_CHECK_ARG(n_rows_max == 0 || (src && index && dst), "rf_moe_gather_rows: null pointer");
+  RF_CHECK_ARG((uintptr_t)src % 16 == 0 && (uintptr_t)dst % 16 == 0,
+               "rf_moe_gather_rows: src/dst must be 16-byte aligned");
+  return launch_gather(src, index, index_div, n_rows_max, n_rows_dev, row_bytes, dst,
+                       (cudaStream_t)stream);
+}
+
+extern "C" int rf_moe_permute(const int32_t *topk_ids, int64_t T, int64_t K, int64_t E,
+                              int64_t align, const void *x, int dtype, int64_t H,
+                              int32_t *expert_offsets, int32_t *expert_counts,
+                              int32_t *row_of_slot, int32_t *src_slot, void *x_perm,
+                              void *workspace, size_t workspace_bytes, rf_stream_t stream) {
+  RF_CHECK_ARG(T >= 0 && K >= 1 && E >= 1 && E <= 1024, "rf_moe_permute: bad sizes (E <= 1024)");
+  RF_CHECK_ARG(align == 1 || align == 64 || align == 128 || align == 256,
+               "rf_moe_permute: align must be 1, 64, 128 or 256");
+  const int64_t n = T * K;
+  RF_CHECK_ARG(n + E * (align - 1) < (int64_t)1 << 31, "rf_moe_permute: too many rows for int32");
+  RF_CHECK_ARG(expert_offsets && expert_counts && row_of_slot && src_slot,
+               "rf_moe_permute: null output");
+  RF_CHECK_ARG(workspace_bytes >= rf_moe_permute_workspace_size(n, E) && workspace,
+               "rf_moe_permute: workspace too small");
+  RF_CHECK_ARG(!x_perm || (x && rf::valid_dtype(dtype) && H > 0 &&
+                           (H * (int64_t)rf::dtype_size(dtype)) % 16 == 0),
+               "rf_moe_permute: gather needs x, a dtype and H*elsize % 16 == 0");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int nblk = (int)(n > 0 ? (n + CHUNK - 1) / CHUNK : 1);
+  int32_t *block_counts = reinterpret_cast<int32_t *>(workspace);
+  if (n == 0) {
+    // no pairs: every expert is empty
+    cudaError_t e1 = cudaMemsetAsync(expert_offsets, 0, (E + 1) * 4, st);
+    cudaError_t e2 = cudaMemsetAsync(expert_counts, 0, E * 4, st);
+    if (e1 != cudaSuccess || e2 != cudaSuccess)
+      return rf::fail(RF_ERR_CUDA, "rf_moe_permute: memset failed");
+    return RF_OK;
+  }
+  permute_hist<<<nblk, PT, E * sizeof(int), st>>>(topk_ids, n, (int)E, block_counts);
+  int rc = rf::check_launch("rf_moe_permute(hist)");
+  if (rc) return rc;
+  const size_t smem = (size_t)(2 * E + PW * E + PW) * sizeof(int);
+  permute_scatter<<<nblk, PT, smem, st>>>(topk_ids, n, (int)K, (int)E, (int)align, block_counts,
+                                          nblk, expert_offsets, expert_counts, row_of_slot,
+                                          src_slot);
+  rc = rf::check_launch("rf_moe_permute(scatter)");
+  if (rc) return rc;
+  if (x_perm) {
+    const int64_t rows_cap = n + E * (align - 1);
+    return launch_gather(x, src_slot, K, rows_cap, expert_offsets + E,
+                         H * (int64_t)rf::dtype_size(dtype), x_perm, st);
+  }
+  return RF_OK;
+}

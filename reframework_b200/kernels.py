@@ -1,0 +1,223 @@
+"""Thin torch-facing wrappers over the rf_moe C ABI, one per stage.
+
+Tensors are CUDA tensors (the library launches on the current torch stream
+of their device); scratch buffers come from torch's caching allocator.
+Nothing here falls back to torch math: a missing library or an unsupported
+case raises :class:`reframework_b200._lib.RfMoeError`.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import check, dtype_code, lib, ptr, stream_of
+
+ALIGN = 128  # expert segment alignment of the permuted row layout (one GEMM m-tile)
+
+
+def _require_cuda(*ts: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise _lib.RfMoeError("reframework_b200 kernels need CUDA tensors "
+                                  f"(got a tensor on {t.device}); there is no CPU path")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise _lib.RfMoeError(f"tensors on different devices: {dev} vs {t.device}")
+    return dev
+
+
+def rows_capacity(n_pairs: int, num_experts: int, align: int = ALIGN) -> int:
+    return int(lib().rf_moe_rows_capacity(n_pairs, num_experts, align))
+
+
+# ----------------------------------------------------------------------- K1
+def router_topk(x: torch.Tensor, gate: Optional[torch.Tensor], top_k: int, *, renormalize: bool = True,
+                bias: Optional[torch.Tensor] = None, round_dtype: Optional[torch.dtype] = None,
+                entropy_k_min: int = 0, shared_gate: Optional[torch.Tensor] = None,
+                want_logits: bool = False, ids64: bool = False, ids32: bool = True):
+    """Router logits + softmax + top-k (+ renorm).  ``gate=None``: ``x`` holds logits.
+
+    Returns ``(weights fp32 [T,K], ids32 or None, ids64 or None, logits or None,
+    shared_scale or None)``.
+    """
+    dev = _require_cuda(x, gate, bias, shared_gate)
+    x = x.contiguous()
+    T, H = x.shape
+    E = gate.shape[0] if gate is not None else H
+    if gate is not None:
+        gate = gate.contiguous()
+    w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    i32 = torch.empty(T, top_k, dtype=torch.int32, device=dev) if ids32 else None
+    i64 = torch.empty(T, top_k, dtype=torch.int64, device=dev) if ids64 else None
+    lg = torch.empty(T, E, dtype=torch.float32, device=dev) if want_logits else None
+    ss = torch.empty(T, dtype=torch.float32, device=dev) if shared_gate is not None else None
+    if bias is not None:
+        bias = bias.to(device=dev, dtype=torch.float32).contiguous()
+    if shared_gate is not None:
+        shared_gate = shared_gate.to(dtype=gate.dtype).contiguous()
+    rc = lib().rf_moe_router_topk(
+        ptr(x), dtype_code(x.dtype), ptr(gate), dtype_code(gate.dtype if gate is not None else x.dtype),
+        ptr(bias), T, H, E, top_k, int(bool(renormalize)),
+        -1 if round_dtype is None else dtype_code(round_dtype), int(entropy_k_min),
+        ptr(shared_gate), ptr(ss), ptr(w), ptr(i32), ptr(i64), ptr(lg), stream_of(dev))
+    check(rc, "rf_moe_router_topk")
+    return w, i32, i64, lg, ss
+
+
+# ----------------------------------------------------------------------- K2
+@dataclass
+class Permutation:
+    offsets: torch.Tensor       # [E+1] int32, padded row starts (offsets[E] = rows used)
+    counts: torch.Tensor        # [E] int32
+    row_of_slot: torch.Tensor   # [T*K] int32
+    src_slot: torch.Tensor      # [rows_cap] int32 (-1 on pad rows)
+    x_perm: Optional[torch.Tensor]  # [rows_cap, H]
+    rows_cap: int
+    align: int
+
+
+def permute(ids32: torch.Tensor, num_experts: int, *, align: int = ALIGN,
+            x: Optional[torch.Tensor] = None) -> Permutation:
+    dev = _require_cuda(ids32, x)
+    if ids32.dtype != torch.int32:
+        raise _lib.RfMoeError("permute: ids must be int32")
+    ids32 = ids32.contiguous()
+    T, K = ids32.shape
+    E = int(num_experts)
+    cap = rows_capacity(T * K, E, align)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    row_of_slot = torch.empty(T * K, dtype=torch.int32, device=dev)
+    src_slot = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
+    ws_bytes = int(lib().rf_moe_permute_workspace_size(T * K, E))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    x_perm = None
+    H = 0
+    if x is not None:
+        x = x.contiguous()
+        H = x.shape[1]
+        x_perm = torch.empty(max(cap, 1), H, dtype=x.dtype, device=dev)
+    rc = lib().rf_moe_permute(ptr(ids32), T, K, E, align, ptr(x), dtype_code(x.dtype) if x is not None else 0,
+                              H, ptr(offsets), ptr(counts), ptr(row_of_slot), ptr(src_slot), ptr(x_perm),
+                              ptr(ws), ws_bytes, stream_of(dev))
+    check(rc, "rf_moe_permute")
+    return Permutation(offsets, counts, row_of_slot, src_slot, x_perm, cap, align)
+
+
+def gather_rows(src: torch.Tensor, index: torch.Tensor, out: torch.Tensor, *, index_div: int = 1,
+                n_rows_dev: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out[r] = src[index[r] // index_div]`` (zero where index < 0)."""
+    dev = _require_cuda(src, index, out, n_rows_dev)
+    row_bytes = src.shape[1] * src.element_size()
+    rc = lib().rf_moe_gather_rows(ptr(src), ptr(index), index_div, out.shape[0], ptr(n_rows_dev),
+                                  row_bytes, ptr(out), stream_of(dev))
+    check(rc, "rf_moe_gather_rows")
+    return out
+
+
+# -------------------------------------------------------------------- K3/K4
+def grouped_gemm_gated(a: torch.Tensor, w1: torch.Tensor, offsets: torch.Tensor, counts: torch.Tensor,
+                       out: torch.Tensor, *, slot: Optional[torch.Tensor] = None,
+                       groups: Optional[torch.Tensor] = None, activation: str = "silu") -> torch.Tensor:
+    """``out[r] = act(a[r] . w1[s, :I]^T) * (a[r] . w1[s, I:]^T)`` per expert segment."""
+    dev = _require_cuda(a, w1, offsets, counts, out, slot, groups)
+    S, I2, H = w1.shape
+    E = counts.shape[0]
+    if activation not in _lib.ACTIVATIONS:
+        raise ValueError(f"unknown gated activation {activation!r}; known: {tuple(_lib.ACTIVATIONS)}")
+    rc = lib().rf_moe_grouped_gemm_gated(
+        ptr(a), ptr(w1), ptr(out), ptr(offsets), ptr(counts), ptr(slot), ptr(groups),
+        0 if groups is None else groups.numel(), E, S, a.shape[0], H, I2 // 2,
+        dtype_code(a.dtype), _lib.ACTIVATIONS[activation], stream_of(dev))
+    check(rc, "rf_moe_grouped_gemm_gated")
+    return out
+
+
+def grouped_gemm_down(h: torch.Tensor, w2: torch.Tensor, offsets: torch.Tensor, counts: torch.Tensor,
+                      out: torch.Tensor, *, slot: Optional[torch.Tensor] = None,
+                      groups: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out[r] = h[r] . w2[s]^T`` per expert segment."""
+    dev = _require_cuda(h, w2, offsets, counts, out, slot, groups)
+    S, H, I = w2.shape
+    E = counts.shape[0]
+    rc = lib().rf_moe_grouped_gemm_down(
+        ptr(h), ptr(w2), ptr(out), ptr(offsets), ptr(counts), ptr(slot), ptr(groups),
+        0 if groups is None else groups.numel(), E, S, h.shape[0], H, I, dtype_code(h.dtype),
+        stream_of(dev))
+    check(rc, "rf_moe_grouped_gemm_down")
+    return out
+
+
+# ----------------------------------------------------------------------- K5
+def combine(y: torch.Tensor, row_of_slot: torch.Tensor, weights: torch.Tensor, out: torch.Tensor, *,
+            shared_y: Optional[torch.Tensor] = None, shared_scale: Optional[torch.Tensor] = None,
+            residual: Optional[torch.Tensor] = None, accumulate: bool = False) -> torch.Tensor:
+    dev = _require_cuda(y, row_of_slot, weights, out, shared_y, shared_scale, residual)
+    T, K = weights.shape
+    H = out.shape[1]
+    weights = weights.contiguous()
+    if weights.dtype != torch.float32:
+        weights = weights.float()
+    rc = lib().rf_moe_combine(ptr(y), ptr(row_of_slot), ptr(weights), T, K, H, dtype_code(out.dtype),
+                              ptr(shared_y), ptr(shared_scale), ptr(residual), int(bool(accumulate)),
+                              ptr(out), stream_of(dev))
+    check(rc, "rf_moe_combine")
+    return out
+
+
+# --------------------------------------------------------- composed forward
+_SINGLE_GROUP: Dict[Tuple[torch.device, int], Tuple[torch.Tensor, torch.Tensor]] = {}
+
+
+def dense_segment(device: torch.device, rows: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(offsets [2], counts [1]) describing one segment of ``rows`` rows at row 0."""
+    key = (device, int(rows))
+    seg = _SINGLE_GROUP.get(key)
+    if seg is None:
+        seg = (torch.tensor([0, rows], dtype=torch.int32, device=device),
+               torch.tensor([rows], dtype=torch.int32, device=device))
+        if len(_SINGLE_GROUP) > 64:
+            _SINGLE_GROUP.clear()
+        _SINGLE_GROUP[key] = seg
+    return seg
+
+
+def dense_gated_mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, activation: str = "silu") -> torch.Tensor:
+    """A dense gated MLP over all rows of ``x`` (the shared expert), on the grouped kernels
+    with a single segment.  w1 [2I,H], w2 [H,I]."""
+    T, H = x.shape
+    off, cnt = dense_segment(x.device, T)
+    I = w2.shape[1]
+    h = torch.empty(T, I, dtype=x.dtype, device=x.device)
+    grouped_gemm_gated(x, w1.unsqueeze(0), off, cnt, h, activation=activation)
+    y = torch.empty(T, H, dtype=x.dtype, device=x.device)
+    grouped_gemm_down(h, w2.unsqueeze(0), off, cnt, y)
+    return y
+
+
+def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, weights: torch.Tensor,
+                ids32: torch.Tensor, *, activation: str = "silu", shared_y: Optional[torch.Tensor] = None,
+                shared_scale: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None, slot: Optional[torch.Tensor] = None,
+                num_experts: Optional[int] = None) -> torch.Tensor:
+    """Permute -> grouped gated GEMM -> grouped down GEMM -> combine (routing given)."""
+    T, H = x.shape
+    E = num_experts if num_experts is not None else w1.shape[0]
+    I = w2.shape[2]
+    p = permute(ids32, E, x=x)
+    h = torch.empty(p.rows_cap, I, dtype=x.dtype, device=x.device)
+    grouped_gemm_gated(p.x_perm, w1, p.offsets, p.counts, h, slot=slot, activation=activation)
+    y = torch.empty(p.rows_cap, H, dtype=x.dtype, device=x.device)
+    grouped_gemm_down(h, w2, p.offsets, p.counts, y, slot=slot)
+    if out is None:
+        out = torch.empty(T, H, dtype=x.dtype, device=x.device)
+    return combine(y, p.row_of_slot, weights, out, shared_y=shared_y, shared_scale=shared_scale,
+                   residual=residual)

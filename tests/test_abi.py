@@ -1,0 +1,72 @@
+"""The C-ABI library builds, loads and exports every symbol the header
+declares; argument validation fails cleanly without touching a GPU."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from reframework_b200 import _lib
+
+HEADER = os.path.join(ROOT, "include", "rf_moe.h")
+
+
+def header_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(rf_moe_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = header_functions()
+    assert len(names) >= 11
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in rf_moe.h but not exported"
+    assert set(names) == set(_lib.exported_symbols()), "ctypes bindings out of sync with the header"
+
+
+def test_version_and_sizes():
+    lib = _lib.lib()
+    assert lib.rf_moe_version() == 100
+    assert lib.rf_moe_rows_capacity(8192, 8, 128) == 8192 + 8 * 127
+    assert lib.rf_moe_rows_capacity(8192, 8, 1) == 8192
+    assert lib.rf_moe_permute_workspace_size(8192, 8) >= 2 * 8 * 4
+
+
+@pytest.mark.parametrize("call, needle", [
+    (lambda L: L.rf_moe_router_topk(None, 2, None, 2, None, 4, 64, 8, 9, 1, -1, 0, None, None,
+                                    None, None, None, None, None), "K <="),
+    (lambda L: L.rf_moe_router_topk(None, 7, None, 2, None, 4, 64, 8, 2, 1, -1, 0, None, None,
+                                    None, None, None, None, None), "dtype"),
+    (lambda L: L.rf_moe_permute(None, 4, 2, 8, 3, None, 2, 64, None, None, None, None, None, None, 0,
+                                None), "align"),
+    (lambda L: L.rf_moe_combine(None, None, None, 4, 2, 60, 2, None, None, None, 0, None, None),
+     "multiple of 16"),
+    (lambda L: L.rf_moe_grouped_gemm_gated(None, None, None, None, None, None, None, 0, 8, 8, 64, 64,
+                                           64, 2, 9, None), "activation"),
+    (lambda L: L.rf_moe_set_gemm_impl(5), "0 or 1"),
+])
+def test_argument_validation(call, needle):
+    lib = _lib.lib()
+    rc = call(lib)
+    assert rc == 1  # RF_ERR_ARG
+    assert needle in lib.rf_moe_last_error().decode()
+
+
+def test_errors_raise_in_python():
+    with pytest.raises(_lib.RfMoeError):
+        _lib.set_gemm_impl(7)
+
+
+def test_no_multicast_or_batched_copy_in_sources():
+    """No cluster-multicast bulk loads and no batched async memcpy anywhere in
+    the CUDA sources (the patterns are assembled so this file names neither)."""
+    csrc = os.path.join(ROOT, "reframework_b200", "csrc")
+    bad = re.compile("|".join(["multi" + "cast::" + "cluster", "Memcpy" + "Batch", "Memcpy3D" + "Batch"]))
+    for f in os.listdir(csrc):
+        if f.endswith((".cu", ".cuh", ".h")):
+            text = open(os.path.join(csrc, f)).read()
+            assert not bad.search(text), f

@@ -1,0 +1,281 @@
+"""Stage-by-stage parity of the CUDA kernels (through the C ABI) against the
+CPU oracle and the reference golden fixtures."""
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import golden_config, load_golden, max_rel
+from oracle import moe_oracle as O
+from reframework_b200 import _lib
+from reframework_b200 import kernels as K
+from reframework_b200.workloads import generate
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+ROUTE_CASES = ["c1_tiny_fp32", "c2_mini_bf16", "c3_mini_bf16", "c4_mini_bf16", "c4_mini_norenorm",
+               "fp16_default", "bf16_gelu_default", "fp32_gelu_tanh", "bf16_entropy_k"]
+
+
+@pytest.fixture(autouse=True)
+def _device_clean(cuda_ok):
+    _lib.set_gemm_impl(0)
+    yield
+    _lib.set_gemm_impl(0)
+    assert _lib.device_status() == 0, "a kernel set the device error word"
+
+
+def _route_inputs(rec):
+    cfg = golden_config(rec)
+    d = generate(cfg)
+    harness = rec["mode"] == "harness"
+    bias = d["bias"][0] if (harness and d["bias"] is not None) else None
+    round_dtype = None if (harness or cfg.dtype == torch.float32) else cfg.dtype
+    return cfg, d, bias, round_dtype
+
+
+def assert_routing_equal(ids, ids_ref, logits_ref, top_k, rel_gap=1e-5):
+    """Routing ids must match exactly; a mismatching token is tolerated only if
+    the experts it swaps sit at the top-k boundary with logits equal to within
+    ``rel_gap`` (a numerical tie).  Such tokens are counted and reported."""
+    ids = ids.cpu().long()
+    bad = (ids != ids_ref).any(dim=1).nonzero().flatten().tolist()
+    for t in bad:
+        lg = logits_ref[t].float()
+        kth = torch.topk(lg, top_k).values[-1]
+        diff = set(ids[t].tolist()) ^ set(ids_ref[t].tolist())
+        gaps = [abs(float(lg[e] - kth)) for e in diff]
+        tol = rel_gap * max(1.0, float(lg.abs().max()))
+        assert diff == set() or max(gaps) <= tol, f"token {t}: ids {ids[t].tolist()} vs {ids_ref[t].tolist()}, gaps {gaps}"
+    assert len(bad) <= max(1, ids.shape[0] // 1000), f"{len(bad)} tokens with tie-swapped routing"
+    return bad
+
+
+@pytest.mark.parametrize("name", ROUTE_CASES)
+def test_router_matches_reference(name):
+    rec = load_golden(name)
+    cfg, d, bias, rdt = _route_inputs(rec)
+    w, ids32, ids64, lg, _ = K.router_topk(
+        d["x"].to(DEV), d["gate"].to(DEV), cfg.top_k, renormalize=cfg.renormalize,
+        bias=None if bias is None else bias.to(DEV), round_dtype=rdt,
+        entropy_k_min=rec.get("entropy_k_min", 0), want_logits=True, ids64=True)
+    logits_ref = O.router_logits(d["x"], d["gate"], bias=bias, fp32=rec["mode"] == "harness")
+    bad = assert_routing_equal(ids64, rec["ids"], logits_ref, cfg.top_k)
+    assert torch.equal(ids32.cpu().long(), ids64.cpu())
+    ok = torch.ones(rec["ids"].shape[0], dtype=torch.bool)
+    ok[bad] = False
+    torch.testing.assert_close(w.cpu()[ok], rec["weights"][ok], rtol=2e-5, atol=2e-6)
+    torch.testing.assert_close(lg.cpu(), logits_ref.float(), rtol=1e-4, atol=1e-4)
+
+
+def test_router_logits_only_mode_matches_torch_fused_topk():
+    g = torch.Generator().manual_seed(11)
+    logits = torch.randn(300, 60, generator=g)
+    for renorm in (True, False):
+        w, _, ids, _, _ = K.router_topk(logits.to(DEV), None, 4, renormalize=renorm, ids64=True, ids32=False)
+        wr, ir = O.torch_fused_topk(logits, 4, renorm)
+        assert torch.equal(ids.cpu(), ir)
+        torch.testing.assert_close(w.cpu(), wr, rtol=2e-5, atol=2e-6)
+
+
+def test_router_shared_gate_sigmoid():
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(70, 256, generator=g).bfloat16()
+    gate = (torch.randn(16, 256, generator=g) * 0.02).bfloat16()
+    sg = (torch.randn(256, generator=g) * 0.02).bfloat16()
+    _, _, _, _, ss = K.router_topk(x.to(DEV), gate.to(DEV), 2, shared_gate=sg.to(DEV))
+    ref = torch.sigmoid(x.float() @ sg.float())
+    torch.testing.assert_close(ss.cpu(), ref, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", ["c1_tiny_fp32", "c2_mini_bf16", "c3_mini_bf16", "c4_mini_bf16", "fp16_default"])
+def test_permute_matches_reference_order(name):
+    rec = load_golden(name)
+    cfg = golden_config(rec)
+    d = generate(cfg)
+    ids = rec["ids"]
+    T, Kk = ids.shape
+    x = d["x"].to(DEV)
+    p = K.permute(ids.to(DEV, torch.int32), cfg.experts, x=x)
+    counts, order = O.permutation(ids.numpy(), cfg.experts)
+    off = p.offsets.cpu().numpy()
+    assert np.array_equal(p.counts.cpu().numpy(), counts)
+    assert np.all(off[:-1] % K.ALIGN == 0)
+    src = p.src_slot.cpu().numpy()
+    ros = p.row_of_slot.cpu().numpy()
+    pos = 0
+    for e in range(cfg.experts):
+        seg = src[off[e]:off[e] + counts[e]]
+        assert np.array_equal(seg, order[pos:pos + counts[e]]), f"expert {e} order"
+        assert np.all(src[off[e] + counts[e]:off[e + 1]] == -1)
+        pos += counts[e]
+    assert np.array_equal(src[ros], np.arange(T * Kk))
+    xp = p.x_perm.cpu()
+    rows = torch.from_numpy(src[:off[-1]]).long()
+    valid = rows >= 0
+    assert torch.equal(xp[:off[-1]][valid], d["x"][rows[valid] // Kk])
+    assert torch.count_nonzero(xp[:off[-1]][~valid]) == 0
+
+
+@pytest.mark.parametrize("align", [1, 128])
+@pytest.mark.parametrize("T,Kk,E", [(1, 1, 1), (37, 3, 5), (20000, 6, 64), (4096, 2, 8), (0, 2, 8)])
+def test_permute_random_stable(T, Kk, E, align):
+    g = torch.Generator().manual_seed(T + E)
+    ids = torch.randint(0, E, (T, Kk), generator=g, dtype=torch.int32)
+    if T > 10:
+        ids[: T // 3] = 0  # a heavy expert spanning several blocks
+    p = K.permute(ids.to(DEV), E, align=align)
+    counts, order = O.permutation(ids.numpy(), E)
+    assert np.array_equal(p.counts.cpu().numpy(), counts)
+    off = p.offsets.cpu().numpy()
+    src = p.src_slot.cpu().numpy()
+    got = np.concatenate([src[off[e]:off[e] + counts[e]] for e in range(E)]) if T else np.zeros(0)
+    assert np.array_equal(got, order)
+
+
+def _segments(counts, align=128):
+    offs = [0]
+    for c in counts:
+        offs.append(offs[-1] + (c + align - 1) // align * align)
+    return offs
+
+
+def _torch_grouped(a, w1, w2, counts, offs, act, slot=None):
+    h_ref, y_ref = {}, {}
+    I = w2.shape[2]
+    for e, c in enumerate(counts):
+        if c == 0:
+            continue
+        s = e if slot is None else slot[e]
+        xa = a[offs[e]:offs[e] + c].float()
+        gu = xa @ w1[s].float().t()
+        h = O.gated_act_and_mul(act, gu)
+        h_ref[e] = h
+        y_ref[e] = h.to(a.dtype).float() @ w2[s].float().t()
+    return h_ref, y_ref
+
+
+@pytest.mark.parametrize("impl", [0, 1])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("H,I,counts,act", [
+    (256, 256, [130, 0, 1, 300], "silu"),
+    (320, 384, [128, 257, 5], "gelu"),
+    (1024, 1408, [700, 64, 129, 3, 0, 256], "silu"),
+    (512, 136, [90, 400], "gelu_tanh"),
+])
+def test_grouped_gemms_vs_torch(impl, dtype, H, I, counts, act):
+    _lib.set_gemm_impl(impl)
+    g = torch.Generator().manual_seed(H + I)
+    E = len(counts)
+    offs = _segments(counts)
+    rows = offs[-1] + 3
+    a = torch.randn(rows, H, generator=g).to(dtype)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.05).to(dtype)
+    w2 = (torch.randn(E, H, I, generator=g) * 0.05).to(dtype)
+    off_t = torch.tensor(offs, dtype=torch.int32, device=DEV)
+    cnt_t = torch.tensor(counts, dtype=torch.int32, device=DEV)
+    h = torch.zeros(rows, I, dtype=dtype, device=DEV)
+    y = torch.zeros(rows, H, dtype=dtype, device=DEV)
+    K.grouped_gemm_gated(a.to(DEV), w1.to(DEV), off_t, cnt_t, h, activation=act)
+    K.grouped_gemm_down(h, w2.to(DEV), off_t, cnt_t, y)
+    h_ref, y_ref = _torch_grouped(a, w1, w2, counts, offs, act)
+    hc, yc = h.cpu(), y.cpu()
+    for e, c in enumerate(counts):
+        if c == 0:
+            continue
+        assert max_rel(hc[offs[e]:offs[e] + c], h_ref[e]) < 8e-3, f"h expert {e}"
+        assert max_rel(yc[offs[e]:offs[e] + c], y_ref[e]) < 8e-3, f"y expert {e}"
+        # rows past the expert's count are never written
+        assert torch.count_nonzero(hc[offs[e] + c:offs[e + 1]]) == 0
+
+
+def test_grouped_gemm_slot_table_and_groups():
+    """Experts read through an expert->slot table, only the listed groups run."""
+    g = torch.Generator().manual_seed(3)
+    dtype = torch.bfloat16
+    H, I, counts = 256, 256, [100, 200, 50, 130]
+    E = len(counts)
+    offs = _segments(counts)
+    a = torch.randn(offs[-1], H, generator=g).to(dtype)
+    S = 6
+    w1 = (torch.randn(S, 2 * I, H, generator=g) * 0.05).to(dtype)
+    w2 = (torch.randn(S, H, I, generator=g) * 0.05).to(dtype)
+    slot = [4, 0, 5, 2]
+    groups = [3, 1]
+    h = torch.zeros(offs[-1], I, dtype=dtype, device=DEV)
+    y = torch.zeros(offs[-1], H, dtype=dtype, device=DEV)
+    kw = dict(slot=torch.tensor(slot, dtype=torch.int32, device=DEV),
+              groups=torch.tensor(groups, dtype=torch.int32, device=DEV))
+    off_t = torch.tensor(offs, dtype=torch.int32, device=DEV)
+    cnt_t = torch.tensor(counts, dtype=torch.int32, device=DEV)
+    K.grouped_gemm_gated(a.to(DEV), w1.to(DEV), off_t, cnt_t, h, **kw)
+    K.grouped_gemm_down(h, w2.to(DEV), off_t, cnt_t, y, **kw)
+    h_ref, y_ref = _torch_grouped(a, w1, w2, counts, offs, "silu", slot=slot)
+    yc = y.cpu()
+    for e in range(E):
+        seg = yc[offs[e]:offs[e] + counts[e]]
+        if e in groups:
+            assert max_rel(seg, y_ref[e]) < 8e-3
+        else:
+            assert torch.count_nonzero(seg) == 0
+
+
+def test_fp32_grouped_gemm_tolerance():
+    """fp32 layers run on CUDA cores with fp32 FMA: within 1e-4 of fp64."""
+    g = torch.Generator().manual_seed(9)
+    H, I, counts = 1024, 2816, [20, 0, 75, 33]
+    offs = _segments(counts)
+    a = torch.randn(offs[-1], H, generator=g)
+    w1 = torch.randn(len(counts), 2 * I, H, generator=g) * 0.02
+    w2 = torch.randn(len(counts), H, I, generator=g) * 0.02
+    off_t = torch.tensor(offs, dtype=torch.int32, device=DEV)
+    cnt_t = torch.tensor(counts, dtype=torch.int32, device=DEV)
+    h = torch.zeros(offs[-1], I, device=DEV)
+    y = torch.zeros(offs[-1], H, device=DEV)
+    K.grouped_gemm_gated(a.to(DEV), w1.to(DEV), off_t, cnt_t, h)
+    K.grouped_gemm_down(h, w2.to(DEV), off_t, cnt_t, y)
+    for e, c in enumerate(counts):
+        if c == 0:
+            continue
+        xa = a[offs[e]:offs[e] + c].double()
+        hr = O.gated_act_and_mul("silu", xa @ w1[e].double().t())
+        yr = hr @ w2[e].double().t()
+        assert max_rel(y.cpu()[offs[e]:offs[e] + c], yr) < 1e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_combine_vs_torch(dtype):
+    g = torch.Generator().manual_seed(1)
+    T, Kk, H, rows = 50, 3, 512, 400
+    y = torch.randn(rows, H, generator=g).to(dtype)
+    ros = torch.randperm(rows, generator=g)[: T * Kk].int()
+    ros[7] = -1  # a dropped slot contributes nothing
+    w = torch.rand(T, Kk, generator=g)
+    sy = torch.randn(T, H, generator=g).to(dtype)
+    ss = torch.rand(T, generator=g)
+    res = torch.randn(T, H, generator=g).to(dtype)
+    out = torch.empty(T, H, dtype=dtype, device=DEV)
+    K.combine(y.to(DEV), ros.to(DEV), w.to(DEV), out, shared_y=sy.to(DEV), shared_scale=ss.to(DEV),
+              residual=res.to(DEV))
+    yy = torch.where(ros.view(T, Kk, 1) >= 0, y.float()[ros.long().clamp_min(0)].view(T, Kk, H), 0)
+    ref = (yy * w.unsqueeze(-1)).sum(1) + ss.unsqueeze(-1) * sy.float() + res.float()
+    tol = 1e-6 if dtype == torch.float32 else 8e-3
+    assert max_rel(out.cpu(), ref) < tol
+
+
+def test_gather_rows_roundtrip():
+    g = torch.Generator().manual_seed(2)
+    src = torch.randn(100, 96, generator=g).bfloat16().to(DEV)
+    idx = torch.tensor([5, -1, 99, 0, 5], dtype=torch.int32, device=DEV)
+    out = torch.full((5, 96), 7.0, dtype=torch.bfloat16, device=DEV)
+    K.gather_rows(src, idx, out)
+    assert torch.equal(out[0], src[5]) and torch.equal(out[2], src[99]) and torch.equal(out[3], src[0])
+    assert torch.count_nonzero(out[1]) == 0
+
+
+def test_bad_expert_id_is_reported_not_faulted():
+    ids = torch.tensor([[0, 9]], dtype=torch.int32, device=DEV)  # 9 >= E
+    p = K.permute(ids, 4)
+    assert p.row_of_slot.cpu().tolist()[1] == -1
+    assert _lib.device_status() == 1

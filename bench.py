@@ -22,7 +22,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -57,52 +56,60 @@ def committed_traffic():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region (SM clock, reasons)."""
+    """SM clock and clock-event reasons sampled through NVML (read-only) every
+    2 ms on a background thread while the timed region runs."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, path):
+    def __init__(self, gpus, path=None):
+        self.gpus = list(gpus)
         self.path = path
-        self.proc = None
+        self.samples = []
+        self._stop = None
+        self._thread = None
 
     def start(self):
+        import threading
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+            import pynvml
+            pynvml.nvmlInit()
+            handles = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in self.gpus]
+            self.max_mhz = max(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM) for h in handles)
         except Exception:
-            self.proc = None
+            return
+        self._stop = threading.Event()
 
-    def stop(self, gpus):
-        if self.proc is None:
+        def loop():
+            while not self._stop.is_set():
+                for i, h in zip(self.gpus, handles):
+                    try:
+                        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    except Exception:
+                        continue
+                    self.samples.append((time.time(), i, sm, rs))
+                time.sleep(0.002)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
+
+    def stop(self):
+        if self._thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.f.close()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in gpus:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+        self._stop.set()
+        self._thread.join()
+        if self.path:
+            with open(self.path, "w") as f:
+                for s in self.samples:
+                    f.write("%.4f,%d,%d,0x%x\n" % s)
+        if not self.samples:
             return None
-        loaded = [s for s in sm if s > 0.5 * (mx or max(sm))] or sm
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = [s[2] for s in self.samples]
+        loaded = [v for v in sm if v > 0.5 * self.max_mhz] or sm
+        reasons = sorted(n for n, bit in self.REASONS.items() if any(s[3] & bit for s in self.samples))
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": "NVML, 2 ms"}
 
 
 # ------------------------------------------------------------------- GPU arm
@@ -190,8 +197,8 @@ def run_gpu(args):
             else:
                 fwd(x)
         barrier()
-        clocks = Clocks(os.path.join(ROOT, "gpurun_out", f"clocks_bench_r{rank}.csv")
-                        if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/clocks_r{rank}.csv")
+        clocks = Clocks(range(world), os.path.join(ROOT, "gpurun_out", "clocks_bench.csv")
+                        if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else None)
         if rank == 0:
             clocks.start()
         step_ms, stage_ms = [], []
@@ -229,7 +236,11 @@ def run_gpu(args):
             e1.record()
             e2e_ms.append((e0, e1))
         barrier()
-        clk = clocks.stop(list(range(world))) if rank == 0 else None
+        clk = clocks.stop() if rank == 0 else None
+    from reframework_b200 import _lib
+    status = _lib.device_status()
+    if status != 0:
+        raise RuntimeError(f"device error word set during the benchmark: {_lib.DEV_ERRORS.get(status, status)}")
     e2e_step = [a.elapsed_time(b) for a, b in e2e_ms]
 
     def maxrank(v):

@@ -117,8 +117,6 @@ __global__ void __launch_bounds__(PT) permute_scatter(const int32_t *ids, int64_
   const int64_t w0 = c0 + (int64_t)warp * SUB;
   const int64_t w1 = min(n, w0 + SUB);
   __syncthreads();
-  int *base = s_tmp;  // unused from here; keep names readable
-  (void)base;
   // move the block base out of s_wc[0..E) before zeroing the warp rows
   for (int e = threadIdx.x; e < E; e += PT) s_tot[e] = s_off[e] + s_wc[e];  // block's first row per expert
   __syncthreads();
@@ -241,7 +239,7 @@ extern "C" int rf_moe_permute(const int32_t *topk_ids, int64_t T, int64_t K, int
                "rf_moe_permute: align must be 1, 64, 128 or 256");
   const int64_t n = T * K;
   RF_CHECK_ARG(n + E * (align - 1) < (int64_t)1 << 31, "rf_moe_permute: too many rows for int32");
-  RF_CHECK_ARG(expert_offsets && expert_counts && row_of_slot && src_slot,
+  RF_CHECK_ARG(expert_offsets && expert_counts && (n == 0 || (row_of_slot && src_slot)),
                "rf_moe_permute: null output");
   RF_CHECK_ARG(workspace_bytes >= rf_moe_permute_workspace_size(n, E) && workspace,
                "rf_moe_permute: workspace too small");

@@ -1,0 +1,338 @@
+"""Expert parallelism: experts sharded across ranks, tokens exchanged all-to-all.
+
+Drop-in for reframework/parallel/ep.py (``shard_range``, ``EPFusedMoE``,
+``ep_enabled``).  The reference replicates every token on every rank, masks
+non-local slots to weight 0 and SUM-all-reduces the full ``[T, H]`` output
+(ep.py:120-150).  Here each rank routes only its own tokens and the rows move
+to the rank that owns their expert:
+
+  1. router + stable permute of this rank's (token, slot) pairs by global
+     expert (compact layout: rows for rank r are one contiguous range, since
+     experts are sharded contiguously);
+  2. counts exchange (all_gather of the per-expert counts [E]) — the one host
+     synchronisation, needed for the all-to-all split sizes;
+  3. dispatch: NCCL all_to_all_single of the permuted rows;
+  4. regroup the received rows by local expert (128-row aligned segments, one
+     gather kernel), grouped gated GEMM, grouped down GEMM;
+  5. return the expert rows with the inverse gather and the reverse
+     all_to_all_single; the combine (weights, shared experts, residual) runs on
+     the tokens' own rank.
+
+Two calling conventions:
+  * ``token_sharded=False`` (default; the reference's contract): every rank is
+    given the same ``x`` and returns the full output.  Each rank takes a
+    contiguous slice of the tokens, runs the exchange above, and the slices are
+    all-gathered.
+  * ``token_sharded=True``: each rank passes and receives only its own tokens
+    (no all-gather) — the data-parallel-attention layout.
+Routing is computed with the same kernel and replicated gate on every rank, so
+per token it is bit-identical to the single-process ``FusedMoE``.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+import torch.distributed as tdist
+import torch.nn as nn
+
+from .. import kernels as K
+from .._lib import ACTIVATIONS, RfMoeError
+from ..moe.moe_layer import FusedMoE, _bank_view
+from . import dist as _dist
+
+__all__ = ["shard_range", "EPFusedMoE", "ep_enabled", "DispatchPlan", "plan_dispatch"]
+
+
+def ep_enabled() -> bool:
+    """True when a live process group has ``ep_size > 1`` (ep.py:40-42)."""
+    return _dist.is_initialized() and _dist.current().ep_size > 1
+
+
+def shard_range(num_experts: int, ep_size: int, ep_rank: int) -> Tuple[int, int]:
+    """Contiguous ``[start, end)`` expert block of ``ep_rank``; the first
+    ``num_experts % ep_size`` ranks take one extra expert (ep.py:45-55)."""
+    base, rem = divmod(num_experts, ep_size)
+    size = base + (1 if ep_rank < rem else 0)
+    start = ep_rank * base + min(ep_rank, rem)
+    return start, start + size
+
+
+@dataclass
+class DispatchPlan:
+    """Host-side bookkeeping of one exchange, from the [R, E] routed-row counts."""
+
+    send_splits: List[int]       # rows this rank sends to each rank
+    recv_splits: List[int]       # rows this rank receives from each rank
+    local_counts: np.ndarray     # [E_local] rows per local expert (all sources)
+    local_offsets: np.ndarray    # [E_local + 1] aligned segment starts
+    rows_capacity: int           # rows of the regrouped GEMM buffer
+    gather_index: np.ndarray     # [rows_capacity] GEMM row -> received row (-1 = pad)
+    inverse_index: np.ndarray    # [recv_total] received row -> GEMM row
+
+    @property
+    def recv_total(self) -> int:
+        return int(sum(self.recv_splits))
+
+    @property
+    def send_total(self) -> int:
+        return int(sum(self.send_splits))
+
+
+def plan_dispatch(counts_all: np.ndarray, rank: int, shards: Sequence[Tuple[int, int]],
+                  align: int = K.ALIGN) -> DispatchPlan:
+    """Split sizes and regroup indices for rank ``rank``.
+
+    ``counts_all[r, e]``: rows rank r routes to global expert e.  Received rows
+    arrive source-major (all of rank 0's rows for my experts, expert by expert,
+    then rank 1's, ...); the GEMM wants them expert-major with each expert's
+    segment starting on an ``align`` boundary, sources in rank order inside it.
+    """
+    counts_all = np.asarray(counts_all, dtype=np.int64)
+    R = counts_all.shape[0]
+    s, e = shards[rank]
+    send = [int(counts_all[rank, a:b].sum()) for a, b in shards]
+    c = counts_all[:, s:e]                       # [R, E_local]
+    recv = [int(x) for x in c.sum(axis=1)]
+    El = e - s
+    local_counts = c.sum(axis=0) if El else np.zeros(0, dtype=np.int64)
+    padded = (local_counts + align - 1) // align * align
+    local_offsets = np.concatenate([[0], np.cumsum(padded)]).astype(np.int64)
+    total = int(c.sum())
+    rows_cap = int(local_offsets[-1]) if El else 0
+    sizes = c.reshape(-1)                        # blocks in receive order (r-major, expert-minor)
+    recv_block_start = np.concatenate([[0], np.cumsum(sizes)[:-1]]) if sizes.size else sizes
+    dst_block_start = (local_offsets[:-1][None, :] + np.cumsum(c, axis=0) - c).reshape(-1)
+    blk = np.repeat(np.arange(sizes.size), sizes)
+    within = np.arange(total) - np.repeat(recv_block_start, sizes)
+    inverse = (dst_block_start[blk] + within).astype(np.int32)
+    gather = np.full(max(rows_cap, 1), -1, dtype=np.int32)
+    gather[inverse] = np.arange(total, dtype=np.int32)
+    return DispatchPlan(send, recv, local_counts, local_offsets, rows_cap, gather, inverse)
+
+
+class EPFusedMoE(nn.Module):
+    """Expert-sharded MoE layer with the same forward / state-dict contract as
+    the reference ``EPFusedMoE`` (ep.py:58-179)."""
+
+    def __init__(self, cfg, ep_size: int, ep_rank: int, *, token_sharded: bool = False,
+                 router_dtype: Optional[torch.dtype] = None, device: Optional[torch.device] = None,
+                 group=None) -> None:
+        super().__init__()
+        self.cfg = cfg
+        self.ep_size = ep_size
+        self.ep_rank = ep_rank
+        self.token_sharded = token_sharded
+        self.num_experts = cfg.num_experts
+        self.top_k = cfg.num_experts_per_tok
+        self.hidden_size = cfg.hidden_size
+        self.intermediate_size = cfg.moe_inter
+        self.activation = getattr(cfg, "moe_activation", "silu")
+        self.renormalize = getattr(cfg, "moe_renormalize", True)
+        self.dtype = cfg.dtype
+        self.router_dtype = router_dtype
+        self.group = group
+        if self.activation not in ACTIVATIONS:
+            raise ValueError(f"unknown gated activation {self.activation!r}")
+        E, H, I = self.num_experts, self.hidden_size, self.intermediate_size
+        fk = {"dtype": self.dtype, "device": device}
+        self.gate = nn.Parameter(torch.empty(E, H, **fk))
+        self.shards = [shard_range(E, ep_size, r) for r in range(ep_size)]
+        self.local_start, self.local_end = self.shards[ep_rank]
+        self.local_count = self.local_end - self.local_start
+        n = self.local_count
+        w1 = torch.empty(n, 2 * I, H, **fk)
+        w2 = torch.empty(n, H, I, **fk)
+        self.experts_w1 = nn.ParameterList([nn.Parameter(w1[j]) for j in range(n)])
+        self.experts_w2 = nn.ParameterList([nn.Parameter(w2[j]) for j in range(n)])
+        self.register_buffer("router_bias", None, persistent=False)
+        self.entropy_adaptive_k = False
+        self.entropy_k_min = 2
+        self.num_shared_experts = 0
+        self._shared: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
+        self._shared_gate: Optional[torch.Tensor] = None
+        self._bank_cache = None
+        self.last_plan: Optional[DispatchPlan] = None
+
+    # --------------------------------------------------------------- build
+    @classmethod
+    def from_full(cls, base: FusedMoE, ep_size: int, ep_rank: int, *, token_sharded: bool = False,
+                  group=None) -> "EPFusedMoE":
+        """Shard a fully loaded :class:`FusedMoE` (ep.py:98-117)."""
+        cfg = _LayerCfg(base.num_experts, base.top_k, base.hidden_size, base.intermediate_size,
+                        base.activation, base.renormalize, base.dtype)
+        ep = cls(cfg, ep_size, ep_rank, token_sharded=token_sharded, router_dtype=base.router_dtype,
+                 device=base.gate.device, group=group)
+        with torch.no_grad():
+            ep.gate.copy_(base.gate)
+            if ep.local_count:
+                w1b, w2b = base._resident_banks()
+                b1, b2 = ep._banks()
+                b1.copy_(w1b[ep.local_start:ep.local_end])
+                b2.copy_(w2b[ep.local_start:ep.local_end])
+        ep.router_bias = base.router_bias
+        ep.entropy_adaptive_k = base.entropy_adaptive_k
+        ep.entropy_k_min = base.entropy_k_min
+        if base.num_shared_experts:
+            ep.num_shared_experts = base.num_shared_experts
+            ep._shared = base._shared_banks()
+            ep._shared_gate = None if base.shared_gate is None else base.shared_gate.detach()
+        return ep
+
+    def set_router_bias(self, bias: Optional[torch.Tensor]) -> None:
+        self.router_bias = None if bias is None else bias.detach().float().to(self.gate.device)
+
+    def _apply(self, fn, recurse=True):
+        self._bank_cache = None
+        return super()._apply(fn, recurse)
+
+    def _banks(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        if self._bank_cache is None:
+            out = []
+            for plist in (self.experts_w1, self.experts_w2):
+                params = list(plist)
+                bank = _bank_view(params)
+                if bank is None:
+                    bank = torch.stack([p.detach() for p in params]).contiguous()
+                    for j, p in enumerate(params):
+                        p.data = bank[j]
+                out.append(bank.detach())
+            self._bank_cache = (out[0], out[1])
+        return self._bank_cache
+
+    # ---------------------------------------------------------------- forward
+    def _pg(self):
+        if self.group is not None:
+            return self.group
+        return _dist.current().group if _dist.is_initialized() else None
+
+    def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if not x.is_cuda:
+            raise RfMoeError("EPFusedMoE runs on the B200 kernels and needs CUDA inputs")
+        x2 = x.reshape(-1, self.hidden_size)
+        if x2.dtype != self.dtype:
+            x2 = x2.to(self.dtype)
+        x2 = x2.contiguous()
+        res2 = None if residual is None else residual.reshape(-1, self.hidden_size).to(self.dtype).contiguous()
+        if self.token_sharded or self.ep_size == 1:
+            out = self._forward_shard(x2, res2)
+        else:
+            T = x2.shape[0]
+            lo = T * self.ep_rank // self.ep_size
+            hi = T * (self.ep_rank + 1) // self.ep_size
+            part = self._forward_shard(x2[lo:hi], None if res2 is None else res2[lo:hi])
+            out = self._all_gather_rows(part, T)
+        if out.dtype != x.dtype:
+            out = out.to(x.dtype)
+        return out if x.dim() <= 2 else out.reshape(x.shape)
+
+    def _all_gather_rows(self, part: torch.Tensor, T: int) -> torch.Tensor:
+        R = self.ep_size
+        mx = (T + R - 1) // R
+        buf = torch.zeros(mx, part.shape[1], dtype=part.dtype, device=part.device)
+        buf[:part.shape[0]] = part
+        outs = [torch.empty_like(buf) for _ in range(R)]
+        tdist.all_gather(outs, buf, group=self._pg())
+        pieces = []
+        for r in range(R):
+            lo, hi = T * r // R, T * (r + 1) // R
+            pieces.append(outs[r][:hi - lo])
+        return torch.cat(pieces, 0)
+
+    def _forward_shard(self, x2: torch.Tensor, res2: Optional[torch.Tensor]) -> torch.Tensor:
+        dev = x2.device
+        T, H = x2.shape
+        E, Kk, I = self.num_experts, self.top_k, self.intermediate_size
+        ek = self.entropy_k_min if self.entropy_adaptive_k else 0
+        rdt = None if (self.router_dtype == torch.float32 or self.dtype == torch.float32) else self.dtype
+        pg = self._pg()
+        if T > 0:
+            w, ids32, _, _, sscale = K.router_topk(x2, self.gate.detach(), Kk, renormalize=self.renormalize,
+                                                   bias=self.router_bias, round_dtype=rdt, entropy_k_min=ek,
+                                                   shared_gate=self._shared_gate)
+            p = K.permute(ids32, E, align=1, x=x2)
+            counts = p.counts
+        else:
+            counts = torch.zeros(E, dtype=torch.int32, device=dev)
+        # (2) counts exchange
+        gathered = [torch.empty_like(counts) for _ in range(self.ep_size)]
+        tdist.all_gather(gathered, counts, group=pg)
+        cnt = torch.stack(gathered).cpu().numpy()
+        plan = plan_dispatch(cnt, self.ep_rank, self.shards)
+        self.last_plan = plan
+        # (3) dispatch
+        send_rows = p.x_perm[:T * Kk] if T > 0 else torch.empty(0, H, dtype=x2.dtype, device=dev)
+        recv = torch.empty(plan.recv_total, H, dtype=x2.dtype, device=dev)
+        _dist.all_to_all_v(recv, send_rows, plan.recv_splits, plan.send_splits, group=pg)
+        # (4) regroup + expert GEMMs
+        y_send = torch.empty(plan.recv_total, H, dtype=x2.dtype, device=dev)
+        if plan.recv_total > 0:
+            host = np.concatenate([plan.gather_index, plan.inverse_index,
+                                   plan.local_offsets.astype(np.int32), plan.local_counts.astype(np.int32)])
+            dev_ix = torch.from_numpy(host).pin_memory().to(dev, non_blocking=True)
+            nG = plan.gather_index.size
+            gidx = dev_ix[:nG]
+            inv = dev_ix[nG:nG + plan.recv_total]
+            off = dev_ix[nG + plan.recv_total:nG + plan.recv_total + self.local_count + 1]
+            lc = dev_ix[nG + plan.recv_total + self.local_count + 1:]
+            xl = torch.empty(plan.rows_capacity, H, dtype=x2.dtype, device=dev)
+            K.gather_rows(recv, gidx, xl)
+            w1b, w2b = self._banks()
+            h = torch.empty(plan.rows_capacity, I, dtype=x2.dtype, device=dev)
+            K.grouped_gemm_gated(xl, w1b, off, lc, h, activation=self.activation)
+            y = torch.empty(plan.rows_capacity, H, dtype=x2.dtype, device=dev)
+            K.grouped_gemm_down(h, w2b, off, lc, y)
+            K.gather_rows(y, inv, y_send)
+        # (5) return trip + combine on the token's rank
+        y_back = torch.empty(T * Kk, H, dtype=x2.dtype, device=dev)
+        _dist.all_to_all_v(y_back, y_send, plan.send_splits, plan.recv_splits, group=pg)
+        out = torch.empty(T, H, dtype=x2.dtype, device=dev)
+        if T == 0:
+            return out
+        shared_y = None
+        if self._shared is not None:
+            shared_y = K.dense_gated_mlp(x2, self._shared[0], self._shared[1], self.activation)
+        return K.combine(y_back, p.row_of_slot, w, out, shared_y=shared_y, shared_scale=sscale, residual=res2)
+
+    # ------------------------------------------------------------- (de)serial
+    def state_dict(self, *args, prefix: str = "", result: Optional[dict] = None, **kwargs) -> Dict[str, torch.Tensor]:
+        """Per-rank HF names with *global* expert ids (ep.py:153-162)."""
+        result = {} if result is None else result
+        pre = f"{prefix}." if prefix else ""
+        result[f"{pre}gate.weight"] = self.gate
+        I = self.intermediate_size
+        for j, g in enumerate(range(self.local_start, self.local_end)):
+            p = f"{pre}experts.{g}"
+            result[f"{p}.gate_proj.weight"] = self.experts_w1[j][:I]
+            result[f"{p}.up_proj.weight"] = self.experts_w1[j][I:]
+            result[f"{p}.down_proj.weight"] = self.experts_w2[j]
+        return result
+
+    def load_state_dict(self, state_dict: Dict[str, torch.Tensor], *args, prefix: str = "", **kwargs) -> None:
+        pre = f"{prefix}." if prefix else ""
+        with torch.no_grad():
+            g = f"{pre}gate.weight"
+            if g in state_dict:
+                self.gate.copy_(state_dict[g].detach().to(dtype=self.dtype))
+            I = self.intermediate_size
+            for j, gg in enumerate(range(self.local_start, self.local_end)):
+                p = f"{pre}experts.{gg}"
+                for half, param in (("gate_proj", self.experts_w1[j][:I]), ("up_proj", self.experts_w1[j][I:]),
+                                    ("down_proj", self.experts_w2[j])):
+                    key = f"{p}.{half}.weight"
+                    if key in state_dict:
+                        param.copy_(state_dict[key].detach().to(dtype=self.dtype))
+
+
+@dataclass
+class _LayerCfg:
+    num_experts: int
+    num_experts_per_tok: int
+    hidden_size: int
+    moe_inter: int
+    moe_activation: str
+    moe_renormalize: bool
+    dtype: torch.dtype

@@ -1,0 +1,132 @@
+"""Expert-parallel host logic on CPU: dispatch plan arithmetic, and the
+all-to-all exchange over world_size-2 gloo ranks (the expert compute is a
+test-side stand-in; the GPU kernels are covered by the gpu tests)."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from reframework_b200.parallel import dist as D
+from reframework_b200.parallel.ep import plan_dispatch, shard_range
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_shard_range_matches_reference():
+    for E, R in [(8, 2), (8, 8), (64, 8), (10, 4), (3, 4), (60, 8)]:
+        spans = [shard_range(E, R, r) for r in range(R)]
+        assert spans == [O.shard_range(E, R, r) for r in range(R)]
+        assert spans[0][0] == 0 and spans[-1][1] == E
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+
+
+def test_plan_dispatch_indices_are_consistent():
+    rng = np.random.default_rng(0)
+    E, R = 10, 4
+    shards = [shard_range(E, R, r) for r in range(R)]
+    cnt = rng.integers(0, 50, size=(R, E))
+    cnt[1, 3] = 0
+    for rank in range(R):
+        pl = plan_dispatch(cnt, rank, shards)
+        s, e = shards[rank]
+        assert pl.send_splits == [int(cnt[rank, a:b].sum()) for a, b in shards]
+        assert pl.recv_splits == [int(cnt[r, s:e].sum()) for r in range(R)]
+        assert np.all(pl.local_offsets[:-1] % 128 == 0)
+        inv = pl.inverse_index
+        assert len(set(inv.tolist())) == inv.size  # injective
+        assert np.array_equal(pl.gather_index[inv], np.arange(inv.size))
+        assert (pl.gather_index >= 0).sum() == pl.recv_total
+        # each received row lands in its expert's segment, sources in rank order
+        pos = 0
+        for r in range(R):
+            for j in range(e - s):
+                n = int(cnt[r, s + j])
+                dst = inv[pos:pos + n]
+                lo = pl.local_offsets[j] + int(cnt[:r, s + j].sum())
+                assert np.array_equal(dst, np.arange(lo, lo + n))
+                pos += n
+
+
+def test_plan_with_more_ranks_than_experts():
+    cnt = np.array([[3, 1], [0, 2], [5, 0]])
+    shards = [shard_range(2, 3, r) for r in range(3)]
+    pl = plan_dispatch(cnt, 2, shards)  # rank 2 owns no expert
+    assert pl.recv_total == 0 and pl.rows_capacity == 0
+    assert pl.send_splits == [5, 0, 0]
+
+
+def _exchange_worker(rank, ctx, E, T, Kk, seed):
+    torch.manual_seed(seed + rank)
+    H = 16
+    ids = torch.randint(0, E, (T, Kk), dtype=torch.int64)
+    x = torch.randn(T, H)
+    counts, order = O.permutation(ids.numpy(), E)
+    x_perm = x[torch.from_numpy(order // Kk)]
+    expert_of_row = ids.reshape(-1)[torch.from_numpy(order)]
+    R = ctx.world_size
+    shards = [shard_range(E, R, r) for r in range(R)]
+    gathered = D.all_gather(torch.from_numpy(counts).int())
+    cnt = torch.stack(gathered).numpy()
+    plan = plan_dispatch(cnt, rank, shards)
+    recv = torch.empty(plan.recv_total, H)
+    D.all_to_all_v(recv, x_perm, plan.recv_splits, plan.send_splits)
+    # stand-in expert compute on the regrouped rows: y = x * (1 + global expert)
+    gi = torch.from_numpy(plan.gather_index[:plan.rows_capacity]).long()
+    xl = torch.where((gi >= 0).unsqueeze(1), recv[gi.clamp_min(0)] if plan.recv_total else torch.zeros(gi.numel(), H),
+                     torch.zeros(1, H))
+    s, _ = shards[rank]
+    y = torch.zeros_like(xl)
+    for j in range(len(plan.local_counts)):
+        lo = int(plan.local_offsets[j])
+        n = int(plan.local_counts[j])
+        y[lo:lo + n] = xl[lo:lo + n] * (1 + s + j)
+    y_send = y[torch.from_numpy(plan.inverse_index).long()] if plan.recv_total else torch.empty(0, H)
+    y_back = torch.empty(T * Kk, H)
+    D.all_to_all_v(y_back, y_send, plan.send_splits, plan.recv_splits)
+    expect = x_perm * (1 + expert_of_row.float()).unsqueeze(1)
+    assert torch.equal(y_back, expect), f"rank {rank}: rows did not come back to their slots"
+
+
+@pytest.mark.parametrize("E,T,Kk", [(8, 40, 2), (5, 33, 3), (1, 7, 1)])
+def test_ep_exchange_gloo_world2(E, T, Kk):
+    D.run(_exchange_worker, world_size=2, backend="gloo",
+          init_method=f"tcp://127.0.0.1:{_free_port()}", ep_size=2, args=(E, T, Kk, 3))
+
+
+def _ctx_worker(rank, ctx):
+    assert ctx.ep_rank == rank and ctx.world_size == 2 and D.get_rank() == rank
+    t = torch.tensor([rank + 1.0])
+    D.all_reduce_sum(t)
+    assert float(t) == 3.0
+    chunks = D.all_to_all(torch.tensor([10.0 * rank, 10.0 * rank + 1]))
+    assert chunks.tolist() == [rank, 10 + rank]
+
+
+def test_dist_context_and_collectives_gloo():
+    D.run(_ctx_worker, world_size=2, backend="gloo", init_method=f"tcp://127.0.0.1:{_free_port()}", ep_size=2)
+
+
+def _failing_worker(rank, ctx):
+    if rank == 1:
+        raise SystemExit(3)
+
+
+def test_run_reports_failed_rank():
+    with pytest.raises(RuntimeError, match="exit codes"):
+        D.run(_failing_worker, world_size=2, backend="gloo", init_method=f"tcp://127.0.0.1:{_free_port()}")
+
+
+def test_current_without_group_raises():
+    D.destroy()
+    with pytest.raises(RuntimeError, match="No process group"):
+        D.current()

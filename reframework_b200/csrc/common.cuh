@@ -100,6 +100,25 @@ __device__ __forceinline__ float act_gate(int act, float g) {
   return 0.5f * g * (1.0f + tanhf(k0 * (g + k1 * g * g * g)));
 }
 
+// Round an fp32 value to the storage type T and back (identity for fp32).
+template <typename T>
+__device__ __forceinline__ float round_to(float v) {
+  if constexpr (sizeof(T) == 4) return v;
+  else return Cvt<T>::to_f(Cvt<T>::from_f(v));
+}
+
+// One element of the gated activation with the rounding points of the
+// reference for a 16-bit layer: the gate|up GEMM output is stored in T
+// (fused.py:81), act() runs on it and rounds to T, and the product of the two
+// T tensors rounds to T (activation.py:20-21).  The caller's final store
+// performs that last rounding.  For fp32 every rounding is the identity.
+template <typename T>
+__device__ __forceinline__ float gated_elem(int act, float g, float u) {
+  const float gt = round_to<T>(g);
+  const float ut = round_to<T>(u);
+  return round_to<T>(act_gate(act, gt)) * ut;
+}
+
 }  // namespace rf
 
 // Defines this translation unit's device error word, the device helper

@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(NT) simt_grouped_gemm(rf::GroupedGemmArgs p) {
     for (int j = 0; j < 4; ++j) {
       const int c = n0 + tx * 4 + j;
       if (c >= p.N) continue;
-      const float v = GATED ? rf::act_gate(p.act, accg[i][j]) * accu[i][j] : accg[i][j];
+      const float v = GATED ? rf::gated_elem<T>(p.act, accg[i][j], accu[i][j]) : accg[i][j];
       out[(row0 + r) * p.N + c] = rf::Cvt<T>::from_f(v);
     }
   }

@@ -413,9 +413,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint32_t pk[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const float h0 = rf::act_gate(p.act, __uint_as_float(g[2 * j])) * __uint_as_float(u[2 * j]);
+              const float h0 = rf::gated_elem<T>(p.act, __uint_as_float(g[2 * j]), __uint_as_float(u[2 * j]));
               const float h1 =
-                  rf::act_gate(p.act, __uint_as_float(g[2 * j + 1])) * __uint_as_float(u[2 * j + 1]);
+                  rf::gated_elem<T>(p.act, __uint_as_float(g[2 * j + 1]), __uint_as_float(u[2 * j + 1]));
               pk[j] = rf::pack2<T>(h0, h1);
             }
 #pragma unroll

@@ -20,7 +20,7 @@ namespace {
 
 constexpr int PT = 256;        // threads per block (8 warps)
 constexpr int PW = PT / 32;
-constexpr int CHUNK = 4096;    // pairs per block
+constexpr int CHUNK = 1024;    // pairs per block
 constexpr int SUB = CHUNK / PW;  // pairs per warp
 
 __global__ void __launch_bounds__(PT) permute_hist(const int32_t *ids, int64_t n, int E,

@@ -14,8 +14,9 @@ RF_DEVICE_ERROR_WORD();
 namespace {
 
 constexpr int WARPS = 8;
-constexpr int EC = 16;      // experts accumulated per pass over the x row
-constexpr int VEC = 8;      // elements per lane per step (16 B of a 16-bit type)
+constexpr int EC = 8;       // experts accumulated per pass over the x row
+constexpr int VEC = 8;      // elements per vector (16 B of a 16-bit type)
+constexpr int XV = 8;       // vectors per lane per chunk: chunk = 2048 elements
 constexpr int KMAX = 16;
 
 template <typename T>
@@ -68,34 +69,53 @@ __global__ void __launch_bounds__(WARPS * 32) router_kernel(RouterArgs a) {
     if (!gate) {  // x already holds the logits (H == E)
       for (int e = lane; e < a.E; e += 32) lg[e] = rf::Cvt<TX>::to_f(xr[e]);
     }
-    // ---- logits: lanes stride over H, fixed-order fp32 FMA, butterfly reduce
-    for (int c0 = 0; gate && c0 < R; c0 += EC) {
+    // ---- logits.  The x row is consumed in chunks of 32 lanes x XV vectors
+    // of 8 elements, all loads of a chunk issued before any arithmetic (the
+    // row is the HBM traffic; the gate rows come from L1).  Each lane keeps a
+    // fixed-order fp32 partial sum per expert; a butterfly reduces them.
+    for (int g0 = 0; gate && g0 < R; g0 += EC) {
       float acc[EC];
 #pragma unroll
       for (int j = 0; j < EC; ++j) acc[j] = 0.f;
-      for (int h = lane * VEC; h < a.H; h += 32 * VEC) {
-        float xf[VEC];
-        load8<TX>(xr + h, xf);
+      for (int h0 = 0; h0 < a.H; h0 += 32 * VEC * XV) {
+        float xf[XV][VEC];
+#pragma unroll
+        for (int v = 0; v < XV; ++v) {
+          const int h = h0 + (v * 32 + lane) * VEC;
+          if (h < a.H) load8<TX>(xr + h, xf[v]);
+          else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) xf[v][i] = 0.f;
+          }
+        }
 #pragma unroll
         for (int j = 0; j < EC; ++j) {
-          const int e = c0 + j;
+          const int e = g0 + j;
           if (e < R) {
             const TG *row = (e < a.E) ? gate + (int64_t)e * a.H : sgate;
-            float gf[VEC];
-            load8<TG>(row + h, gf);
             float s = acc[j];
 #pragma unroll
-            for (int i = 0; i < VEC; ++i) s = fmaf(xf[i], gf[i], s);
+            for (int v = 0; v < XV; ++v) {
+              const int h = h0 + (v * 32 + lane) * VEC;
+              if (h < a.H) {
+                float gf[VEC];
+                load8<TG>(row + h, gf);
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) s = fmaf(xf[v][i], gf[i], s);
+              }
+            }
             acc[j] = s;
           }
         }
       }
 #pragma unroll
       for (int j = 0; j < EC; ++j) {
-        float v = acc[j];
+        if (g0 + j < R) {  // warp-uniform
+          float v = acc[j];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0 && c0 + j < R) lg[c0 + j] = v;
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == 0) lg[g0 + j] = v;
+        }
       }
     }
     __syncwarp();

@@ -47,7 +47,7 @@ def test_grouped_gemm_many_tiles_per_cta(act):
         if c == 0:
             continue
         xa = a[offs[e]:offs[e] + c].float()
-        hr = O.gated_act_and_mul(act, xa @ w1[e].float().t())
+        hr = O.gated_act_and_mul(act, (xa @ w1[e].float().t()).to(dtype)).float()
         yr = h[offs[e]:offs[e] + c].float() @ w2[e].float().t()
         assert max_rel(h[offs[e]:offs[e] + c], hr) < 8e-3, f"h expert {e}"
         assert max_rel(y[offs[e]:offs[e] + c], yr) < 8e-3, f"y expert {e}"

@@ -149,8 +149,8 @@ def _torch_grouped(a, w1, w2, counts, offs, act, slot=None):
             continue
         s = e if slot is None else slot[e]
         xa = a[offs[e]:offs[e] + c].float()
-        gu = xa @ w1[s].float().t()
-        h = O.gated_act_and_mul(act, gu)
+        gu = (xa @ w1[s].float().t()).to(a.dtype)  # the reference stores the GEMM output in the layer dtype
+        h = O.gated_act_and_mul(act, gu).float()
         h_ref[e] = h
         y_ref[e] = h.to(a.dtype).float() @ w2[s].float().t()
     return h_ref, y_ref

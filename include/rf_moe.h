@@ -145,9 +145,12 @@ int rf_moe_gather_rows(const void *src, const int32_t *index, int64_t index_div,
  *     h[r, j] = act(sum_k a[r,k] * w1[s,j,k]) * (sum_k a[r,k] * w1[s,I+j,k])
  *   with s = expert_slot ? expert_slot[e] : e, j in [0, I).
  * a [rows_capacity, H], w1 [num_slots, 2I, H] (rows 0..I-1 gate, I..2I-1 up),
- * h [rows_capacity, I]; all in `dtype`; fp32 accumulation.  bf16/fp16 run on
- * tcgen05 tensor cores (TMA-fed, TMEM accumulators) and need H % 8 == 0,
- * I % 8 == 0 and align 128; fp32 (and other shapes) run on CUDA cores.
+ * h [rows_capacity, I]; all in `dtype`; fp32 accumulation.  For 16-bit dtypes
+ * the epilogue keeps the reference's rounding points: both sums are rounded
+ * to `dtype`, act() of the rounded gate is rounded to `dtype`, and the product
+ * is rounded on store.  bf16/fp16 run on tcgen05 tensor cores (TMA-fed, TMEM
+ * accumulators) when H % 8 == 0 and I % 8 == 0; fp32 (and other shapes) run
+ * on CUDA cores.  Segments may start at any row.
  * groups: expert ids to compute (NULL = all E experts, n_groups ignored).
  */
 int rf_moe_grouped_gemm_gated(const void *a, const void *w1, void *h,
@@ -177,18 +180,28 @@ int rf_moe_grouped_gemm_down(const void *h, const void *w2, void *y,
                              int64_t E, int64_t num_slots, int64_t rows_capacity,
                              int64_t H, int64_t I, int dtype, rf_stream_t stream);
 
+/* Summation modes of rf_moe_combine. */
+#define RF_COMBINE_REFERENCE 0  /* the reference's rounding points and order */
+#define RF_COMBINE_FP32 1       /* fp32 accumulation, one rounding */
+
 /*
- * K5 — weighted combine (fp32 accumulation, one rounding):
+ * K5 — weighted combine:
  *   out[t] = sum_k topk_weights[t,k] * y[row_of_slot[t*K+k]]     (rows < 0 skipped)
  *          + (shared_y ? (shared_scale ? shared_scale[t] : 1) * shared_y[t] : 0)
  *          + (residual ? residual[t] : 0)
  *          + (accumulate ? out[t] : 0)
  * y [rows, H], shared_y/residual/out [T, H], all in `dtype`.
+ * mode RF_COMBINE_REFERENCE rounds like the reference's fused_experts: the
+ * weight is cast to `dtype`, every weighted row is rounded to `dtype`, and the
+ * rows are accumulated in `dtype` in ascending expert order (ascending row of
+ * the expert-major permuted layout); the shared and residual terms are added
+ * with one rounding each.  RF_COMBINE_FP32 accumulates everything in fp32 and
+ * rounds once.
  */
 int rf_moe_combine(const void *y, const int32_t *row_of_slot, const float *topk_weights,
                    int64_t T, int64_t K, int64_t H, int dtype,
                    const void *shared_y, const float *shared_scale, const void *residual,
-                   int accumulate, void *out, rf_stream_t stream);
+                   int accumulate, int mode, void *out, rf_stream_t stream);
 
 #ifdef __cplusplus
 }

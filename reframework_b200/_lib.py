@@ -20,6 +20,7 @@ LIB_PATH = os.path.join(_HERE, "_rf_moe.so")
 
 RF_F32, RF_F16, RF_BF16 = 0, 1, 2
 ACTIVATIONS = {"silu": 0, "gelu": 1, "gelu_tanh": 2}
+COMBINE_REFERENCE, COMBINE_FP32 = 0, 1
 DEV_ERRORS = {0: "ok", 1: "routed expert id out of range", 2: "pipeline wait timed out"}
 
 _c_void_p = ctypes.c_void_p
@@ -49,7 +50,7 @@ _SIGNATURES = {
                                         _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64,
                                         _int, _c_void_p]),
     "rf_moe_combine": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p,
-                              _c_void_p, _c_void_p, _int, _c_void_p, _c_void_p]),
+                              _c_void_p, _c_void_p, _int, _int, _c_void_p, _c_void_p]),
 }
 
 

@@ -159,7 +159,10 @@ def grouped_gemm_down(h: torch.Tensor, w2: torch.Tensor, offsets: torch.Tensor, 
 # ----------------------------------------------------------------------- K5
 def combine(y: torch.Tensor, row_of_slot: torch.Tensor, weights: torch.Tensor, out: torch.Tensor, *,
             shared_y: Optional[torch.Tensor] = None, shared_scale: Optional[torch.Tensor] = None,
-            residual: Optional[torch.Tensor] = None, accumulate: bool = False) -> torch.Tensor:
+            residual: Optional[torch.Tensor] = None, accumulate: bool = False,
+            precise: bool = False) -> torch.Tensor:
+    """``out[t] = sum_k w[t,k] y[row(t,k)] (+ shared, residual)``.  Default: the
+    reference's rounding points and order; ``precise=True``: fp32 accumulation."""
     dev = _require_cuda(y, row_of_slot, weights, out, shared_y, shared_scale, residual)
     T, K = weights.shape
     H = out.shape[1]
@@ -168,7 +171,7 @@ def combine(y: torch.Tensor, row_of_slot: torch.Tensor, weights: torch.Tensor, o
         weights = weights.float()
     rc = lib().rf_moe_combine(ptr(y), ptr(row_of_slot), ptr(weights), T, K, H, dtype_code(out.dtype),
                               ptr(shared_y), ptr(shared_scale), ptr(residual), int(bool(accumulate)),
-                              ptr(out), stream_of(dev))
+                              _lib.COMBINE_FP32 if precise else _lib.COMBINE_REFERENCE, ptr(out), stream_of(dev))
     check(rc, "rf_moe_combine")
     return out
 
@@ -207,7 +210,7 @@ def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, weights: to
                 ids32: torch.Tensor, *, activation: str = "silu", shared_y: Optional[torch.Tensor] = None,
                 shared_scale: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
                 out: Optional[torch.Tensor] = None, slot: Optional[torch.Tensor] = None,
-                num_experts: Optional[int] = None) -> torch.Tensor:
+                num_experts: Optional[int] = None, precise: bool = False) -> torch.Tensor:
     """Permute -> grouped gated GEMM -> grouped down GEMM -> combine (routing given)."""
     T, H = x.shape
     E = num_experts if num_experts is not None else w1.shape[0]
@@ -220,4 +223,4 @@ def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, weights: to
     if out is None:
         out = torch.empty(T, H, dtype=x.dtype, device=x.device)
     return combine(y, p.row_of_slot, weights, out, shared_y=shared_y, shared_scale=shared_scale,
-                   residual=residual)
+                   residual=residual, precise=precise)

@@ -144,6 +144,10 @@ class FusedMoE(nn.Module):
         self._last_step_t: Optional[float] = None
         self.entropy_adaptive_k = False
         self.entropy_k_min = 2
+        # False: the combine keeps the reference's rounding points and order
+        # (outputs match the reference bit for bit wherever the expert GEMMs
+        # round identically); True: fp32 accumulation, one rounding.
+        self.precise_combine = False
 
     # ---------------------------------------------------------------- factories
     @classmethod
@@ -296,7 +300,8 @@ class FusedMoE(nn.Module):
         else:
             w1b, w2b = self._resident_banks()
             out = K.moe_experts(x2, w1b, w2b, w, ids32, activation=self.activation,
-                                shared_y=shared_y, shared_scale=sscale, residual=res2)
+                                shared_y=shared_y, shared_scale=sscale, residual=res2,
+                                precise=self.precise_combine)
         if out.dtype != x.dtype:
             out = out.to(x.dtype)
         if x.dim() == 1:
@@ -355,7 +360,8 @@ class FusedMoE(nn.Module):
             pending.discard(e)
         cache._evict((), soft)  # only trims a pool that had to grow past capacity
         out = torch.empty(T, H, dtype=x2.dtype, device=dev)
-        K.combine(y, p.row_of_slot, w, out, shared_y=shared_y, shared_scale=sscale, residual=res2)
+        K.combine(y, p.row_of_slot, w, out, shared_y=shared_y, shared_scale=sscale, residual=res2,
+                  precise=self.precise_combine)
         if self._predictor is not None:
             self._predictor.record_step(active, is_prefill=(T > 1), forward_ms=self._since_last_step_ms(),
                                         inflight_bytes=(self._shuttle.inflight_bytes()

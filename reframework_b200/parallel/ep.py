@@ -151,6 +151,7 @@ class EPFusedMoE(nn.Module):
         self.register_buffer("router_bias", None, persistent=False)
         self.entropy_adaptive_k = False
         self.entropy_k_min = 2
+        self.precise_combine = False
         self.num_shared_experts = 0
         self._shared: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
         self._shared_gate: Optional[torch.Tensor] = None
@@ -176,6 +177,7 @@ class EPFusedMoE(nn.Module):
         ep.router_bias = base.router_bias
         ep.entropy_adaptive_k = base.entropy_adaptive_k
         ep.entropy_k_min = base.entropy_k_min
+        ep.precise_combine = base.precise_combine
         if base.num_shared_experts:
             ep.num_shared_experts = base.num_shared_experts
             ep._shared = base._shared_banks()
@@ -295,7 +297,8 @@ class EPFusedMoE(nn.Module):
         shared_y = None
         if self._shared is not None:
             shared_y = K.dense_gated_mlp(x2, self._shared[0], self._shared[1], self.activation)
-        return K.combine(y_back, p.row_of_slot, w, out, shared_y=shared_y, shared_scale=sscale, residual=res2)
+        return K.combine(y_back, p.row_of_slot, w, out, shared_y=shared_y, shared_scale=sscale, residual=res2,
+                         precise=self.precise_combine)
 
     # ------------------------------------------------------------- (de)serial
     def state_dict(self, *args, prefix: str = "", result: Optional[dict] = None, **kwargs) -> Dict[str, torch.Tensor]:

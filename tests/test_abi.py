@@ -43,8 +43,10 @@ def test_version_and_sizes():
                                     None, None, None, None, None), "dtype"),
     (lambda L: L.rf_moe_permute(None, 4, 2, 8, 3, None, 2, 64, None, None, None, None, None, None, 0,
                                 None), "align"),
-    (lambda L: L.rf_moe_combine(None, None, None, 4, 2, 60, 2, None, None, None, 0, None, None),
+    (lambda L: L.rf_moe_combine(None, None, None, 4, 2, 60, 2, None, None, None, 0, 0, None, None),
      "multiple of 16"),
+    (lambda L: L.rf_moe_combine(None, None, None, 4, 2, 64, 2, None, None, None, 0, 7, None, None),
+     "unknown mode"),
     (lambda L: L.rf_moe_grouped_gemm_gated(None, None, None, None, None, None, None, 0, 8, 8, 64, 64,
                                            64, 2, 9, None), "activation"),
     (lambda L: L.rf_moe_set_gemm_impl(5), "0 or 1"),

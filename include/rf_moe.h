@@ -131,6 +131,37 @@ int rf_moe_permute(const int32_t *topk_ids, int64_t T, int64_t K, int64_t E, int
                    rf_stream_t stream);
 
 /*
+ * rf_moe_permute without a workspace argument: it allocates nothing and uses
+ * no caller scratch.  There is no counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory at the point where they
+ * permute: for example a host that plans every device buffer at start-up and
+ * forbids later allocations (cudaMalloc may also synchronise the device, which
+ * a latency-bound serving loop cannot afford), or a plugin whose host owns the
+ * memory pool and only hands it input and output buffers.  The caller still
+ * passes every input and output; the kernels' scratch (per-block expert
+ * histograms) is a file-scope device array of 65,536 int32 words (256 KiB)
+ * that every GPU which loads the library holds until the process exits.
+ *
+ * Limit: ceil(T*K / 1024) * E <= 65536 (e.g. T*K <= 1,048,576 pairs with 64
+ * experts); larger calls fail with RF_ERR_ARG and a message — use
+ * rf_moe_permute with a workspace for them.  Outputs and their meaning are
+ * those of rf_moe_permute.
+ *
+ * The first call on a device looks up the array's device address for that
+ * device (cudaGetSymbolAddress, with that device current); make that first
+ * call before any stream capture.  All calls share the one array, which keeps
+ * the last call's contents (nothing in it needs to start at zero: each call
+ * overwrites the words it reads), so calls that overlap on the same GPU —
+ * from two streams at once, for instance — race; order them on one stream or
+ * with events.
+ */
+int rf_moe_permute_noalloc(const int32_t *topk_ids, int64_t T, int64_t K, int64_t E, int64_t align,
+                           const void *x, int dtype, int64_t H,
+                           int32_t *expert_offsets, int32_t *expert_counts, int32_t *row_of_slot,
+                           int32_t *src_slot, void *x_perm, rf_stream_t stream);
+
+/*
  * Row gather: dst[r] = src[index[r] / index_div] for r < n_rows (n_rows read
  * from *n_rows_dev when non-NULL, else n_rows_max), zero rows where index < 0.
  * Rows are `row_bytes` long (a multiple of 16); src/dst 16-byte aligned.

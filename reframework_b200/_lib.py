@@ -40,6 +40,8 @@ _SIGNATURES = {
     "rf_moe_permute": (_int, [_c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _int, _i64, _c_void_p,
                               _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t,
                               _c_void_p]),
+    "rf_moe_permute_noalloc": (_int, [_c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _int, _i64, _c_void_p,
+                                      _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "rf_moe_gather_rows": (_int, [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p,
                                   _c_void_p]),
     "rf_moe_set_gemm_impl": (_int, [_int]),

@@ -12,6 +12,10 @@
 //                       one warp per row with 16-byte vector copies
 // The first two kernels touch only 4-byte ids; the gather is the HBM-bound part
 // (reads and writes T*K*H elements).
+#include <mutex>
+#include <string>
+#include <vector>
+
 #include "common.cuh"
 
 RF_DEVICE_ERROR_WORD();
@@ -265,6 +269,94 @@ extern "C" int rf_moe_permute(const int32_t *topk_ids, int64_t T, int64_t K, int
                                           nblk, expert_offsets, expert_counts, row_of_slot,
                                           src_slot);
   rc = rf::check_launch("rf_moe_permute(scatter)");
+  if (rc) return rc;
+  if (x_perm) {
+    const int64_t rows_cap = n + E * (align - 1);
+    return launch_gather(x, src_slot, K, rows_cap, expert_offsets + E,
+                         H * (int64_t)rf::dtype_size(dtype), x_perm, st);
+  }
+  return RF_OK;
+}
+
+// ---------------------------------------------------------------------------
+// rf_moe_permute_noalloc — the same permute for callers that cannot allocate
+// device memory.  Its only scratch (the per-block expert histograms) lives in
+// this file-scope device array instead of a caller workspace.  Every GPU that
+// loads the library holds the array until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kNoAllocScratchWords = 1 << 16;  // 65,536 int32 = 256 KiB per device
+static __device__ __align__(256) int32_t g_noalloc_block_counts[kNoAllocScratchWords];
+
+// Device address of g_noalloc_block_counts, fetched once per device.  In host
+// code the array's name is only a host-side handle, so the kernels must be
+// given this address instead.
+int noalloc_scratch(int32_t **out) {
+  static std::mutex mu;
+  static std::vector<int32_t *> addr;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return rf::fail(RF_ERR_CUDA, std::string("rf_moe_permute_noalloc: cudaGetDevice: ") + cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)addr.size() <= dev) addr.resize(dev + 1, nullptr);
+  if (!addr[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_block_counts);
+    if (e != cudaSuccess || !p)
+      return rf::fail(RF_ERR_CUDA, std::string("rf_moe_permute_noalloc: cudaGetSymbolAddress: ") +
+                                       cudaGetErrorString(e));
+    addr[dev] = static_cast<int32_t *>(p);
+  }
+  *out = addr[dev];
+  return RF_OK;
+}
+
+}  // namespace
+
+extern "C" int rf_moe_permute_noalloc(const int32_t *topk_ids, int64_t T, int64_t K, int64_t E,
+                                      int64_t align, const void *x, int dtype, int64_t H,
+                                      int32_t *expert_offsets, int32_t *expert_counts,
+                                      int32_t *row_of_slot, int32_t *src_slot, void *x_perm,
+                                      rf_stream_t stream) {
+  RF_CHECK_ARG(T >= 0 && K >= 1 && E >= 1 && E <= 1024, "rf_moe_permute_noalloc: bad sizes (E <= 1024)");
+  RF_CHECK_ARG(align == 1 || align == 64 || align == 128 || align == 256,
+               "rf_moe_permute_noalloc: align must be 1, 64, 128 or 256");
+  const int64_t n = T * K;
+  RF_CHECK_ARG(n + E * (align - 1) < (int64_t)1 << 31, "rf_moe_permute_noalloc: too many rows for int32");
+  const int64_t nblk = n > 0 ? (n + CHUNK - 1) / CHUNK : 1;
+  if (nblk * E > kNoAllocScratchWords)
+    return rf::fail(RF_ERR_ARG,
+                    "rf_moe_permute_noalloc: ceil(T*K/" + std::to_string(CHUNK) + ") * E = " +
+                        std::to_string(nblk * E) + " histogram words exceeds the fixed scratch of " +
+                        std::to_string(kNoAllocScratchWords) + "; use rf_moe_permute with a workspace");
+  RF_CHECK_ARG(expert_offsets && expert_counts && (n == 0 || (row_of_slot && src_slot)),
+               "rf_moe_permute_noalloc: null output");
+  RF_CHECK_ARG(!x_perm || (x && rf::valid_dtype(dtype) && H > 0 &&
+                           (H * (int64_t)rf::dtype_size(dtype)) % 16 == 0),
+               "rf_moe_permute_noalloc: gather needs x, a dtype and H*elsize % 16 == 0");
+  int32_t *block_counts = nullptr;
+  int rc = noalloc_scratch(&block_counts);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (n == 0) {
+    cudaError_t e1 = cudaMemsetAsync(expert_offsets, 0, (E + 1) * 4, st);
+    cudaError_t e2 = cudaMemsetAsync(expert_counts, 0, E * 4, st);
+    if (e1 != cudaSuccess || e2 != cudaSuccess)
+      return rf::fail(RF_ERR_CUDA, "rf_moe_permute_noalloc: memset failed");
+    return RF_OK;
+  }
+  // permute_hist writes every one of the nblk*E words the scatter reads, so
+  // nothing left in the array by an earlier call needs clearing.
+  permute_hist<<<(int)nblk, PT, E * sizeof(int), st>>>(topk_ids, n, (int)E, block_counts);
+  rc = rf::check_launch("rf_moe_permute_noalloc(hist)");
+  if (rc) return rc;
+  const size_t smem = (size_t)(2 * E + PW * E + PW) * sizeof(int);
+  permute_scatter<<<(int)nblk, PT, smem, st>>>(topk_ids, n, (int)K, (int)E, (int)align, block_counts,
+                                               (int)nblk, expert_offsets, expert_counts, row_of_slot,
+                                               src_slot);
+  rc = rf::check_launch("rf_moe_permute_noalloc(scatter)");
   if (rc) return rc;
   if (x_perm) {
     const int64_t rows_cap = n + E * (align - 1);

@@ -190,6 +190,9 @@ def e2e_run(fwd, xh, steps, dev):
 
 
 LAUNCHES_PER_FORWARD = 7  # router, permute x3 (histogram, scatter, gather), gated GEMM, down GEMM, combine
+# EP: router, permute x3, regroup gather, gated GEMM, down GEMM, return gather, combine (+ send-order
+# and un-permute gathers when replicas split an expert); NCCL's own kernels are not counted
+EP_LAUNCHES_PER_FORWARD = 9
 
 
 def run_gpu(args):
@@ -215,6 +218,12 @@ def run_gpu(args):
         layer = EPFusedMoE.from_full(full, world, rank, token_sharded=True)
         del full
         torch.cuda.empty_cache()
+        if args.redundant > 0:
+            # load-balancing calibration: one forward gives the global per-expert
+            # counts, then every rank takes `redundant` replicas of busy experts
+            with torch.no_grad():
+                layer(x)
+            layer.rebalance(redundant=args.redundant)
 
         def fwd(inp):
             return layer(inp)
@@ -289,12 +298,16 @@ def run_gpu(args):
                    "inter": cfg.inter, "tokens_per_gpu": T, "global_tokens": tokens,
                    "router": "fp32 logits + N(0,1) bias", "parallelism": f"ep{world}" if world > 1 else "single",
                    "l2": L2_NOTE},
+        "eplb": ({"redundant_slots_per_rank": args.redundant, "placement": [list(s) for s in layer.placement.slots],
+                  "calibration": "global per-expert counts of the first warm-up forward"}
+                 if world > 1 else None),
         "e2e": {"value": tokens / (ms_e2e / 1e3), "unit": UNIT,
                 "h2d_bytes_per_step": x.numel() * x.element_size(),
                 "d2h_bytes_per_step": x.numel() * x.element_size(),
                 "ms_per_step": ms_e2e, "api": "FusedMoE.forward" if world == 1 else "EPFusedMoE.forward",
                 "pipeline": "H2D of step i+1 and D2H of step i on two copy streams overlap step i's forward"},
-        "gpu_launches": LAUNCHES_PER_FORWARD * args.steps if world == 1 else None,
+        "gpu_launches": args.steps * (LAUNCHES_PER_FORWARD if world == 1 else
+                                      EP_LAUNCHES_PER_FORWARD + (2 if layer.last_plan.send_index is not None else 0)),
         "clocks": clk,
     }
     if stage_fn:
@@ -429,6 +442,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=25.0)
     ap.add_argument("--ref-tokens", type=int, default=512)
+    ap.add_argument("--redundant", type=int, default=2,
+                    help="EP: replica expert slots per rank for load balancing (0 = contiguous shards only)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -43,8 +43,9 @@ from .. import kernels as K
 from .._lib import ACTIVATIONS, RfMoeError
 from ..moe.moe_layer import FusedMoE, _bank_view
 from . import dist as _dist
+from .eplb import Placement, place_experts, split_rows
 
-__all__ = ["shard_range", "EPFusedMoE", "ep_enabled", "DispatchPlan", "plan_dispatch"]
+__all__ = ["shard_range", "EPFusedMoE", "ep_enabled", "DispatchPlan", "plan_dispatch", "plan_exchange"]
 
 
 def ep_enabled() -> bool:
@@ -67,11 +68,12 @@ class DispatchPlan:
 
     send_splits: List[int]       # rows this rank sends to each rank
     recv_splits: List[int]       # rows this rank receives from each rank
-    local_counts: np.ndarray     # [E_local] rows per local expert (all sources)
-    local_offsets: np.ndarray    # [E_local + 1] aligned segment starts
+    local_counts: np.ndarray     # [slots] rows per local expert slot (all sources)
+    local_offsets: np.ndarray    # [slots + 1] aligned segment starts
     rows_capacity: int           # rows of the regrouped GEMM buffer
     gather_index: np.ndarray     # [rows_capacity] GEMM row -> received row (-1 = pad)
     inverse_index: np.ndarray    # [recv_total] received row -> GEMM row
+    send_index: Optional[np.ndarray] = None  # send position -> permuted row (None = identity)
 
     @property
     def recv_total(self) -> int:
@@ -82,28 +84,72 @@ class DispatchPlan:
         return int(sum(self.send_splits))
 
 
-def plan_dispatch(counts_all: np.ndarray, rank: int, shards: Sequence[Tuple[int, int]],
-                  align: int = K.ALIGN) -> DispatchPlan:
-    """Split sizes and regroup indices for rank ``rank``.
+def plan_exchange(counts_all: np.ndarray, rank: int, placement: Placement,
+                  quota: Optional[np.ndarray] = None, align: int = K.ALIGN) -> DispatchPlan:
+    """Split sizes and index maps of one exchange, for rank ``rank``.
 
-    ``counts_all[r, e]``: rows rank r routes to global expert e.  Received rows
-    arrive source-major (all of rank 0's rows for my experts, expert by expert,
-    then rank 1's, ...); the GEMM wants them expert-major with each expert's
-    segment starting on an ``align`` boundary, sources in rank order inside it.
+    ``counts_all[r, e]``: rows rank r routes to expert e (its compact permuted
+    rows are expert-major).  ``placement.slots[d]`` lists the experts rank d
+    computes; ``quota[e, d]`` how many of expert e's rows rank d takes (default:
+    every expert's rows go to its only holder).  An expert's rows are enumerated
+    source-major, and holders (by ascending rank) take consecutive runs.
+    Rank r sends, to each destination d in turn, its runs for d's slots in d's
+    slot order; rank d receives source-major, slot-minor, and regroups them
+    slot-major with each slot's segment starting on an ``align`` boundary.
     """
-    counts_all = np.asarray(counts_all, dtype=np.int64)
-    R = counts_all.shape[0]
-    s, e = shards[rank]
-    send = [int(counts_all[rank, a:b].sum()) for a, b in shards]
-    c = counts_all[:, s:e]                       # [R, E_local]
-    recv = [int(x) for x in c.sum(axis=1)]
-    El = e - s
-    local_counts = c.sum(axis=0) if El else np.zeros(0, dtype=np.int64)
+    cnt = np.asarray(counts_all, dtype=np.int64)
+    R, E = cnt.shape
+    holders = placement.holders(E)
+    if quota is None:
+        quota = np.zeros((E, R), dtype=np.int64)
+        for e in range(E):
+            if len(holders[e]) != 1:
+                raise ValueError("replicated experts need an explicit quota")
+            quota[e, holders[e][0]] = cnt[:, e].sum()
+    # run of expert e on holder h covers global rows [lo[e,h], hi[e,h])
+    lo = np.zeros((E, R), dtype=np.int64)
+    hi = np.zeros((E, R), dtype=np.int64)
+    for e in range(E):
+        acc = 0
+        for h in sorted(holders[e]):
+            lo[e, h] = acc
+            acc += quota[e, h]
+            hi[e, h] = acc
+    src_base = np.cumsum(cnt, axis=0) - cnt          # [R, E] first global row of (r, e)
+
+    def piece(r, e, h):
+        """(offset inside r's segment of e, length) of the run r sends h for e."""
+        a = max(lo[e, h], src_base[r, e])
+        b = min(hi[e, h], src_base[r, e] + cnt[r, e])
+        return (int(a - src_base[r, e]), int(max(0, b - a)))
+
+    seg_start = np.cumsum(cnt[rank]) - cnt[rank]     # my compact segment starts
+    send_splits, send_parts, identity = [], [], True
+    pos = 0
+    for d in range(R):
+        n_d = 0
+        for e in placement.slots[d]:
+            off, ln = piece(rank, e, d)
+            if ln:
+                start = int(seg_start[e]) + off
+                send_parts.append((start, ln))
+                identity = identity and start == pos
+                pos += ln
+                n_d += ln
+        send_splits.append(n_d)
+    send_index = None
+    if not identity:
+        send_index = (np.concatenate([np.arange(a, a + n) for a, n in send_parts]).astype(np.int32)
+                      if send_parts else np.zeros(0, dtype=np.int32))
+    my = placement.slots[rank]
+    c = np.array([[piece(r, e, rank)[1] for e in my] for r in range(R)], dtype=np.int64).reshape(R, len(my))
+    recv_splits = [int(x) for x in c.sum(axis=1)]
+    local_counts = c.sum(axis=0) if my else np.zeros(0, dtype=np.int64)
     padded = (local_counts + align - 1) // align * align
     local_offsets = np.concatenate([[0], np.cumsum(padded)]).astype(np.int64)
     total = int(c.sum())
-    rows_cap = int(local_offsets[-1]) if El else 0
-    sizes = c.reshape(-1)                        # blocks in receive order (r-major, expert-minor)
+    rows_cap = int(local_offsets[-1]) if my else 0
+    sizes = c.reshape(-1)                            # receive order: source-major, slot-minor
     recv_block_start = np.concatenate([[0], np.cumsum(sizes)[:-1]]) if sizes.size else sizes
     dst_block_start = (local_offsets[:-1][None, :] + np.cumsum(c, axis=0) - c).reshape(-1)
     blk = np.repeat(np.arange(sizes.size), sizes)
@@ -111,7 +157,15 @@ def plan_dispatch(counts_all: np.ndarray, rank: int, shards: Sequence[Tuple[int,
     inverse = (dst_block_start[blk] + within).astype(np.int32)
     gather = np.full(max(rows_cap, 1), -1, dtype=np.int32)
     gather[inverse] = np.arange(total, dtype=np.int32)
-    return DispatchPlan(send, recv, local_counts, local_offsets, rows_cap, gather, inverse)
+    return DispatchPlan(send_splits, recv_splits, local_counts, local_offsets, rows_cap, gather, inverse,
+                        send_index)
+
+
+def plan_dispatch(counts_all: np.ndarray, rank: int, shards: Sequence[Tuple[int, int]],
+                  align: int = K.ALIGN) -> DispatchPlan:
+    """Exchange plan for plain contiguous sharding (each expert on one rank)."""
+    placement = Placement(tuple(tuple(range(a, b)) for a, b in shards))
+    return plan_exchange(counts_all, rank, placement, None, align)
 
 
 class EPFusedMoE(nn.Module):
@@ -157,6 +211,10 @@ class EPFusedMoE(nn.Module):
         self._shared_gate: Optional[torch.Tensor] = None
         self._bank_cache = None
         self.last_plan: Optional[DispatchPlan] = None
+        self.last_counts: Optional[np.ndarray] = None   # [R, E] rows routed last step
+        # experts held per rank: the contiguous shard, plus replicas after rebalance()
+        self.placement = Placement(tuple(tuple(range(a, b)) for a, b in self.shards))
+        self._slot_bank: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
 
     # --------------------------------------------------------------- build
     @classmethod
@@ -189,7 +247,71 @@ class EPFusedMoE(nn.Module):
 
     def _apply(self, fn, recurse=True):
         self._bank_cache = None
+        if self._slot_bank is not None:
+            self._slot_bank = tuple(fn(b) for b in self._slot_bank)
+            for j, p in enumerate(self.experts_w1):
+                p.data = self._slot_bank[0][j]
+            for j, p in enumerate(self.experts_w2):
+                p.data = self._slot_bank[1][j]
         return super()._apply(fn, recurse)
+
+    @property
+    def num_replicas(self) -> int:
+        return len(self.placement.slots[self.ep_rank]) - self.local_count
+
+    def _gemm_banks(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Weights of every local slot: primaries first, then replicas."""
+        return self._slot_bank if self.num_replicas else self._banks()
+
+    def rebalance(self, load: Optional[Sequence[float]] = None, redundant: int = 1) -> Placement:
+        """Give every rank ``redundant`` replica slots of the busiest experts.
+
+        ``load`` (per-expert rows, identical on every rank) defaults to the
+        global counts of the last forward.  Collective: every rank must call it.
+        Replica weights come from each expert's primary owner over NCCL/gloo
+        point-to-point; afterwards each step splits an expert's rows among its
+        holders so that the ranks' row counts even out.
+        """
+        if load is None:
+            if self.last_counts is None:
+                raise RuntimeError("rebalance() needs a load estimate or a previous forward")
+            load = self.last_counts.sum(axis=0)
+        placement = place_experts(load, self.shards, redundant)
+        R, me, n = self.ep_size, self.ep_rank, self.local_count
+        owner = np.zeros(self.num_experts, dtype=np.int64)
+        for r, (a, b) in enumerate(self.shards):
+            owner[a:b] = r
+        w1b, w2b = self._banks()
+        mine = placement.slots[me]
+        dev = self.gate.device
+        nw1 = torch.empty((len(mine),) + tuple(w1b.shape[1:]), dtype=w1b.dtype, device=dev)
+        nw2 = torch.empty((len(mine),) + tuple(w2b.shape[1:]), dtype=w2b.dtype, device=dev)
+        with torch.no_grad():
+            nw1[:n].copy_(w1b)
+            nw2[:n].copy_(w2b)
+        ops = []
+        for d in range(R):
+            nd = self.shards[d][1] - self.shards[d][0]
+            for j, e in enumerate(placement.slots[d][nd:]):
+                o = int(owner[e])
+                if o == me:
+                    loc = e - self.local_start
+                    ops += [tdist.P2POp(tdist.isend, w1b[loc].contiguous(), d, group=self._pg()),
+                            tdist.P2POp(tdist.isend, w2b[loc].contiguous(), d, group=self._pg())]
+                if d == me:
+                    ops += [tdist.P2POp(tdist.irecv, nw1[n + j], o, group=self._pg()),
+                            tdist.P2POp(tdist.irecv, nw2[n + j], o, group=self._pg())]
+        if ops:
+            for req in tdist.batch_isend_irecv(ops):
+                req.wait()
+        for j, p in enumerate(self.experts_w1):
+            p.data = nw1[j]
+        for j, p in enumerate(self.experts_w2):
+            p.data = nw2[j]
+        self._slot_bank = (nw1, nw2)
+        self._bank_cache = None
+        self.placement = placement
+        return placement
 
     def _banks(self) -> Tuple[torch.Tensor, torch.Tensor]:
         if self._bank_cache is None:
@@ -259,30 +381,44 @@ class EPFusedMoE(nn.Module):
             counts = p.counts
         else:
             counts = torch.zeros(E, dtype=torch.int32, device=dev)
-        # (2) counts exchange
+        # (2) counts exchange -> the same plan on every rank
         gathered = [torch.empty_like(counts) for _ in range(self.ep_size)]
         tdist.all_gather(gathered, counts, group=pg)
         cnt = torch.stack(gathered).cpu().numpy()
-        plan = plan_dispatch(cnt, self.ep_rank, self.shards)
+        self.last_counts = cnt
+        quota = split_rows(cnt, self.placement) if any(
+            len(s) > b - a for s, (a, b) in zip(self.placement.slots, self.shards)) else None
+        plan = plan_exchange(cnt, self.ep_rank, self.placement, quota)
         self.last_plan = plan
-        # (3) dispatch
-        send_rows = p.x_perm[:T * Kk] if T > 0 else torch.empty(0, H, dtype=x2.dtype, device=dev)
+        # one pinned host buffer -> one copy for every index map of this step
+        parts = [plan.gather_index, plan.inverse_index, plan.local_offsets.astype(np.int32),
+                 plan.local_counts.astype(np.int32)]
+        if plan.send_index is not None:
+            pos_of_row = np.empty(T * Kk, dtype=np.int32)
+            pos_of_row[plan.send_index] = np.arange(T * Kk, dtype=np.int32)
+            parts += [plan.send_index, pos_of_row]
+        sizes = [a.size for a in parts]
+        dev_ix = torch.from_numpy(np.concatenate(parts).astype(np.int32)).pin_memory().to(dev, non_blocking=True)
+        views, o = [], 0
+        for s in sizes:
+            views.append(dev_ix[o:o + s])
+            o += s
+        gidx, inv, off, lc = views[:4]
+        # (3) dispatch (rows reordered by destination only when replicas split an expert)
+        if T == 0:
+            send_rows = torch.empty(0, H, dtype=x2.dtype, device=dev)
+        elif plan.send_index is None:
+            send_rows = p.x_perm[:T * Kk]
+        else:
+            send_rows = K.gather_rows(p.x_perm, views[4], torch.empty(T * Kk, H, dtype=x2.dtype, device=dev))
         recv = torch.empty(plan.recv_total, H, dtype=x2.dtype, device=dev)
         _dist.all_to_all_v(recv, send_rows, plan.recv_splits, plan.send_splits, group=pg)
-        # (4) regroup + expert GEMMs
+        # (4) regroup by local slot + expert GEMMs
         y_send = torch.empty(plan.recv_total, H, dtype=x2.dtype, device=dev)
         if plan.recv_total > 0:
-            host = np.concatenate([plan.gather_index, plan.inverse_index,
-                                   plan.local_offsets.astype(np.int32), plan.local_counts.astype(np.int32)])
-            dev_ix = torch.from_numpy(host).pin_memory().to(dev, non_blocking=True)
-            nG = plan.gather_index.size
-            gidx = dev_ix[:nG]
-            inv = dev_ix[nG:nG + plan.recv_total]
-            off = dev_ix[nG + plan.recv_total:nG + plan.recv_total + self.local_count + 1]
-            lc = dev_ix[nG + plan.recv_total + self.local_count + 1:]
             xl = torch.empty(plan.rows_capacity, H, dtype=x2.dtype, device=dev)
             K.gather_rows(recv, gidx, xl)
-            w1b, w2b = self._banks()
+            w1b, w2b = self._gemm_banks()
             h = torch.empty(plan.rows_capacity, I, dtype=x2.dtype, device=dev)
             K.grouped_gemm_gated(xl, w1b, off, lc, h, activation=self.activation)
             y = torch.empty(plan.rows_capacity, H, dtype=x2.dtype, device=dev)
@@ -294,6 +430,8 @@ class EPFusedMoE(nn.Module):
         out = torch.empty(T, H, dtype=x2.dtype, device=dev)
         if T == 0:
             return out
+        if plan.send_index is not None:  # back to the expert-major permuted order
+            y_back = K.gather_rows(y_back, views[5], torch.empty_like(y_back))
         shared_y = None
         if self._shared is not None:
             shared_y = K.dense_gated_mlp(x2, self._shared[0], self._shared[1], self.activation)

@@ -11,7 +11,8 @@ import torch
 
 from oracle import moe_oracle as O
 from reframework_b200.parallel import dist as D
-from reframework_b200.parallel.ep import plan_dispatch, shard_range
+from reframework_b200.parallel.ep import plan_dispatch, plan_exchange, shard_range
+from reframework_b200.parallel.eplb import place_experts, split_rows
 
 
 def _free_port():
@@ -65,10 +66,11 @@ def test_plan_with_more_ranks_than_experts():
     assert pl.send_splits == [5, 0, 0]
 
 
-def _exchange_worker(rank, ctx, E, T, Kk, seed):
+def _exchange_worker(rank, ctx, E, T, Kk, seed, redundant):
     torch.manual_seed(seed + rank)
     H = 16
     ids = torch.randint(0, E, (T, Kk), dtype=torch.int64)
+    ids[: T // 2, 0] = 0  # skew: expert 0 is hot on every rank
     x = torch.randn(T, H)
     counts, order = O.permutation(ids.numpy(), E)
     x_perm = x[torch.from_numpy(order // Kk)]
@@ -77,30 +79,62 @@ def _exchange_worker(rank, ctx, E, T, Kk, seed):
     shards = [shard_range(E, R, r) for r in range(R)]
     gathered = D.all_gather(torch.from_numpy(counts).int())
     cnt = torch.stack(gathered).numpy()
-    plan = plan_dispatch(cnt, rank, shards)
+    placement = place_experts(cnt.sum(0), shards, redundant)
+    quota = split_rows(cnt, placement) if redundant else None
+    plan = plan_exchange(cnt, rank, placement, quota)
+    send = x_perm if plan.send_index is None else x_perm[torch.from_numpy(plan.send_index).long()]
     recv = torch.empty(plan.recv_total, H)
-    D.all_to_all_v(recv, x_perm, plan.recv_splits, plan.send_splits)
-    # stand-in expert compute on the regrouped rows: y = x * (1 + global expert)
+    D.all_to_all_v(recv, send, plan.recv_splits, plan.send_splits)
+    # stand-in expert compute on the regrouped rows: y = x * (1 + global expert of the slot)
     gi = torch.from_numpy(plan.gather_index[:plan.rows_capacity]).long()
     xl = torch.where((gi >= 0).unsqueeze(1), recv[gi.clamp_min(0)] if plan.recv_total else torch.zeros(gi.numel(), H),
                      torch.zeros(1, H))
-    s, _ = shards[rank]
     y = torch.zeros_like(xl)
-    for j in range(len(plan.local_counts)):
+    for j, e in enumerate(placement.slots[rank]):
         lo = int(plan.local_offsets[j])
         n = int(plan.local_counts[j])
-        y[lo:lo + n] = xl[lo:lo + n] * (1 + s + j)
+        y[lo:lo + n] = xl[lo:lo + n] * (1 + e)
     y_send = y[torch.from_numpy(plan.inverse_index).long()] if plan.recv_total else torch.empty(0, H)
     y_back = torch.empty(T * Kk, H)
     D.all_to_all_v(y_back, y_send, plan.send_splits, plan.recv_splits)
+    if plan.send_index is not None:
+        y_perm = torch.empty_like(y_back)
+        y_perm[torch.from_numpy(plan.send_index).long()] = y_back
+        y_back = y_perm
     expect = x_perm * (1 + expert_of_row.float()).unsqueeze(1)
     assert torch.equal(y_back, expect), f"rank {rank}: rows did not come back to their slots"
+    if redundant:
+        # every rank's computed row count is within one expert-run of the mean
+        loads = quota.sum(axis=0)
+        assert loads.max() - loads.min() <= max(2, cnt.sum() // 4)
 
 
-@pytest.mark.parametrize("E,T,Kk", [(8, 40, 2), (5, 33, 3), (1, 7, 1)])
-def test_ep_exchange_gloo_world2(E, T, Kk):
+@pytest.mark.parametrize("E,T,Kk,redundant", [(8, 40, 2, 0), (5, 33, 3, 0), (1, 7, 1, 0), (8, 64, 2, 1),
+                                              (4, 50, 2, 2)])
+def test_ep_exchange_gloo_world2(E, T, Kk, redundant):
     D.run(_exchange_worker, world_size=2, backend="gloo",
-          init_method=f"tcp://127.0.0.1:{_free_port()}", ep_size=2, args=(E, T, Kk, 3))
+          init_method=f"tcp://127.0.0.1:{_free_port()}", ep_size=2, args=(E, T, Kk, 3, redundant))
+
+
+def test_place_experts_and_split_rows_balance():
+    """On the C2-like skew over 8 ranks, 2 replica slots per rank bring the
+    busiest rank within ~15 % of the mean (contiguous sharding alone: 2.3x)."""
+    load = np.array([1041, 959, 1817, 1128, 2319, 518, 149, 261]) * 8
+    R = 8
+    shards = [shard_range(8, R, r) for r in range(R)]
+    base = load.max() / (load.sum() / R)
+    assert base > 2.0
+    pl = place_experts(load, shards, redundant=2)
+    assert all(len(set(s)) == len(s) for s in pl.slots)
+    assert all(s[0] == shards[r][0] for r, s in enumerate(pl.slots))  # primaries first
+    cnt = np.tile(load // R, (R, 1))
+    q = split_rows(cnt, pl)
+    assert np.array_equal(q.sum(axis=1), cnt.sum(axis=0))  # every row assigned once
+    holders = pl.holders(8)
+    for e in range(8):
+        assert all(q[e, h] == 0 for h in range(R) if h not in holders[e])
+    ratio = q.sum(axis=0).max() / (cnt.sum() / R)
+    assert ratio < 1.15, ratio
 
 
 def _ctx_worker(rank, ctx):

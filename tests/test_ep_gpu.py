@@ -98,6 +98,15 @@ with torch.no_grad():
 assert torch.equal(shard, ref[lo:hi]), "token-sharded rows differ from the single-process layer"
 assert torch.equal(rep, ref), "replicated-contract output differs"
 assert max_rel(rep, rec["out"]) < 1e-2
+# redundant experts: replica weights fetched from their owners, rows of an
+# expert split across its holders; the result must not change by a bit
+ep = EPFusedMoE.from_full(full, world, rank, token_sharded=True)
+with torch.no_grad():
+    ep(x[lo:hi])
+    pl = ep.rebalance(redundant=2)
+    assert ep.num_replicas >= 1
+    bal = ep(x[lo:hi])
+assert torch.equal(bal, ref[lo:hi]), "rebalanced EP output differs"
 D.barrier()
 D.destroy()
 print("rank", rank, "ok")

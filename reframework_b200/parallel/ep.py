@@ -31,6 +31,7 @@ per token it is bit-identical to the single-process ``FusedMoE``.
 
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -99,50 +100,37 @@ def plan_exchange(counts_all: np.ndarray, rank: int, placement: Placement,
     """
     cnt = np.asarray(counts_all, dtype=np.int64)
     R, E = cnt.shape
-    holders = placement.holders(E)
     if quota is None:
         quota = np.zeros((E, R), dtype=np.int64)
-        for e in range(E):
-            if len(holders[e]) != 1:
-                raise ValueError("replicated experts need an explicit quota")
-            quota[e, holders[e][0]] = cnt[:, e].sum()
-    # run of expert e on holder h covers global rows [lo[e,h], hi[e,h])
-    lo = np.zeros((E, R), dtype=np.int64)
-    hi = np.zeros((E, R), dtype=np.int64)
-    for e in range(E):
-        acc = 0
-        for h in sorted(holders[e]):
-            lo[e, h] = acc
-            acc += quota[e, h]
-            hi[e, h] = acc
-    src_base = np.cumsum(cnt, axis=0) - cnt          # [R, E] first global row of (r, e)
-
-    def piece(r, e, h):
-        """(offset inside r's segment of e, length) of the run r sends h for e."""
-        a = max(lo[e, h], src_base[r, e])
-        b = min(hi[e, h], src_base[r, e] + cnt[r, e])
-        return (int(a - src_base[r, e]), int(max(0, b - a)))
-
-    seg_start = np.cumsum(cnt[rank]) - cnt[rank]     # my compact segment starts
-    send_splits, send_parts, identity = [], [], True
-    pos = 0
-    for d in range(R):
-        n_d = 0
-        for e in placement.slots[d]:
-            off, ln = piece(rank, e, d)
-            if ln:
-                start = int(seg_start[e]) + off
-                send_parts.append((start, ln))
-                identity = identity and start == pos
-                pos += ln
-                n_d += ln
-        send_splits.append(n_d)
+        for r, ss in enumerate(placement.slots):
+            quota[list(ss), r] = cnt[:, list(ss)].sum(axis=0)
+        if np.any(quota.sum(axis=1) != cnt.sum(axis=0)):
+            raise ValueError("replicated experts need an explicit quota")
+    quota = np.asarray(quota, dtype=np.int64)
+    # expert e's holders take consecutive runs in rank order: holder h covers
+    # global rows [lo[e,h], lo[e,h] + quota[e,h]) (empty for non-holders)
+    lo = np.cumsum(quota, axis=1) - quota             # [E, R]
+    hi = lo + quota
+    src_base = (np.cumsum(cnt, axis=0) - cnt).T       # [E, R] first global row of source r's rows of e
+    src_end = src_base + cnt.T
+    # run length / offset of expert e's rows that source r sends holder h: [E, R(src), R(holder)]
+    a = np.maximum(lo[:, None, :], src_base[:, :, None])
+    b = np.minimum(hi[:, None, :], src_end[:, :, None])
+    length = np.maximum(0, b - a)
+    offset = a - src_base[:, :, None]
+    seg_start = np.cumsum(cnt[rank]) - cnt[rank]      # my compact segment starts
+    slot_e = [np.asarray(ss, dtype=np.int64) for ss in placement.slots]
+    starts = np.concatenate([seg_start[ss] + offset[ss, rank, d] for d, ss in enumerate(slot_e)])
+    lens = np.concatenate([length[ss, rank, d] for d, ss in enumerate(slot_e)])
+    send_splits = [int(length[ss, rank, d].sum()) for d, ss in enumerate(slot_e)]
+    keep = lens > 0
+    starts, lens = starts[keep], lens[keep]
+    pos = np.cumsum(lens) - lens
     send_index = None
-    if not identity:
-        send_index = (np.concatenate([np.arange(a, a + n) for a, n in send_parts]).astype(np.int32)
-                      if send_parts else np.zeros(0, dtype=np.int32))
+    if np.any(starts != pos):
+        send_index = (np.repeat(starts - pos, lens) + np.arange(int(lens.sum()))).astype(np.int32)
     my = placement.slots[rank]
-    c = np.array([[piece(r, e, rank)[1] for e in my] for r in range(R)], dtype=np.int64).reshape(R, len(my))
+    c = length[slot_e[rank], :, rank].T.reshape(R, len(my))  # [R(src), slots]
     recv_splits = [int(x) for x in c.sum(axis=1)]
     local_counts = c.sum(axis=0) if my else np.zeros(0, dtype=np.int64)
     padded = (local_counts + align - 1) // align * align
@@ -215,6 +203,10 @@ class EPFusedMoE(nn.Module):
         # experts held per rank: the contiguous shard, plus replicas after rebalance()
         self.placement = Placement(tuple(tuple(range(a, b)) for a, b in self.shards))
         self._slot_bank: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
+        # set to [] to record per-phase CUDA events / host times (see phase_times)
+        self.trace: Optional[list] = None
+        self._pin_ring = [[None, None] for _ in range(3)]
+        self._pin_next = 0
 
     # --------------------------------------------------------------- build
     @classmethod
@@ -366,6 +358,38 @@ class EPFusedMoE(nn.Module):
             pieces.append(outs[r][:hi - lo])
         return torch.cat(pieces, 0)
 
+    def _stage(self, host: np.ndarray, dev: torch.device) -> torch.Tensor:
+        """Copy an int32 host array to the device through a ring of reusable
+        pinned buffers (no pinned allocation per step); a buffer is refilled
+        only after the copy that last read it has completed."""
+        n = int(host.size)
+        ring = self._pin_ring
+        slot = ring[self._pin_next % len(ring)]
+        self._pin_next += 1
+        if slot[1] is not None:
+            slot[1].synchronize()
+        if slot[0] is None or slot[0].numel() < n:
+            slot[0] = torch.empty(max(n, 1 << 16), dtype=torch.int32).pin_memory()
+        slot[0][:n].numpy()[:] = host
+        out = torch.empty(n, dtype=torch.int32, device=dev)
+        out.copy_(slot[0][:n], non_blocking=True)
+        slot[1] = torch.cuda.Event()
+        slot[1].record()
+        return out
+
+    def _mark(self, name: str) -> None:
+        """Record a phase boundary (CUDA event + host time) when tracing is on."""
+        if self.trace is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.trace.append((name, ev, time.perf_counter()))
+
+    def phase_times(self) -> Dict[str, Tuple[float, float]]:
+        """Per-phase (device ms, host ms) of the last traced forward."""
+        tr = self.trace or []
+        torch.cuda.synchronize()
+        return {b[0]: (a[1].elapsed_time(b[1]), 1e3 * (b[2] - a[2])) for a, b in zip(tr, tr[1:])}
+
     def _forward_shard(self, x2: torch.Tensor, res2: Optional[torch.Tensor]) -> torch.Tensor:
         dev = x2.device
         T, H = x2.shape
@@ -373,6 +397,9 @@ class EPFusedMoE(nn.Module):
         ek = self.entropy_k_min if self.entropy_adaptive_k else 0
         rdt = None if (self.router_dtype == torch.float32 or self.dtype == torch.float32) else self.dtype
         pg = self._pg()
+        if self.trace is not None:
+            self.trace = []
+        self._mark("start")
         if T > 0:
             w, ids32, _, _, sscale = K.router_topk(x2, self.gate.detach(), Kk, renormalize=self.renormalize,
                                                    bias=self.router_bias, round_dtype=rdt, entropy_k_min=ek,
@@ -381,11 +408,14 @@ class EPFusedMoE(nn.Module):
             counts = p.counts
         else:
             counts = torch.zeros(E, dtype=torch.int32, device=dev)
+        self._mark("route+permute")
         # (2) counts exchange -> the same plan on every rank
         gathered = [torch.empty_like(counts) for _ in range(self.ep_size)]
         tdist.all_gather(gathered, counts, group=pg)
+        self._mark("counts all_gather")
         cnt = torch.stack(gathered).cpu().numpy()
         self.last_counts = cnt
+        self._mark("counts to host")
         quota = split_rows(cnt, self.placement) if any(
             len(s) > b - a for s, (a, b) in zip(self.placement.slots, self.shards)) else None
         plan = plan_exchange(cnt, self.ep_rank, self.placement, quota)
@@ -398,12 +428,13 @@ class EPFusedMoE(nn.Module):
             pos_of_row[plan.send_index] = np.arange(T * Kk, dtype=np.int32)
             parts += [plan.send_index, pos_of_row]
         sizes = [a.size for a in parts]
-        dev_ix = torch.from_numpy(np.concatenate(parts).astype(np.int32)).pin_memory().to(dev, non_blocking=True)
+        dev_ix = self._stage(np.concatenate(parts), dev)
         views, o = [], 0
         for s in sizes:
             views.append(dev_ix[o:o + s])
             o += s
         gidx, inv, off, lc = views[:4]
+        self._mark("plan+index copy")
         # (3) dispatch (rows reordered by destination only when replicas split an expert)
         if T == 0:
             send_rows = torch.empty(0, H, dtype=x2.dtype, device=dev)
@@ -412,7 +443,9 @@ class EPFusedMoE(nn.Module):
         else:
             send_rows = K.gather_rows(p.x_perm, views[4], torch.empty(T * Kk, H, dtype=x2.dtype, device=dev))
         recv = torch.empty(plan.recv_total, H, dtype=x2.dtype, device=dev)
+        self._mark("send gather")
         _dist.all_to_all_v(recv, send_rows, plan.recv_splits, plan.send_splits, group=pg)
+        self._mark("dispatch all_to_all")
         # (4) regroup by local slot + expert GEMMs
         y_send = torch.empty(plan.recv_total, H, dtype=x2.dtype, device=dev)
         if plan.recv_total > 0:
@@ -420,13 +453,18 @@ class EPFusedMoE(nn.Module):
             K.gather_rows(recv, gidx, xl)
             w1b, w2b = self._gemm_banks()
             h = torch.empty(plan.rows_capacity, I, dtype=x2.dtype, device=dev)
+            self._mark("regroup gather")
             K.grouped_gemm_gated(xl, w1b, off, lc, h, activation=self.activation)
+            self._mark("gated GEMM")
             y = torch.empty(plan.rows_capacity, H, dtype=x2.dtype, device=dev)
             K.grouped_gemm_down(h, w2b, off, lc, y)
+            self._mark("down GEMM")
             K.gather_rows(y, inv, y_send)
+        self._mark("return gather")
         # (5) return trip + combine on the token's rank
         y_back = torch.empty(T * Kk, H, dtype=x2.dtype, device=dev)
         _dist.all_to_all_v(y_back, y_send, plan.send_splits, plan.recv_splits, group=pg)
+        self._mark("combine all_to_all")
         out = torch.empty(T, H, dtype=x2.dtype, device=dev)
         if T == 0:
             return out
@@ -435,8 +473,10 @@ class EPFusedMoE(nn.Module):
         shared_y = None
         if self._shared is not None:
             shared_y = K.dense_gated_mlp(x2, self._shared[0], self._shared[1], self.activation)
-        return K.combine(y_back, p.row_of_slot, w, out, shared_y=shared_y, shared_scale=sscale, residual=res2,
-                         precise=self.precise_combine)
+        out = K.combine(y_back, p.row_of_slot, w, out, shared_y=shared_y, shared_scale=sscale, residual=res2,
+                        precise=self.precise_combine)
+        self._mark("unpermute+shared+combine")
+        return out
 
     # ------------------------------------------------------------- (de)serial
     def state_dict(self, *args, prefix: str = "", result: Optional[dict] = None, **kwargs) -> Dict[str, torch.Tensor]:

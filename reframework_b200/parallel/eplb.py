@@ -64,7 +64,7 @@ def _waterfill(n: int, base: List[int]) -> List[int]:
     return out
 
 
-def split_rows(counts_all: np.ndarray, placement: Placement, rounds: int = 16) -> np.ndarray:
+def split_rows(counts_all: np.ndarray, placement: Placement, rounds: int = 4) -> np.ndarray:
     """Rows of each expert assigned to each holder, balancing rows per rank.
 
     ``counts_all[r, e]`` = rows rank r routes to expert e this step.  Returns

@@ -104,7 +104,7 @@ ep = EPFusedMoE.from_full(full, world, rank, token_sharded=True)
 with torch.no_grad():
     ep(x[lo:hi])
     pl = ep.rebalance(redundant=2)
-    assert ep.num_replicas >= 1
+    assert sum(len(s) for s in pl.slots) > cfg.experts  # at least one replica somewhere
     bal = ep(x[lo:hi])
 assert torch.equal(bal, ref[lo:hi]), "rebalanced EP output differs"
 D.barrier()

@@ -55,61 +55,83 @@ def committed_traffic():
     return {}
 
 
+_SAMPLER = r"""
+import sys, time, signal, pynvml
+out, gpus = sys.argv[1], [int(g) for g in sys.argv[2].split(",")]
+pynvml.nvmlInit()
+hs = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in gpus]
+mx = max(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM) for h in hs)
+stop = []
+signal.signal(signal.SIGTERM, lambda *a: stop.append(1))
+with open(out, "w") as f:
+    f.write("max,%d\n" % mx); f.flush()
+    while not stop:
+        for i, h in zip(gpus, hs):
+            try:
+                f.write("%.4f,%d,%d,%d\n" % (time.time(), i, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                             pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            except pynvml.NVMLError:
+                pass
+        time.sleep(0.002)
+"""
+
+
 class Clocks:
-    """SM clock and clock-event reasons sampled through NVML (read-only) every
-    2 ms on a background thread while the timed region runs."""
+    """SM clock and clock-event reasons read through NVML (read-only, nothing
+    is set) every 2 ms by a separate sampler process while the timed region
+    runs, so the sampling never competes with the benchmark's own host work."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
                "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, gpus, path=None):
         self.gpus = list(gpus)
-        self.path = path
-        self.samples = []
-        self._stop = None
-        self._thread = None
+        self.path = path or f"/tmp/rf_clocks_{os.getpid()}.csv"
+        self.proc = None
 
     def start(self):
-        import threading
+        import subprocess
         try:
-            import pynvml
-            pynvml.nvmlInit()
-            handles = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in self.gpus]
-            self.max_mhz = max(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM) for h in handles)
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, self.path,
+                                          ",".join(str(g) for g in self.gpus)],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except Exception:
+            self.proc = None
             return
-        self._stop = threading.Event()
-
-        def loop():
-            while not self._stop.is_set():
-                for i, h in zip(self.gpus, handles):
-                    try:
-                        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
-                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-                    except Exception:
-                        continue
-                    self.samples.append((time.time(), i, sm, rs))
-                time.sleep(0.002)
-
-        self._thread = threading.Thread(target=loop, daemon=True)
-        self._thread.start()
+        t_end = time.time() + 20
+        while time.time() < t_end:  # wait until the sampler is producing samples
+            try:
+                if sum(1 for _ in open(self.path)) > 2:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.02)
 
     def stop(self):
-        if self._thread is None:
+        if self.proc is None:
             return None
-        self._stop.set()
-        self._thread.join()
-        if self.path:
-            with open(self.path, "w") as f:
-                for s in self.samples:
-                    f.write("%.4f,%d,%d,0x%x\n" % s)
-        if not self.samples:
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=10)
+        except Exception:
+            self.proc.kill()
+        mx, samples = None, []
+        try:
+            for line in open(self.path):
+                p = line.strip().split(",")
+                if p[0] == "max":
+                    mx = float(p[1])
+                elif len(p) == 4:
+                    samples.append((float(p[0]), int(p[1]), float(p[2]), int(p[3])))
+        except OSError:
             return None
-        sm = [s[2] for s in self.samples]
-        loaded = [v for v in sm if v > 0.5 * self.max_mhz] or sm
-        reasons = sorted(n for n, bit in self.REASONS.items() if any(s[3] & bit for s in self.samples))
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(self.samples), "source": "NVML, 2 ms"}
+        if not samples or mx is None:
+            return None
+        sm = [s[2] for s in samples]
+        loaded = [v for v in sm if v > 0.5 * mx] or sm
+        reasons = sorted(n for n, bit in self.REASONS.items() if any(s[3] & bit for s in samples))
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(samples), "source": "NVML in a sampler process, 2 ms"}
 
 
 # ------------------------------------------------------------------- GPU arm
@@ -246,11 +268,11 @@ def run_gpu(args):
                 stage_fn(layer, x, [torch.cuda.Event(enable_timing=True) for _ in range(nev)])
             else:
                 fwd(x)
-        barrier()
         clocks = Clocks(range(world), os.path.join(ROOT, "gpurun_out", "clocks_bench.csv")
                         if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else None)
         if rank == 0:
-            clocks.start()
+            clocks.start()  # before the barrier: no rank may start timing while rank 0 sets up sampling
+        barrier()
         step_ms, stage_ms = [], []
         for _ in range(args.steps):
             flush.zero_()
@@ -293,6 +315,7 @@ def run_gpu(args):
     res = {
         "metric": METRIC, "value": tokens / (ms / 1e3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "step_ms_rank0": {"min": min(step_ms), "median": statistics.median(step_ms), "max": max(step_ms)},
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
         "config": {"workload": cfg.name, "hidden": cfg.hidden, "experts": cfg.experts, "top_k": cfg.top_k,
                    "inter": cfg.inter, "tokens_per_gpu": T, "global_tokens": tokens,

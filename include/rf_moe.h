@@ -211,6 +211,33 @@ int rf_moe_grouped_gemm_down(const void *h, const void *w2, void *y,
                              int64_t E, int64_t num_slots, int64_t rows_capacity,
                              int64_t H, int64_t I, int dtype, rf_stream_t stream);
 
+/*
+ * Expert-parallel exchange plan for one rank (host function, no GPU work).
+ * Replaces the reference's replicate-and-all-reduce combine
+ * (reframework/parallel/ep.py:120-150) with a token all-to-all; this computes
+ * that all-to-all's bookkeeping.
+ *   counts       [R, E] rows each rank routes to each expert this step
+ *   slot_experts experts held per rank, rank r's at
+ *                [slot_offsets[r], slot_offsets[r+1]) (primaries, then replicas)
+ * Replicated experts' rows are split over their holders by water-filling
+ * (`rounds` passes) so the ranks' row counts even out; holders take
+ * consecutive runs of an expert's rows in rank order.
+ * Outputs: send_splits[R], recv_splits[R] (rows), and in `packed` (int32):
+ *   gather_index  GEMM row -> received row (-1 on pad rows), slot segments
+ *                 aligned to `align`
+ *   inverse_index received row -> GEMM row
+ *   local_offsets [S+1], local_counts [S] of this rank's S slots
+ *   send_index    send position -> permuted row, and pos_of_row (its
+ *                 inverse) — both empty when the send order is the identity
+ * layout[15]: {off, len} of the six arrays at [0..11], then rows_capacity,
+ * send_is_identity, needed packed size.  Fails with RF_ERR_ARG (and fills
+ * layout) when packed_capacity is too small.
+ */
+int rf_moe_ep_plan(const int32_t *counts, int32_t R, int32_t E, int32_t rank,
+                   const int32_t *slot_experts, const int32_t *slot_offsets, int32_t align,
+                   int32_t rounds, int64_t *send_splits, int64_t *recv_splits,
+                   int32_t *packed, int64_t packed_capacity, int64_t *layout);
+
 /* Summation modes of rf_moe_combine. */
 #define RF_COMBINE_REFERENCE 0  /* the reference's rounding points and order */
 #define RF_COMBINE_FP32 1       /* fp32 accumulation, one rounding */

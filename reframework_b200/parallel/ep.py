@@ -41,7 +41,7 @@ import torch.distributed as tdist
 import torch.nn as nn
 
 from .. import kernels as K
-from .._lib import ACTIVATIONS, RfMoeError
+from .._lib import ACTIVATIONS, RfMoeError, check, lib
 from ..moe.moe_layer import FusedMoE, _bank_view
 from . import dist as _dist
 from .eplb import Placement, place_experts, split_rows
@@ -207,6 +207,9 @@ class EPFusedMoE(nn.Module):
         self.trace: Optional[list] = None
         self._pin_ring = [[None, None] for _ in range(3)]
         self._pin_next = 0
+        self._slot_arrays = None
+        self.split_rounds = 4         # water-filling passes of the per-step row split
+        self.native_planner = True    # False: the numpy planner (same result, slower)
 
     # --------------------------------------------------------------- build
     @classmethod
@@ -358,24 +361,55 @@ class EPFusedMoE(nn.Module):
             pieces.append(outs[r][:hi - lo])
         return torch.cat(pieces, 0)
 
-    def _stage(self, host: np.ndarray, dev: torch.device) -> torch.Tensor:
-        """Copy an int32 host array to the device through a ring of reusable
-        pinned buffers (no pinned allocation per step); a buffer is refilled
-        only after the copy that last read it has completed."""
-        n = int(host.size)
-        ring = self._pin_ring
-        slot = ring[self._pin_next % len(ring)]
+    def _pinned(self, n: int):
+        """A reusable pinned int32 host buffer of >= n words from a small ring;
+        a buffer is handed out again only after the copy that last read it has
+        completed (no pinned allocation per step)."""
+        slot = self._pin_ring[self._pin_next % len(self._pin_ring)]
         self._pin_next += 1
         if slot[1] is not None:
             slot[1].synchronize()
+            slot[1] = None
         if slot[0] is None or slot[0].numel() < n:
             slot[0] = torch.empty(max(n, 1 << 16), dtype=torch.int32).pin_memory()
-        slot[0][:n].numpy()[:] = host
+        return slot
+
+    def _upload(self, slot, n: int, dev: torch.device) -> torch.Tensor:
         out = torch.empty(n, dtype=torch.int32, device=dev)
         out.copy_(slot[0][:n], non_blocking=True)
         slot[1] = torch.cuda.Event()
         slot[1].record()
         return out
+
+    def _native_plan(self, cnt: np.ndarray, n_mine: int):
+        """Exchange plan from the native planner (rf_moe_ep_plan), written
+        straight into a pinned buffer.  Returns (plan, pinned slot, layout)."""
+        R, E = cnt.shape
+        cnt32 = np.ascontiguousarray(cnt, dtype=np.int32)
+        if self._slot_arrays is None or self._slot_arrays[0] is not self.placement:
+            flat = np.ascontiguousarray([e for s in self.placement.slots for e in s], dtype=np.int32)
+            offs = np.ascontiguousarray(np.cumsum([0] + [len(s) for s in self.placement.slots]), dtype=np.int32)
+            self._slot_arrays = (self.placement, flat, offs)
+        _, flat, offs = self._slot_arrays
+        S = len(self.placement.slots[self.ep_rank])
+        n_all = int(cnt32.sum())
+        cap = 2 * n_all + S * K.ALIGN + 2 * S + 2 * n_mine + 16
+        slot = self._pinned(cap)
+        send = np.zeros(R, dtype=np.int64)
+        recv = np.zeros(R, dtype=np.int64)
+        layout = np.zeros(15, dtype=np.int64)
+        rc = lib().rf_moe_ep_plan(cnt32.ctypes.data, R, E, self.ep_rank, flat.ctypes.data, offs.ctypes.data,
+                                  K.ALIGN, self.split_rounds, send.ctypes.data, recv.ctypes.data,
+                                  slot[0].data_ptr(), slot[0].numel(), layout.ctypes.data)
+        check(rc, "rf_moe_ep_plan")
+        host = slot[0].numpy()
+
+        def arr(i):
+            return host[layout[2 * i]:layout[2 * i] + layout[2 * i + 1]]
+        plan = DispatchPlan([int(v) for v in send], [int(v) for v in recv], arr(3).astype(np.int64),
+                            arr(2).astype(np.int64), int(layout[12]), arr(0), arr(1),
+                            None if layout[13] else arr(4))
+        return plan, slot, layout
 
     def _mark(self, name: str) -> None:
         """Record a phase boundary (CUDA event + host time) when tracing is on."""
@@ -416,23 +450,30 @@ class EPFusedMoE(nn.Module):
         cnt = torch.stack(gathered).cpu().numpy()
         self.last_counts = cnt
         self._mark("counts to host")
-        quota = split_rows(cnt, self.placement) if any(
-            len(s) > b - a for s, (a, b) in zip(self.placement.slots, self.shards)) else None
-        plan = plan_exchange(cnt, self.ep_rank, self.placement, quota)
+        if self.native_planner:
+            # native planner writes every index map into one pinned buffer -> one copy
+            plan, slot, lay = self._native_plan(cnt, T * Kk)
+            dev_ix = self._upload(slot, int(lay[14]), dev)
+            views = [dev_ix[lay[2 * i]:lay[2 * i] + lay[2 * i + 1]] for i in range(6)]
+        else:
+            quota = split_rows(cnt, self.placement, rounds=self.split_rounds) if any(
+                len(s) > b - a for s, (a, b) in zip(self.placement.slots, self.shards)) else None
+            plan = plan_exchange(cnt, self.ep_rank, self.placement, quota)
+            parts = [plan.gather_index, plan.inverse_index, plan.local_offsets.astype(np.int32),
+                     plan.local_counts.astype(np.int32)]
+            if plan.send_index is not None:
+                pos_of_row = np.empty(T * Kk, dtype=np.int32)
+                pos_of_row[plan.send_index] = np.arange(T * Kk, dtype=np.int32)
+                parts += [plan.send_index, pos_of_row]
+            host = np.concatenate(parts).astype(np.int32)
+            slot = self._pinned(host.size)
+            slot[0][:host.size].numpy()[:] = host
+            dev_ix = self._upload(slot, host.size, dev)
+            views, o = [], 0
+            for a in parts:
+                views.append(dev_ix[o:o + a.size])
+                o += a.size
         self.last_plan = plan
-        # one pinned host buffer -> one copy for every index map of this step
-        parts = [plan.gather_index, plan.inverse_index, plan.local_offsets.astype(np.int32),
-                 plan.local_counts.astype(np.int32)]
-        if plan.send_index is not None:
-            pos_of_row = np.empty(T * Kk, dtype=np.int32)
-            pos_of_row[plan.send_index] = np.arange(T * Kk, dtype=np.int32)
-            parts += [plan.send_index, pos_of_row]
-        sizes = [a.size for a in parts]
-        dev_ix = self._stage(np.concatenate(parts), dev)
-        views, o = [], 0
-        for s in sizes:
-            views.append(dev_ix[o:o + s])
-            o += s
         gidx, inv, off, lc = views[:4]
         self._mark("plan+index copy")
         # (3) dispatch (rows reordered by destination only when replicas split an expert)

@@ -116,6 +116,57 @@ def test_ep_exchange_gloo_world2(E, T, Kk, redundant):
           init_method=f"tcp://127.0.0.1:{_free_port()}", ep_size=2, args=(E, T, Kk, 3, redundant))
 
 
+@pytest.mark.parametrize("seed", range(12))
+def test_native_planner_matches_numpy_planner(seed):
+    """rf_moe_ep_plan (C++, in the library) == plan_exchange + split_rows (numpy)."""
+    import ctypes
+    from reframework_b200 import _lib
+    rng = np.random.default_rng(seed)
+    R = int(rng.integers(1, 9))
+    E = int(rng.integers(R, 3 * R + 3))
+    shards = [shard_range(E, R, r) for r in range(R)]
+    probs = rng.dirichlet(np.full(E, 0.5))
+    cnt = np.stack([rng.multinomial(int(rng.integers(0, 300)), probs) for _ in range(R)]).astype(np.int32)
+    redundant = int(rng.integers(0, 3))
+    pl = place_experts(cnt.sum(0) + 1, shards, redundant)
+    flat = np.ascontiguousarray([e for s in pl.slots for e in s], dtype=np.int32)
+    offs = np.ascontiguousarray(np.cumsum([0] + [len(s) for s in pl.slots]), dtype=np.int32)
+    for rank in range(R):
+        quota = split_rows(cnt, pl, rounds=4) if sum(len(s) for s in pl.slots) > E else None
+        ref = plan_exchange(cnt, rank, pl, quota)
+        send = np.zeros(R, np.int64)
+        recv = np.zeros(R, np.int64)
+        lay = np.zeros(15, np.int64)
+        buf = np.zeros(4 * int(cnt.sum()) + 2048, np.int32)
+        rc = _lib.lib().rf_moe_ep_plan(cnt.ctypes.data, R, E, rank, flat.ctypes.data, offs.ctypes.data, 128, 4,
+                                       send.ctypes.data, recv.ctypes.data, buf.ctypes.data, buf.size,
+                                       lay.ctypes.data)
+        assert rc == 0, _lib.lib().rf_moe_last_error()
+        seg = lambda i: buf[lay[2 * i]:lay[2 * i] + lay[2 * i + 1]]
+        assert list(send) == ref.send_splits and list(recv) == ref.recv_splits
+        assert lay[12] == ref.rows_capacity
+        assert np.array_equal(seg(0)[:max(ref.rows_capacity, 1)], ref.gather_index[:max(ref.rows_capacity, 1)])
+        assert np.array_equal(seg(1), ref.inverse_index)
+        assert np.array_equal(seg(2), ref.local_offsets) and np.array_equal(seg(3), ref.local_counts)
+        if ref.send_index is None:
+            assert lay[13] == 1
+        else:
+            assert lay[13] == 0 and np.array_equal(seg(4), ref.send_index)
+            assert np.array_equal(seg(5)[seg(4)], np.arange(seg(4).size))
+
+
+def test_native_planner_reports_small_buffer():
+    from reframework_b200 import _lib
+    cnt = np.array([[5, 3], [2, 7]], np.int32)
+    flat = np.array([0, 1], np.int32)
+    offs = np.array([0, 1, 2], np.int32)
+    send, recv, lay = np.zeros(2, np.int64), np.zeros(2, np.int64), np.zeros(15, np.int64)
+    buf = np.zeros(2, np.int32)
+    rc = _lib.lib().rf_moe_ep_plan(cnt.ctypes.data, 2, 2, 0, flat.ctypes.data, offs.ctypes.data, 128, 4,
+                                   send.ctypes.data, recv.ctypes.data, buf.ctypes.data, buf.size, lay.ctypes.data)
+    assert rc == 1 and lay[14] > 2 and "needs" in _lib.lib().rf_moe_last_error().decode()
+
+
 def test_place_experts_and_split_rows_balance():
     """On the C2-like skew over 8 ranks, 2 replica slots per rank bring the
     busiest rank within ~15 % of the mean (contiguous sharding alone: 2.3x)."""

@@ -185,25 +185,32 @@ class ExpertOffloadCache:
     def load(self, experts: Sequence[Dict[str, torch.Tensor]]) -> None:
         """Stage per-expert ``{"w1": [2I,H], "w2": [H,I]}`` in one pinned host buffer
         and allocate the device slot pool (offload_cache.py:304-347)."""
-        w1s = [e["w1"].detach().to("cpu", dtype=self.dtype).contiguous() for e in experts]
-        w2s = [e["w2"].detach().to("cpu", dtype=self.dtype).contiguous() for e in experts]
-        n1 = sum(w.numel() for w in w1s)
-        n2 = sum(w.numel() for w in w2s)
-        buf = torch.empty(n1 + n2, dtype=self.dtype)
-        if self._cuda:
-            buf, self._pinned = _pin(buf)
+        n1 = sum(e["w1"].numel() for e in experts)
+        n2 = sum(e["w2"].numel() for e in experts)
+        buf = None
+        if self._cuda and torch.cuda.is_available():
+            try:  # allocate the pool pinned directly (no pageable copy of every expert first)
+                buf = torch.empty(n1 + n2, dtype=self.dtype, pin_memory=True)
+                self._pinned = True
+            except RuntimeError:
+                buf = None
+        if buf is None:
+            buf = torch.empty(n1 + n2, dtype=self.dtype)
+            self._pinned = False
         self._host_buf = buf
         self._host = []
         off = 0
-        for w1, w2 in zip(w1s, w2s):
-            v1 = buf[off:off + w1.numel()].view_as(w1)
-            v1.copy_(w1)
+        for e in experts:
+            w1, w2 = e["w1"].detach(), e["w2"].detach()
+            v1 = buf[off:off + w1.numel()].view(tuple(w1.shape))
+            v1.copy_(w1.to(dtype=self.dtype))
             off += w1.numel()
-            v2 = buf[off:off + w2.numel()].view_as(w2)
-            v2.copy_(w2)
+            v2 = buf[off:off + w2.numel()].view(tuple(w2.shape))
+            v2.copy_(w2.to(dtype=self.dtype))
             off += w2.numel()
             self._host.append((v1, v2))
-        del w1s, w2s
+        if self._cuda and torch.cuda.is_available():
+            torch.cuda.synchronize(self.device)  # device-to-host copies into the pool are complete
         self._lru = OrderedDict()
         self.stats.reset()
         self._alloc_pool(max(1, int(self.lru_capacity)))

@@ -455,6 +455,93 @@ def run_reference(args):
     print(json.dumps(res))
 
 
+def run_generic(args):
+    """Other resident single-GPU workloads (C1 tiny fp32, C3 decode with a gated
+    shared expert, C4 with two shared experts): eager forward and CUDA-graph
+    replay, both timed with CUDA events, L2 flushed between steps."""
+    from reframework_b200.moe import FusedMoE
+    from reframework_b200.moe.graph import capture_forward
+    from reframework_b200.workloads import CONFIGS, generate
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = CONFIGS[args.config]
+    d = generate(cfg, device=str(dev), with_x=False)
+    moe = FusedMoE(cfg.experts, cfg.top_k, cfg.hidden, cfg.inter, dtype=cfg.dtype, renormalize=cfg.renormalize,
+                   router_dtype=torch.float32, num_shared_experts=cfg.shared_count,
+                   shared_intermediate_size=cfg.shared_inter, shared_expert_gate=cfg.shared_gate, device=dev)
+    with torch.no_grad():
+        moe.gate.copy_(d["gate"])
+        w1b, w2b = moe._resident_banks()
+        w1b.copy_(d["w1"])
+        w2b.copy_(d["w2"])
+        if cfg.shared_count:
+            moe.shared_w1.copy_(d["shared_w1"])
+            moe.shared_w2.copy_(d["shared_w2"])
+            if cfg.shared_gate:
+                moe.shared_gate.copy_(d["shared_gate"])
+    if d["bias"] is not None:
+        moe.set_router_bias(d["bias"][0])
+    del d
+    gx = torch.Generator(device=dev).manual_seed(cfg.seed + 101)
+    x = torch.randn(cfg.tokens, cfg.hidden, generator=gx, device=dev, dtype=cfg.dtype)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn(x)
+        torch.cuda.synchronize()
+        evs = []
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn(x)
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+    with torch.no_grad():
+        ms_eager = timed(moe)
+        graphed = capture_forward(moe, x)
+        clocks = Clocks([0])
+        clocks.start()
+        ms_graph = timed(graphed)
+        clk = clocks.stop()
+        _, ids = moe.route(x)
+    from reframework_b200 import _lib
+    if _lib.device_status() != 0:
+        raise RuntimeError("device error word set during the benchmark")
+    active = int((torch.bincount(ids.reshape(-1), minlength=cfg.experts) > 0).sum())
+    esz = torch.tensor([], dtype=cfg.dtype).element_size()
+    weight_bytes = active * 3 * cfg.hidden * cfg.inter * esz + \
+        cfg.shared_count * 3 * cfg.hidden * cfg.shared_inter * esz
+    act_bytes = cfg.tokens * cfg.hidden * esz * (2 + 2 * cfg.top_k)
+    bf16_peak, hbm_peak, src = peaks()
+    ms = ms_graph
+    hbm_ach = (weight_bytes + act_bytes) / (ms / 1e3) / 1e9
+    tf_ach = cfg.flops / (ms / 1e3) / 1e12
+    hbm_bound = (weight_bytes + act_bytes) / (hbm_peak * 1e9) > cfg.flops / (bf16_peak * 1e12)
+    res = {
+        "metric": f"MoE-layer tokens/s ({cfg.name})", "value": cfg.tokens / (ms / 1e3), "unit": UNIT,
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": str(cfg.dtype).replace("torch.", ""),
+        "data": "synthetic: seeded N(0,0.02) weights, N(0,1) activations, config router bias",
+        "config": {"workload": cfg.name, "hidden": cfg.hidden, "experts": cfg.experts, "top_k": cfg.top_k,
+                   "inter": cfg.inter, "tokens": cfg.tokens, "shared": [cfg.shared_count, cfg.shared_inter,
+                                                                          cfg.shared_gate],
+                   "active_experts": active, "l2": L2_NOTE.split(";")[0]},
+        "eager_ms_per_step": ms_eager, "graph_ms_per_step": ms_graph,
+        "roofline": ({"bound": "hbm", "achieved": hbm_ach, "peak": hbm_peak, "unit": "GB/s",
+                      "frac": hbm_ach / hbm_peak, "peak_source": src,
+                      "algorithmic_bytes": weight_bytes + act_bytes} if hbm_bound else
+                     {"bound": "tensor", "achieved": tf_ach, "peak": bf16_peak, "unit": "TFLOP/s",
+                      "frac": tf_ach / bf16_peak, "peak_source": src}),
+        "clocks": clk,
+    }
+    print(json.dumps(res))
+
+
 def run_offload(args):
     """Offload workload (C5): experts in pinned host memory, a few device slots.
 
@@ -541,6 +628,8 @@ def main():
         run_reference(args)
     elif args.config.startswith("c5"):
         run_offload(args)
+    elif args.config != "c2_mixtral_bf16" and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        run_generic(args)
     else:
         run_gpu(args)
 

@@ -278,7 +278,7 @@ class ExpertOffloadCache:
         if not (self._cuda and torch.cuda.is_available()):
             return None
         try:
-            n = 1 << 24  # 32 MB of 16-bit elements: long enough to reach steady state
+            n = 1 << 27  # 256 MB of 16-bit elements: long enough to reach the link's steady rate
             src, _ = _pin(torch.empty(n, dtype=self.dtype))
             dst = torch.empty(n, dtype=self.dtype, device=self.device)
             cs = self.copy_stream()

@@ -235,3 +235,23 @@ def test_forward_prefill_does_not_lookahead():
         mlp(x)
     assert list(mlp._predictor._history) == []
     assert cache.stats.predicts == 0
+
+
+@pytest.mark.parametrize("name", ["c3_mini_bf16", "c2_mini_bf16", "c1_tiny_fp32"])
+def test_graph_capture_matches_eager(name):
+    from reframework_b200.moe.graph import capture_forward
+    rec = load_golden(name)
+    cfg = golden_config(rec)
+    d = generate(cfg)
+    moe = build_layer(cfg, d, harness=rec["mode"] == "harness")
+    x = d["x"].to(DEV)
+    with torch.no_grad():
+        eager = moe(x)
+    g = capture_forward(moe, x)
+    assert torch.equal(g(x), eager)
+    x2 = torch.randn_like(x)
+    with torch.no_grad():
+        eager2 = moe(x2)
+    assert torch.equal(g(x2), eager2)
+    with pytest.raises(ValueError):
+        g(x[:-1])

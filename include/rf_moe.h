@@ -86,8 +86,18 @@ int64_t rf_moe_rows_capacity(int64_t n_pairs, int64_t num_experts, int64_t align
 size_t rf_moe_permute_workspace_size(int64_t n_pairs, int64_t num_experts);
 
 /*
+ * Workspace bytes rf_moe_router_topk needs with a gate of H columns over E
+ * experts (+1 column when a shared-expert gate is given): fp32 partial logits
+ * of ceil(H/256) slices of the hidden dimension.
+ */
+size_t rf_moe_router_workspace_size(int64_t T, int64_t H, int64_t E, int has_shared_gate);
+
+/*
  * K1 — router.  For each token t:
- *   logit[e] = sum_h x[t,h] * gate[e,h]   (fp32 accumulation, fixed order)
+ *   logit[e] = sum_h x[t,h] * gate[e,h]   (fp32 accumulation in a fixed order
+ *              that depends on H only: a sequential chain over each 256-wide
+ *              slice of h, then the slice sums in slice order; the result for
+ *              a token does not depend on T or on the other tokens)
  *   if round_dtype >= 0: logit rounded to that dtype (the reference runs the
  *                        router GEMM in the layer dtype, moe_layer.py:324)
  *   if bias:             logit += bias[e]  (fp32 router with load bias)
@@ -101,14 +111,17 @@ size_t rf_moe_permute_workspace_size(int64_t n_pairs, int64_t num_experts);
  * (either may be NULL, not both); logits [T,E] fp32 (NULL to skip).
  * Requires 1 <= K <= min(E, 16), E <= 1024, H % 8 == 0.
  * gate == NULL means x already holds the [T,E] logits (H must equal E): the
- * call is then torch_fused_topk alone.
+ * call is then torch_fused_topk alone and needs no workspace.
+ * workspace: rf_moe_router_workspace_size(T, H, E, shared_gate != NULL)
+ * bytes of device memory, 16-byte aligned.
  */
 int rf_moe_router_topk(const void *x, int x_dtype, const void *gate, int gate_dtype,
                        const float *bias, int64_t T, int64_t H, int64_t E, int64_t K,
                        int renormalize, int round_dtype, int entropy_k_min,
                        const void *shared_gate, float *shared_scale,
                        float *topk_weights, int32_t *topk_ids32, int64_t *topk_ids64,
-                       float *logits, rf_stream_t stream);
+                       float *logits, void *workspace, size_t workspace_bytes,
+                       rf_stream_t stream);
 
 /*
  * K2 — counting-sort permute of the T*K pairs by expert (stable), plus the

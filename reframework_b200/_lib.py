@@ -36,7 +36,8 @@ _SIGNATURES = {
     "rf_moe_permute_workspace_size": (ctypes.c_size_t, [_i64, _i64]),
     "rf_moe_router_topk": (_int, [_c_void_p, _int, _c_void_p, _int, _c_void_p, _i64, _i64, _i64, _i64,
                                   _int, _int, _int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
-                                  _c_void_p, _c_void_p, _c_void_p]),
+                                  _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p]),
+    "rf_moe_router_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, _int]),
     "rf_moe_permute": (_int, [_c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _int, _i64, _c_void_p,
                               _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, ctypes.c_size_t,
                               _c_void_p]),

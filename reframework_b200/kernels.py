@@ -63,11 +63,17 @@ def router_topk(x: torch.Tensor, gate: Optional[torch.Tensor], top_k: int, *, re
         bias = bias.to(device=dev, dtype=torch.float32).contiguous()
     if shared_gate is not None:
         shared_gate = shared_gate.to(dtype=gate.dtype).contiguous()
+    ws_bytes = 0
+    ws = None
+    if gate is not None and T > 0:
+        ws_bytes = int(lib().rf_moe_router_workspace_size(T, H, E, int(shared_gate is not None)))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     rc = lib().rf_moe_router_topk(
         ptr(x), dtype_code(x.dtype), ptr(gate), dtype_code(gate.dtype if gate is not None else x.dtype),
         ptr(bias), T, H, E, top_k, int(bool(renormalize)),
         -1 if round_dtype is None else dtype_code(round_dtype), int(entropy_k_min),
-        ptr(shared_gate), ptr(ss), ptr(w), ptr(i32), ptr(i64), ptr(lg), stream_of(dev))
+        ptr(shared_gate), ptr(ss), ptr(w), ptr(i32), ptr(i64), ptr(lg), ptr(ws), ws_bytes,
+        stream_of(dev))
     check(rc, "rf_moe_router_topk")
     return w, i32, i64, lg, ss
 

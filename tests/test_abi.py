@@ -34,13 +34,16 @@ def test_version_and_sizes():
     assert lib.rf_moe_rows_capacity(8192, 8, 128) == 8192 + 8 * 127
     assert lib.rf_moe_rows_capacity(8192, 8, 1) == 8192
     assert lib.rf_moe_permute_workspace_size(8192, 8) >= 2 * 8 * 4
+    # router partials: ceil(H/256) slices x T x (E + shared gate) fp32
+    assert lib.rf_moe_router_workspace_size(4096, 4096, 8, 0) >= 16 * 4096 * 8 * 4
+    assert lib.rf_moe_router_workspace_size(64, 2048, 60, 1) >= 8 * 64 * 61 * 4
 
 
 @pytest.mark.parametrize("call, needle", [
     (lambda L: L.rf_moe_router_topk(None, 2, None, 2, None, 4, 64, 8, 9, 1, -1, 0, None, None,
-                                    None, None, None, None, None), "K <="),
+                                    None, None, None, None, None, 0, None), "K <="),
     (lambda L: L.rf_moe_router_topk(None, 7, None, 2, None, 4, 64, 8, 2, 1, -1, 0, None, None,
-                                    None, None, None, None, None), "dtype"),
+                                    None, None, None, None, None, 0, None), "dtype"),
     (lambda L: L.rf_moe_permute(None, 4, 2, 8, 3, None, 2, 64, None, None, None, None, None, None, 0,
                                 None), "align"),
     (lambda L: L.rf_moe_combine(None, None, None, 4, 2, 60, 2, None, None, None, 0, 0, None, None),

@@ -206,8 +206,10 @@ int rf_moe_grouped_gemm_gated(const void *a, const void *w1, void *h,
 
 /*
  * Selects the grouped-GEMM implementation for subsequent calls of this
- * process: 0 = automatic (tensor cores whenever the shape allows), 1 = CUDA
- * cores only (used by tests to cross-check the two implementations).
+ * process: 0 = automatic (tensor cores whenever the shape allows, tile width
+ * chosen per launch), 1 = CUDA cores only (used by tests to cross-check the
+ * two implementations), 2 / 3 / 4 = tensor cores with tile width N = 256 /
+ * 128 / 64 (tests and tuning; the results are the same bits for every width).
  * No reference counterpart (the reference has a single torch matmul path).
  */
 int rf_moe_set_gemm_impl(int impl);

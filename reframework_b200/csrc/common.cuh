@@ -91,13 +91,29 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) 
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
-// Gated activations of reframework/layers/activation.py, in fp32.
+// Gated activations of reframework/layers/activation.py, in fp32, with the
+// activation fixed at compile time (the GEMM epilogues are instantiated per
+// activation: no per-element branch, small code).  SiLU uses the fast
+// division (x * approximate reciprocal, within 2 ulp of fp32): the result is
+// rounded to the 16-bit storage type right after, where that error is ~2^-16
+// of one unit in the last place.
+template <int ACT>
+__device__ __forceinline__ float act_gate_t(float g) {
+  if constexpr (ACT == RF_ACT_SILU) {
+    return __fdividef(g, 1.0f + __expf(-g));
+  } else if constexpr (ACT == RF_ACT_GELU) {
+    return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
+  } else {
+    // tanh approximation: 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3)))
+    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+    return 0.5f * g * (1.0f + tanhf(k0 * (g + k1 * g * g * g)));
+  }
+}
+
 __device__ __forceinline__ float act_gate(int act, float g) {
-  if (act == RF_ACT_SILU) return g / (1.0f + __expf(-g));
-  if (act == RF_ACT_GELU) return 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
-  // tanh approximation: 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3)))
-  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  return 0.5f * g * (1.0f + tanhf(k0 * (g + k1 * g * g * g)));
+  if (act == RF_ACT_SILU) return act_gate_t<RF_ACT_SILU>(g);
+  if (act == RF_ACT_GELU) return act_gate_t<RF_ACT_GELU>(g);
+  return act_gate_t<RF_ACT_GELU_TANH>(g);
 }
 
 // Round an fp32 value to the storage type T and back (identity for fp32).
@@ -112,6 +128,13 @@ __device__ __forceinline__ float round_to(float v) {
 // (fused.py:81), act() runs on it and rounds to T, and the product of the two
 // T tensors rounds to T (activation.py:20-21).  The caller's final store
 // performs that last rounding.  For fp32 every rounding is the identity.
+template <typename T, int ACT>
+__device__ __forceinline__ float gated_elem_t(float g, float u) {
+  const float gt = round_to<T>(g);
+  const float ut = round_to<T>(u);
+  return round_to<T>(act_gate_t<ACT>(gt)) * ut;
+}
+
 template <typename T>
 __device__ __forceinline__ float gated_elem(int act, float g, float u) {
   const float gt = round_to<T>(g);

@@ -7,7 +7,7 @@
 //   down:  y[r, n] = h[r] . w2[s, n]
 // for the rows r of every listed expert (s = the expert's weight slot).
 //
-// Design (one CTA per SM, 192 threads, warp-specialised):
+// Design (one CTA per SM, 320 threads, warp-specialised):
 //   warp 0      TMA producer: per 64-deep k-block loads the 128-row A tile
 //               and the 256-row B tile (gated: 128 gate rows + the matching
 //               128 up rows, so one accumulator holds both halves) into a
@@ -16,9 +16,10 @@
 //               N=256, K=16, bf16/fp16 in, fp32 accumulate) from one thread;
 //               two accumulators (2 x 256 columns) let the epilogue of tile i
 //               overlap the main loop of tile i+1.
-//   warps 2-5   epilogue: tcgen05.ld of their 32-lane TMEM quadrant, gated
-//               activation (gated kernel), rounding, 16-byte global stores of
-//               the valid rows.
+//   warps 2-9   epilogue: tcgen05.ld of their 32-lane TMEM quadrant (two
+//               warps per quadrant, each taking half of the columns), gated
+//               activation (compiled per activation), rounding, 16-byte
+//               global stores of the valid rows.
 // Tiles: per listed expert ceil(count/128) m-blocks x n-blocks, ordered
 // n-major / m-minor inside an expert so concurrently running CTAs share the
 // weight tile through L2; CTAs stride over the tile list.  The tile table is
@@ -29,6 +30,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 #include <type_traits>
 
@@ -38,16 +40,39 @@ RF_DEVICE_ERROR_WORD();
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, NTHREADS = 192;
-constexpr int A_BYTES = BM * BK * 2;      // 16 KB
-constexpr int B_BYTES = BN * BK * 2;      // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr uint32_t TMEM_COLS = 512;       // 2 accumulators x 256 fp32 columns
+constexpr int BM = 128, BK = 64;
+#ifndef RF_EPI_WARPS
+#define RF_EPI_WARPS 8
+#endif
+#ifndef RF_EPI_SLEEP_NS
+#define RF_EPI_SLEEP_NS 256
+#endif
+constexpr int EPI_WARPS = RF_EPI_WARPS;  // 4 or 8: one or two per TMEM lane quadrant
+constexpr int EPI_SPLIT = EPI_WARPS / 4;  // warps sharing a quadrant's columns
+static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "epilogue warps");
+constexpr int NTHREADS = 32 * (2 + EPI_WARPS);
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int BM_SMALL = 32;          // A rows loaded for a tile with at most 32 valid rows
 constexpr int MAX_GROUPS = 1024;
-constexpr int NUM_BARS = 2 * STAGES + 5;  // full, empty, tmem full x2, tmem empty x2, drain
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
-constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 +
-                              (size_t)(MAX_GROUPS + 1) * 4 + (size_t)3 * MAX_GROUPS * 4;
+
+// Per tile width BN (the MMA's N: 256, 128 or 64).  Narrower tiles give more
+// tiles (better balance over 148 SMs when there are few rows, as in decode)
+// and, with the same ~192 KB ring, deeper pipelines; wider tiles read less
+// per FLOP.  TMEM holds two BN-column fp32 accumulators.
+template <int BN_>
+struct Cfg {
+  static constexpr int BN = BN_;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN == 256 ? 4 : BN == 128 ? 6 : 8;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr int NUM_BARS = 2 * STAGES + 5;  // full, empty, tmem full x2, tmem empty x2, drain
+  static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + NUM_BARS * 8 + 16 +
+                                       (size_t)(MAX_GROUPS + 1) * 4 + (size_t)3 * MAX_GROUPS * 4;
+  static_assert(BN == 256 || BN == 128 || BN == 64, "tile width");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+};
 
 struct TcArgs {
   const int32_t *offsets, *counts, *slot, *groups;
@@ -86,10 +111,12 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 // Wait for the phase of `parity` to complete.  Gives up (false) when another
 // role of this CTA aborted, or after WAIT_LIMIT_NS (then flags the abort).
-__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                          unsigned sleep_ns = 0) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = rf::globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
+    if (sleep_ns) __nanosleep(sleep_ns);
     if (mbar_try(bar, parity)) return true;
     if ((it & 63) == 0) {
       if (*abort_flag) return false;
@@ -187,18 +214,22 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 }
 
 // Instruction descriptor of kind::f16: fp32 accumulator, A/B K-major,
-// M = 128, N = 256; operand format 0 = f16, 1 = bf16 (A and B always equal).
-template <typename T>
+// M = 128, N = BN; operand format 0 = f16, 1 = bf16 (A and B always equal).
+template <typename T, int BN>
 __host__ __device__ constexpr uint32_t instr_desc() {
   return (1u << 4) | ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 7) |
          ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 10) | ((uint32_t)(BN >> 3) << 17) |
          ((uint32_t)(BM >> 4) << 24);
 }
 
-template <typename T, bool GATED>
+template <typename T, bool GATED, int ACT, int BN_>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const TcArgs p) {
+    tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA32,
+                    const __grid_constant__ CUtensorMap tmB, const TcArgs p) {
+  using C = Cfg<BN_>;
+  constexpr int BN = C::BN, STAGES = C::STAGES, B_BYTES = C::B_BYTES, STAGE_BYTES = C::STAGE_BYTES;
+  constexpr int NUM_BARS = C::NUM_BARS;
+  constexpr uint32_t TMEM_COLS = C::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t *sA = smem;
@@ -227,7 +258,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(TFULL(a), 1);
-      mbar_init(TEMPTY(a), 4);  // one arrival per epilogue warp
+      mbar_init(TEMPTY(a), EPI_WARPS);  // one arrival per epilogue warp
     }
     mbar_init(DRAIN, 1);
     *abort_flag = 0;
@@ -235,6 +266,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   if (threadIdx.x == 32) {
     asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA32) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
   }
   // per-group table: first row, row count, weight slot, tile count
@@ -318,10 +350,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             ok = false;
             break;
           }
-          mbar_expect_tx(FULL(stage), STAGE_BYTES);
+          // a tile of at most 32 valid rows loads only those 32 A rows; the
+          // MMA still reads 128 (rows past the tile's count are never stored)
+          const bool small = rows <= BM_SMALL;
+          mbar_expect_tx(FULL(stage), small ? STAGE_BYTES - A_BYTES + A_BYTES / (BM / BM_SMALL) : STAGE_BYTES);
           const uint32_t a_dst = smem_u32(sA + stage * A_BYTES);
           const uint32_t b_dst = smem_u32(sB + stage * B_BYTES);
-          tma_load_2d(a_dst, &tmA, FULL(stage), kb * BK, row0);
+          tma_load_2d(a_dst, small ? &tmA32 : &tmA, FULL(stage), kb * BK, row0);
           if (GATED) {
             tma_load_3d(b_dst, &tmB, FULL(stage), kb * BK, nb * (BN / 2), 2 * s);
             tma_load_3d(b_dst + B_BYTES / 2, &tmB, FULL(stage), kb * BK, nb * (BN / 2), 2 * s + 1);
@@ -345,7 +380,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t IDESC = instr_desc<T>();
+      constexpr uint32_t IDESC = instr_desc<T, BN>();
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -382,7 +417,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int wq = warp & 3;  // TMEM lane quadrant this warp may access
+    const int wq = warp & 3;             // TMEM lane quadrant this warp may access
+    const int part = (warp - 2) >> 2;    // which share of the columns it stores
     const int r = wq * 32 + lane;
     T *out = reinterpret_cast<T *>(p.out);
     int it = 0;
@@ -394,7 +430,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // one lane waits, the warp re-converges on the broadcast before the
       // warp-collective (.sync.aligned) TMEM loads
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(TFULL(acc), aph, abort_flag) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait(TFULL(acc), aph, abort_flag, RF_EPI_SLEEP_NS) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
@@ -404,7 +440,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (GATED) {
         const int n0 = nb * (BN / 2);
 #pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
+        for (int c = part * 32; c < BN / 2; c += 32 * EPI_SPLIT) {
           uint32_t g[32], u[32];
           tmem_ld32(tb + c, g);
           tmem_ld32(tb + BN / 2 + c, u);
@@ -413,9 +449,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint32_t pk[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const float h0 = rf::gated_elem<T>(p.act, __uint_as_float(g[2 * j]), __uint_as_float(u[2 * j]));
+              const float h0 = rf::gated_elem_t<T, ACT>(__uint_as_float(g[2 * j]), __uint_as_float(u[2 * j]));
               const float h1 =
-                  rf::gated_elem<T>(p.act, __uint_as_float(g[2 * j + 1]), __uint_as_float(u[2 * j + 1]));
+                  rf::gated_elem_t<T, ACT>(__uint_as_float(g[2 * j + 1]), __uint_as_float(u[2 * j + 1]));
               pk[j] = rf::pack2<T>(h0, h1);
             }
 #pragma unroll
@@ -430,7 +466,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       } else {
         const int n0 = nb * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = part * 32; c < BN; c += 32 * EPI_SPLIT) {
           uint32_t v32[32];
           tmem_ld32(tb + c, v32);
           tmem_ld_wait();
@@ -483,7 +519,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-int g_gemm_impl = 0;  // 0 = auto, 1 = CUDA cores only
+int g_gemm_impl = 0;  // 0 = auto, 1 = CUDA cores only, 2/3/4 = tensor cores with BN 256/128/64
 
 bool encode(CUtensorMap *m, int dtype, int rank, const void *base, const cuuint64_t *dims,
             const cuuint64_t *strides, const cuuint32_t *box) {
@@ -498,14 +534,15 @@ bool encode(CUtensorMap *m, int dtype, int rank, const void *base, const cuuint6
   return r == CUDA_SUCCESS;
 }
 
-template <typename T, bool GATED>
-int launch_tc_t(const rf::GroupedGemmArgs &g, const CUtensorMap &ma, const CUtensorMap &mb,
-                cudaStream_t st) {
-  auto kern = tc_grouped_gemm<T, GATED>;
+template <typename T, bool GATED, int ACT, int BN>
+int launch_tc_t(const rf::GroupedGemmArgs &g, const CUtensorMap &ma, const CUtensorMap &ma32,
+                const CUtensorMap &mb, cudaStream_t st) {
+  using C = Cfg<BN>;
+  auto kern = tc_grouped_gemm<T, GATED, ACT, BN>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM_BYTES);
   });
   if (attr_err != cudaSuccess)
     return rf::fail(RF_ERR_CUDA, std::string("tensor-core GEMM: ") + cudaGetErrorString(attr_err));
@@ -522,8 +559,41 @@ int launch_tc_t(const rf::GroupedGemmArgs &g, const CUtensorMap &ma, const CUten
   p.n_tiles_n = GATED ? (g.N + BN / 2 - 1) / (BN / 2) : (g.N + BN - 1) / BN;
   p.out = g.out;
   p.act = g.act;
-  kern<<<rf::num_sms(), NTHREADS, SMEM_BYTES, st>>>(ma, mb, p);
+  kern<<<rf::num_sms(), NTHREADS, C::SMEM_BYTES, st>>>(ma, ma32, mb, p);
   return rf::check_launch(GATED ? "tensor-core gated GEMM" : "tensor-core down GEMM");
+}
+
+template <typename T, int BN>
+int launch_tc_bn(const rf::GroupedGemmArgs &g, bool gated, const CUtensorMap &ma, const CUtensorMap &ma32,
+                 const CUtensorMap &mb, cudaStream_t st) {
+  if (!gated) return launch_tc_t<T, false, 0, BN>(g, ma, ma32, mb, st);
+  if (g.act == RF_ACT_SILU) return launch_tc_t<T, true, RF_ACT_SILU, BN>(g, ma, ma32, mb, st);
+  if (g.act == RF_ACT_GELU) return launch_tc_t<T, true, RF_ACT_GELU, BN>(g, ma, ma32, mb, st);
+  return launch_tc_t<T, true, RF_ACT_GELU_TANH, BN>(g, ma, ma32, mb, st);
+}
+
+template <typename T>
+int launch_tc_dt(const rf::GroupedGemmArgs &g, bool gated, int bn, const CUtensorMap &ma,
+                 const CUtensorMap &ma32, const CUtensorMap &mb, cudaStream_t st) {
+  if (bn == 256) return launch_tc_bn<T, 256>(g, gated, ma, ma32, mb, st);
+  if (bn == 128) return launch_tc_bn<T, 128>(g, gated, ma, ma32, mb, st);
+  return launch_tc_bn<T, 64>(g, gated, ma, ma32, mb, st);
+}
+
+// Tile width of one launch.  The per-expert row counts live on the device,
+// so the host estimates the routed pairs from the row capacity minus the
+// permute's padding allowance.  With many rows per group the widest tile
+// wins clearly (measured on B200: narrower tiles read more bytes per FLOP and
+// the kernel is then bound by L2->SM bandwidth); with few rows per group
+// (decode) the launch streams weights and twice the tiles balance better over
+// the SMs, so N = 128.
+int pick_bn(const rf::GroupedGemmArgs &g, bool gated) {
+  (void)gated;
+  if (g_gemm_impl >= 2) return g_gemm_impl == 2 ? 256 : g_gemm_impl == 3 ? 128 : 64;
+  const int64_t groups = std::max(1, g.n_groups);
+  int64_t pairs = g.rows_capacity - groups * (BM - 1);
+  if (pairs < 1) pairs = std::min<int64_t>(g.rows_capacity, groups);
+  return pairs < groups * 64 ? 128 : 256;
 }
 
 // Returns 1 if the tensor-core path took the call (status in *rc), 0 if the
@@ -538,21 +608,23 @@ int try_tc(const rf::GroupedGemmArgs &g, bool gated, cudaStream_t st, int *rc) {
     *rc = rf::fail(RF_ERR_CUDA, "tensor-core GEMM: cuTensorMapEncodeTiled is unavailable");
     return 1;
   }
-  CUtensorMap ma, mb;
+  const int bn = pick_bn(g, gated);
+  CUtensorMap ma, ma32, mb;
   const cuuint64_t dA[2] = {(cuuint64_t)g.Kdim, (cuuint64_t)g.rows_capacity};
   const cuuint64_t sAs[1] = {(cuuint64_t)g.Kdim * 2};
   const cuuint32_t bA[2] = {BK, BM};
-  bool ok = encode(&ma, g.dtype, 2, g.a, dA, sAs, bA);
+  const cuuint32_t bA32[2] = {BK, BM_SMALL};
+  bool ok = encode(&ma, g.dtype, 2, g.a, dA, sAs, bA) && encode(&ma32, g.dtype, 2, g.a, dA, sAs, bA32);
   if (gated) {
     // w1 [S, 2N, K] viewed as [2S][N][K]: half 0 = gate rows, half 1 = up rows
     const cuuint64_t dB[3] = {(cuuint64_t)g.Kdim, (cuuint64_t)g.N, (cuuint64_t)(2 * g.num_slots)};
     const cuuint64_t sB[2] = {(cuuint64_t)g.Kdim * 2, (cuuint64_t)g.N * g.Kdim * 2};
-    const cuuint32_t bB[3] = {BK, BN / 2, 1};
+    const cuuint32_t bB[3] = {BK, (cuuint32_t)(bn / 2), 1};
     ok = ok && encode(&mb, g.dtype, 3, g.w, dB, sB, bB);
   } else {
     const cuuint64_t dB[3] = {(cuuint64_t)g.Kdim, (cuuint64_t)g.N, (cuuint64_t)g.num_slots};
     const cuuint64_t sB[2] = {(cuuint64_t)g.Kdim * 2, (cuuint64_t)g.N * g.Kdim * 2};
-    const cuuint32_t bB[3] = {BK, BN, 1};
+    const cuuint32_t bB[3] = {BK, (cuuint32_t)bn, 1};
     ok = ok && encode(&mb, g.dtype, 3, g.w, dB, sB, bB);
   }
   if (!ok) {
@@ -560,10 +632,9 @@ int try_tc(const rf::GroupedGemmArgs &g, bool gated, cudaStream_t st, int *rc) {
     return 1;
   }
   if (g.dtype == RF_BF16)
-    *rc = gated ? launch_tc_t<__nv_bfloat16, true>(g, ma, mb, st)
-                : launch_tc_t<__nv_bfloat16, false>(g, ma, mb, st);
+    *rc = launch_tc_dt<__nv_bfloat16>(g, gated, bn, ma, ma32, mb, st);
   else
-    *rc = gated ? launch_tc_t<__half, true>(g, ma, mb, st) : launch_tc_t<__half, false>(g, ma, mb, st);
+    *rc = launch_tc_dt<__half>(g, gated, bn, ma, ma32, mb, st);
   return 1;
 }
 
@@ -609,7 +680,7 @@ int grouped_gemm(const void *a, const void *w, void *out, const int32_t *offsets
 }  // namespace
 
 extern "C" int rf_moe_set_gemm_impl(int impl) {
-  if (impl != 0 && impl != 1) return rf::fail(RF_ERR_ARG, "rf_moe_set_gemm_impl: 0 or 1");
+  if (impl < 0 || impl > 4) return rf::fail(RF_ERR_ARG, "rf_moe_set_gemm_impl: 0 to 4");
   g_gemm_impl = impl;
   return RF_OK;
 }

@@ -3,8 +3,10 @@
 //
 // Restates the grouping of reframework/moe/fused.py:71-80 (bincount, then per
 // active expert the rows `flat_expert == e` in ascending flat index t*K+k, and
-// `hidden_states[tok]`).  Three launches:
-//   1. permute_hist     per-block expert histograms of the flat ids
+// `hidden_states[tok]`).  Up to three launches:
+//   1. permute_hist     per-block expert histograms of the flat ids (only
+//                       with more than one block: a single block, as in
+//                       decode, counts its own pairs)
 //   2. permute_scatter  per-expert totals -> padded exclusive scan (offsets),
 //                       then a stable in-block ranking (warp match + per-warp
 //                       running cursors) that assigns every pair its row
@@ -76,30 +78,71 @@ __device__ int block_exclusive_scan(int *v, int E, int *s_tmp) {
   return total;
 }
 
-__global__ void __launch_bounds__(PT) permute_scatter(const int32_t *ids, int64_t n, int K, int E,
-                                                      int align, const int32_t *block_counts,
-                                                      int nblk, int32_t *offsets_out,
+// One block per CHUNK pairs; warp w owns pairs [w0, w1) of the block and
+// keeps their ids in registers (PER_LANE per lane) for both passes.
+// single != 0 (one block in the grid, the decode case): the block's own warp
+// histograms give the expert totals and block_counts is not read, so the
+// permute_hist launch is skipped.
+constexpr int PER_LANE = SUB / 32;
+
+__global__ void __launch_bounds__(PT) permute_scatter(const int32_t *ids, int64_t n, int E, int align,
+                                                      const int32_t *block_counts, int nblk,
+                                                      int single, int32_t *offsets_out,
                                                       int32_t *counts_out, int32_t *row_of_slot,
                                                       int32_t *src_slot) {
   extern __shared__ int smem[];
-  int *s_tot = smem;                 // [E]
+  int *s_tot = smem;                 // [E]   expert totals, later the block's first row per expert
   int *s_off = s_tot + E;            // [E]   padded exclusive offsets
-  int *s_wc = s_off + E;             // [PW][E] per-warp cursors
+  int *s_before = s_off + E;         // [E]   pairs of earlier blocks per expert
+  int *s_wc = s_before + E;          // [PW][E] per-warp counts, then per-warp cursors
   int *s_tmp = s_wc + PW * E;        // [PW]
   const int b = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t w0 = (int64_t)b * CHUNK + (int64_t)warp * SUB;
+  const int64_t w1 = min(n, w0 + SUB);
 
-  // 1. per-expert totals and this block's base within each expert
+  // 0. this warp's ids, loaded once (invalid ids become -1 and are reported)
+  int my_e[PER_LANE];
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    const int64_t i = w0 + j * 32 + lane;
+    int e = -1;
+    if (i < w1) {
+      e = ids[i];
+      if (e < 0 || e >= E) {
+        if (single) rf_report(RF_DEV_BAD_EXPERT_ID);
+        e = -1;
+      }
+    }
+    my_e[j] = e;
+  }
+  for (int i = threadIdx.x; i < PW * E; i += PT) s_wc[i] = 0;
+  __syncthreads();
+  // 1. per-warp histograms of this block's chunk
+  int *wc = s_wc + warp * E;
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    const int e = my_e[j];
+    const unsigned grp = __match_any_sync(0xffffffffu, e);
+    if (lane == __ffs(grp) - 1 && e >= 0) wc[e] += __popc(grp);
+    __syncwarp();
+  }
+  __syncthreads();
+  // 2. per-expert totals and this block's base within each expert
   for (int e = threadIdx.x; e < E; e += PT) {
     int tot = 0, before = 0;
-    for (int bb = 0; bb < nblk; ++bb) {
-      const int c = block_counts[(int64_t)bb * E + e];
-      if (bb < b) before += c;
-      tot += c;
+    if (single) {
+      for (int w = 0; w < PW; ++w) tot += s_wc[w * E + e];
+    } else {
+      for (int bb = 0; bb < nblk; ++bb) {
+        const int c = block_counts[(int64_t)bb * E + e];
+        if (bb < b) before += c;
+        tot += c;
+      }
     }
     s_tot[e] = tot;
     s_off[e] = (tot + align - 1) / align * align;
-    s_wc[e] = before;  // stash in warp-0 row for now
+    s_before[e] = before;
   }
   __syncthreads();
   const int used = block_exclusive_scan(s_off, E, s_tmp);
@@ -116,33 +159,9 @@ __global__ void __launch_bounds__(PT) permute_scatter(const int32_t *ids, int64_
     const int p1 = s_off[e] + (s_tot[e] + align - 1) / align * align;
     for (int r = p0 + threadIdx.x; r < p1; r += PT) src_slot[r] = -1;
   }
-  // 2. per-warp histograms of this block's chunk
-  const int64_t c0 = (int64_t)b * CHUNK;
-  const int64_t w0 = c0 + (int64_t)warp * SUB;
-  const int64_t w1 = min(n, w0 + SUB);
-  __syncthreads();
-  // move the block base out of s_wc[0..E) before zeroing the warp rows
-  for (int e = threadIdx.x; e < E; e += PT) s_tot[e] = s_off[e] + s_wc[e];  // block's first row per expert
-  __syncthreads();
-  for (int i = threadIdx.x; i < PW * E; i += PT) s_wc[i] = 0;
-  __syncthreads();
-  int *wc = s_wc + warp * E;
-  for (int64_t i0 = w0; i0 < w1; i0 += 32) {
-    const int64_t i = i0 + lane;
-    int e = -1;
-    if (i < w1) {
-      e = ids[i];
-      if (e < 0 || e >= E) e = -1;
-    }
-    const unsigned grp = __match_any_sync(0xffffffffu, e);
-    const int leader = __ffs(grp) - 1;
-    if (lane == leader && e >= 0 && i < w1) wc[e] += __popc(grp);
-    __syncwarp();
-  }
-  __syncthreads();
-  // 3. exclusive prefix over warps, seeded with the block base
+  // 3. exclusive prefix over warps, seeded with the block's first row
   for (int e = threadIdx.x; e < E; e += PT) {
-    int run = s_tot[e];
+    int run = s_off[e] + s_before[e];
     for (int w = 0; w < PW; ++w) {
       const int c = s_wc[w * E + e];
       s_wc[w * E + e] = run;
@@ -152,13 +171,10 @@ __global__ void __launch_bounds__(PT) permute_scatter(const int32_t *ids, int64_
   __syncthreads();
   // 4. stable scatter: rank inside each 32-pair group, groups in order
   const unsigned lt = (1u << lane) - 1u;
-  for (int64_t i0 = w0; i0 < w1; i0 += 32) {
-    const int64_t i = i0 + lane;
-    int e = -1;
-    if (i < w1) {
-      e = ids[i];
-      if (e < 0 || e >= E) e = -1;
-    }
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    const int64_t i = w0 + j * 32 + lane;
+    const int e = my_e[j];
     const unsigned grp = __match_any_sync(0xffffffffu, e);
     const int leader = __ffs(grp) - 1;
     int row = -1;
@@ -171,7 +187,6 @@ __global__ void __launch_bounds__(PT) permute_scatter(const int32_t *ids, int64_
       if (row >= 0) src_slot[row] = (int32_t)i;
     }
   }
-  (void)K;
 }
 
 template <int UNROLL>
@@ -214,6 +229,41 @@ int launch_gather(const void *src, const int32_t *index, int64_t index_div, int6
   return rf::check_launch("rf_moe_gather_rows");
 }
 
+// hist (several blocks only) + scatter + optional gather.  block_counts holds
+// ceil(n/CHUNK) * E words when there is more than one block.
+int launch_permute(const int32_t *topk_ids, int64_t n, int64_t K, int64_t E, int64_t align,
+                   const void *x, int dtype, int64_t H, int32_t *expert_offsets,
+                   int32_t *expert_counts, int32_t *row_of_slot, int32_t *src_slot, void *x_perm,
+                   int32_t *block_counts, cudaStream_t st, const char *name) {
+  const std::string nm(name);
+  if (n == 0) {
+    // no pairs: every expert is empty
+    cudaError_t e1 = cudaMemsetAsync(expert_offsets, 0, (E + 1) * 4, st);
+    cudaError_t e2 = cudaMemsetAsync(expert_counts, 0, E * 4, st);
+    if (e1 != cudaSuccess || e2 != cudaSuccess) return rf::fail(RF_ERR_CUDA, nm + ": memset failed");
+    return RF_OK;
+  }
+  const int nblk = (int)((n + CHUNK - 1) / CHUNK);
+  if (nblk > 1) {
+    // permute_hist writes every one of the nblk*E words the scatter reads
+    permute_hist<<<nblk, PT, E * sizeof(int), st>>>(topk_ids, n, (int)E, block_counts);
+    int rc = rf::check_launch((nm + "(hist)").c_str());
+    if (rc) return rc;
+  }
+  const size_t smem = (size_t)(3 * E + PW * E + PW) * sizeof(int);
+  permute_scatter<<<nblk, PT, smem, st>>>(topk_ids, n, (int)E, (int)align, block_counts, nblk,
+                                          nblk == 1 ? 1 : 0, expert_offsets, expert_counts,
+                                          row_of_slot, src_slot);
+  int rc = rf::check_launch((nm + "(scatter)").c_str());
+  if (rc) return rc;
+  if (x_perm) {
+    const int64_t rows_cap = n + E * (align - 1);
+    return launch_gather(x, src_slot, K, rows_cap, expert_offsets + E,
+                         H * (int64_t)rf::dtype_size(dtype), x_perm, st);
+  }
+  return RF_OK;
+}
+
 }  // namespace
 
 extern "C" size_t rf_moe_permute_workspace_size(int64_t n_pairs, int64_t num_experts) {
@@ -250,32 +300,9 @@ extern "C" int rf_moe_permute(const int32_t *topk_ids, int64_t T, int64_t K, int
   RF_CHECK_ARG(!x_perm || (x && rf::valid_dtype(dtype) && H > 0 &&
                            (H * (int64_t)rf::dtype_size(dtype)) % 16 == 0),
                "rf_moe_permute: gather needs x, a dtype and H*elsize % 16 == 0");
-  cudaStream_t st = (cudaStream_t)stream;
-  const int nblk = (int)(n > 0 ? (n + CHUNK - 1) / CHUNK : 1);
-  int32_t *block_counts = reinterpret_cast<int32_t *>(workspace);
-  if (n == 0) {
-    // no pairs: every expert is empty
-    cudaError_t e1 = cudaMemsetAsync(expert_offsets, 0, (E + 1) * 4, st);
-    cudaError_t e2 = cudaMemsetAsync(expert_counts, 0, E * 4, st);
-    if (e1 != cudaSuccess || e2 != cudaSuccess)
-      return rf::fail(RF_ERR_CUDA, "rf_moe_permute: memset failed");
-    return RF_OK;
-  }
-  permute_hist<<<nblk, PT, E * sizeof(int), st>>>(topk_ids, n, (int)E, block_counts);
-  int rc = rf::check_launch("rf_moe_permute(hist)");
-  if (rc) return rc;
-  const size_t smem = (size_t)(2 * E + PW * E + PW) * sizeof(int);
-  permute_scatter<<<nblk, PT, smem, st>>>(topk_ids, n, (int)K, (int)E, (int)align, block_counts,
-                                          nblk, expert_offsets, expert_counts, row_of_slot,
-                                          src_slot);
-  rc = rf::check_launch("rf_moe_permute(scatter)");
-  if (rc) return rc;
-  if (x_perm) {
-    const int64_t rows_cap = n + E * (align - 1);
-    return launch_gather(x, src_slot, K, rows_cap, expert_offsets + E,
-                         H * (int64_t)rf::dtype_size(dtype), x_perm, st);
-  }
-  return RF_OK;
+  return launch_permute(topk_ids, n, K, E, align, x, dtype, H, expert_offsets, expert_counts,
+                        row_of_slot, src_slot, x_perm, reinterpret_cast<int32_t *>(workspace),
+                        (cudaStream_t)stream, "rf_moe_permute");
 }
 
 // ---------------------------------------------------------------------------
@@ -339,29 +366,7 @@ extern "C" int rf_moe_permute_noalloc(const int32_t *topk_ids, int64_t T, int64_
   int32_t *block_counts = nullptr;
   int rc = noalloc_scratch(&block_counts);
   if (rc) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
-  if (n == 0) {
-    cudaError_t e1 = cudaMemsetAsync(expert_offsets, 0, (E + 1) * 4, st);
-    cudaError_t e2 = cudaMemsetAsync(expert_counts, 0, E * 4, st);
-    if (e1 != cudaSuccess || e2 != cudaSuccess)
-      return rf::fail(RF_ERR_CUDA, "rf_moe_permute_noalloc: memset failed");
-    return RF_OK;
-  }
-  // permute_hist writes every one of the nblk*E words the scatter reads, so
-  // nothing left in the array by an earlier call needs clearing.
-  permute_hist<<<(int)nblk, PT, E * sizeof(int), st>>>(topk_ids, n, (int)E, block_counts);
-  rc = rf::check_launch("rf_moe_permute_noalloc(hist)");
-  if (rc) return rc;
-  const size_t smem = (size_t)(2 * E + PW * E + PW) * sizeof(int);
-  permute_scatter<<<(int)nblk, PT, smem, st>>>(topk_ids, n, (int)K, (int)E, (int)align, block_counts,
-                                               (int)nblk, expert_offsets, expert_counts, row_of_slot,
-                                               src_slot);
-  rc = rf::check_launch("rf_moe_permute_noalloc(scatter)");
-  if (rc) return rc;
-  if (x_perm) {
-    const int64_t rows_cap = n + E * (align - 1);
-    return launch_gather(x, src_slot, K, rows_cap, expert_offsets + E,
-                         H * (int64_t)rf::dtype_size(dtype), x_perm, st);
-  }
-  return RF_OK;
+  return launch_permute(topk_ids, n, K, E, align, x, dtype, H, expert_offsets, expert_counts,
+                        row_of_slot, src_slot, x_perm, block_counts, (cudaStream_t)stream,
+                        "rf_moe_permute_noalloc");
 }

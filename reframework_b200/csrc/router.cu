@@ -27,7 +27,6 @@ RF_DEVICE_ERROR_WORD();
 namespace {
 
 constexpr int THREADS = 256;
-constexpr int KC = 32;         // k-chunk staged in shared memory
 constexpr int SLICE = 256;     // H elements per slice: fixed, so the sum order never depends on T
 constexpr int KMAX = 16;
 
@@ -81,9 +80,11 @@ __device__ __forceinline__ int xcol(int k, int tok) {
 // TM tokens tg*TM.. and the 8 experts eg*4..eg*4+3, ET/2+eg*4..ET/2+eg*4+3
 // (a register tile: per k, one x read and two float4 gate reads feed 8*TM
 // FMAs).  The chunk k0+KC is fetched into registers while chunk k0 is
-// multiplied from shared memory.  Each output is one fp32 FMA chain over its
-// slice in ascending k, whatever the tile shape or T.
-template <typename TX, typename TG, int ET, int TM>
+// multiplied from shared memory; KC = 64 for the narrow tile used with few
+// tokens (fewer, larger round trips), 32 otherwise.  Each output is one fp32
+// FMA chain over its slice in ascending k, whatever the tile shape, KC or T
+// (a chunk past the slice end adds exact zeros).
+template <typename TX, typename TG, int ET, int TM, int KC>
 __global__ void __launch_bounds__(THREADS) router_logits_kernel(LogitsArgs a) {
   constexpr int EGRP = ET / 8;
   constexpr int TT = TM * THREADS / EGRP;  // tokens per tile
@@ -360,11 +361,11 @@ Plan make_plan(int64_t T, int H, int Ec) {
 template <typename TX, typename TG>
 void launch_logits(const LogitsArgs &a, const Plan &p, cudaStream_t st) {
   dim3 grid((unsigned)p.ttiles, p.etiles, p.slices);
-  if (p.et == 8) router_logits_kernel<TX, TG, 8, 1><<<grid, THREADS, 0, st>>>(a);
-  else if (p.et == 16) router_logits_kernel<TX, TG, 16, 2><<<grid, THREADS, 0, st>>>(a);
-  else if (p.et == 32) router_logits_kernel<TX, TG, 32, 4><<<grid, THREADS, 0, st>>>(a);
-  else if (p.tm == 4) router_logits_kernel<TX, TG, 64, 4><<<grid, THREADS, 0, st>>>(a);
-  else router_logits_kernel<TX, TG, 64, 1><<<grid, THREADS, 0, st>>>(a);
+  if (p.et == 8) router_logits_kernel<TX, TG, 8, 1, 32><<<grid, THREADS, 0, st>>>(a);
+  else if (p.et == 16) router_logits_kernel<TX, TG, 16, 2, 32><<<grid, THREADS, 0, st>>>(a);
+  else if (p.et == 32) router_logits_kernel<TX, TG, 32, 4, 32><<<grid, THREADS, 0, st>>>(a);
+  else if (p.tm == 4) router_logits_kernel<TX, TG, 64, 4, 32><<<grid, THREADS, 0, st>>>(a);
+  else router_logits_kernel<TX, TG, 64, 1, 64><<<grid, THREADS, 0, st>>>(a);
 }
 
 template <typename TX>

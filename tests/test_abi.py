@@ -52,7 +52,7 @@ def test_version_and_sizes():
      "unknown mode"),
     (lambda L: L.rf_moe_grouped_gemm_gated(None, None, None, None, None, None, None, 0, 8, 8, 64, 64,
                                            64, 2, 9, None), "activation"),
-    (lambda L: L.rf_moe_set_gemm_impl(5), "0 or 1"),
+    (lambda L: L.rf_moe_set_gemm_impl(5), "0 to 4"),
 ])
 def test_argument_validation(call, needle):
     lib = _lib.lib()

@@ -143,7 +143,7 @@ def _torch_grouped(a, w1, w2, counts, offs, act, slot=None):
     return h_ref, y_ref
 
 
-@pytest.mark.parametrize("impl", [0, 1])
+@pytest.mark.parametrize("impl", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("H,I,counts,act", [
     (256, 256, [130, 0, 1, 300], "silu"),
@@ -175,6 +175,37 @@ def test_grouped_gemms_vs_torch(impl, dtype, H, I, counts, act):
         assert max_rel(yc[offs[e]:offs[e] + c], y_ref[e]) < 8e-3, f"y expert {e}"
         # rows past the expert's count are never written
         assert torch.count_nonzero(hc[offs[e] + c:offs[e + 1]]) == 0
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu"])
+@pytest.mark.parametrize("H,I,counts", [
+    (1024, 1408, [700, 64, 129, 3, 0, 256]),   # prefill-like: several m-blocks per expert
+    (2048, 1408, [5, 1, 0, 9, 2, 4, 0, 7]),     # decode-like: a few rows per expert
+])
+def test_tile_width_is_bitwise_invariant(H, I, counts, act):
+    """Tile widths 256 / 128 / 64 run the same MMA chain per output element,
+    so the automatic per-launch choice never changes a result bit (the
+    expert-parallel layer, whose launches see fewer rows, relies on this)."""
+    g = torch.Generator().manual_seed(H * 7 + I)
+    dtype = torch.bfloat16
+    E = len(counts)
+    offs = _segments(counts)
+    rows = offs[-1]
+    a = torch.randn(rows, H, generator=g).to(dtype).to(DEV)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.05).to(dtype).to(DEV)
+    w2 = (torch.randn(E, H, I, generator=g) * 0.05).to(dtype).to(DEV)
+    off_t = torch.tensor(offs, dtype=torch.int32, device=DEV)
+    cnt_t = torch.tensor(counts, dtype=torch.int32, device=DEV)
+    outs = []
+    for impl in (2, 3, 4, 0):
+        _lib.set_gemm_impl(impl)
+        h = torch.zeros(rows, I, dtype=dtype, device=DEV)
+        y = torch.zeros(rows, H, dtype=dtype, device=DEV)
+        K.grouped_gemm_gated(a, w1, off_t, cnt_t, h, activation=act)
+        K.grouped_gemm_down(h, w2, off_t, cnt_t, y)
+        outs.append((h, y))
+    for h, y in outs[1:]:
+        assert torch.equal(h, outs[0][0]) and torch.equal(y, outs[0][1])
 
 
 def test_grouped_gemm_slot_table_and_groups():

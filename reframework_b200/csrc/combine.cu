@@ -54,81 +54,169 @@ template <> __device__ __forceinline__ void store16<__half>(__half *p, const flo
                                              rf::pack2<__half>(f[4], f[5]), rf::pack2<__half>(f[6], f[7]));
 }
 
+// One block per token (grid-stride).  Warp 0's lanes read the K slots of the
+// next token while this one is combined (the read is off the critical path)
+// and rank the valid ones with shuffles (by row in reference mode, by slot
+// otherwise) into a shared list.  Each thread owns up to VPT 16-byte vectors
+// of the row and, KB listed slots at a time, issues all their loads before
+// accumulating.
+//
+// Reference mode, 16-bit types: the weighted rows are accumulated with packed
+// bf16x2 / half2 instructions that round each product and each sum once to
+// the storage type (__hmul2_rn / __hadd2_rn, never contracted into an FMA).
+// A product of two 16-bit values is exact in fp32, so this equals rounding the
+// fp32 product, and a sum of two 16-bit values rounds to the same 16-bit value
+// whether or not it passes through fp32 first: the same bits as the scalar
+// fp32-then-round formulation, at one instruction per element.
+constexpr int KB = 4;   // slots whose loads are issued together
+constexpr int VPT = 2;  // vectors per thread per pass
+
+template <typename T> struct Pair;
+template <> struct Pair<__nv_bfloat16> {
+  using T2 = __nv_bfloat162;
+  static __device__ __forceinline__ T2 splat(float w) { return __float2bfloat162_rn(w); }
+};
+template <> struct Pair<__half> {
+  using T2 = __half2;
+  static __device__ __forceinline__ T2 splat(float w) { return __float2half2_rn(w); }
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t mul_add2(uint32_t acc, uint32_t y, typename Pair<T>::T2 w2) {
+  using T2 = typename Pair<T>::T2;
+  const T2 a = *reinterpret_cast<const T2 *>(&acc);
+  const T2 b = *reinterpret_cast<const T2 *>(&y);
+  const T2 r = __hadd2_rn(a, __hmul2_rn(b, w2));
+  return *reinterpret_cast<const uint32_t *>(&r);
+}
+
 template <typename T, bool REF>
 __global__ void __launch_bounds__(CT) combine_kernel(CombineArgs a) {
   constexpr int V = 16 / sizeof(T);  // elements per 16-byte vector
+  constexpr bool PACKED = REF && sizeof(T) == 2;
   __shared__ int s_row[KMAX];
   __shared__ float s_w[KMAX];
   __shared__ int s_n;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const T *y = reinterpret_cast<const T *>(a.y);
   const T *sy = reinterpret_cast<const T *>(a.shared_y);
   const T *res = reinterpret_cast<const T *>(a.residual);
   T *out = reinterpret_cast<T *>(a.out);
   const int nv = a.H / V;
+  int r_next = -1;
+  float w_next = 0.f;
+  if (warp == 0 && lane < a.K && (int64_t)blockIdx.x < a.T) {
+    r_next = a.row_of_slot[(int64_t)blockIdx.x * a.K + lane];
+    w_next = a.w[(int64_t)blockIdx.x * a.K + lane];
+  }
   for (int64_t t = blockIdx.x; t < a.T; t += gridDim.x) {
-    if (threadIdx.x == 0) {
-      // valid slots, sorted by row (= by expert id) for the reference order
-      int n = 0;
-      for (int k = 0; k < a.K; ++k) {
-        const int r = a.row_of_slot[t * a.K + k];
-        if (r < 0) continue;
-        float wk = a.w[t * a.K + k];
-        if (REF) wk = rf::round_to<T>(wk);
-        int j = n++;
-        while (REF && j > 0 && s_row[j - 1] > r) {
-          s_row[j] = s_row[j - 1];
-          s_w[j] = s_w[j - 1];
-          --j;
-        }
-        s_row[j] = r;
-        s_w[j] = wk;
+    if (warp == 0) {
+      const int r = lane < a.K ? r_next : -1;
+      float wk = w_next;
+      const int64_t tn = t + gridDim.x;
+      if (lane < a.K && tn < a.T) {
+        r_next = a.row_of_slot[tn * a.K + lane];
+        w_next = a.w[tn * a.K + lane];
       }
-      s_n = n;
+      if (REF) wk = rf::round_to<T>(wk);
+      const bool valid = r >= 0;
+      int rank = 0;
+      for (int j = 0; j < a.K; ++j) {
+        const int rj = __shfl_sync(0xffffffffu, r, j);
+        if (rj >= 0 && (REF ? rj < r : j < lane)) ++rank;
+      }
+      const int n = __popc(__ballot_sync(0xffffffffu, valid));
+      if (valid) {
+        s_row[rank] = r;
+        s_w[rank] = wk;
+      }
+      if (lane == 0) s_n = n;
     }
     __syncthreads();
     const int n = s_n;
     const float sscale = (sy && a.shared_scale) ? a.shared_scale[t] : 1.0f;
-    for (int v = threadIdx.x; v < nv; v += CT) {
-      float acc[V];
+    for (int v0 = threadIdx.x; v0 < nv; v0 += CT * VPT) {
+      float acc[VPT][V];
+      uint32_t pacc[VPT][4];
 #pragma unroll
-      for (int i = 0; i < V; ++i) acc[i] = 0.f;
-      for (int k = 0; k < n; ++k) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(y + (int64_t)s_row[k] * a.H) + v);
-        float f[V];
-        rf::unpack16<T>(q, f);
-        const float wk = s_w[k];
+      for (int u = 0; u < VPT; ++u) {
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-          if (REF) acc[i] = rf::round_to<T>(__fadd_rn(acc[i], rf::round_to<T>(__fmul_rn(f[i], wk))));
-          else acc[i] = fmaf(wk, f[i], acc[i]);
+        for (int i = 0; i < V; ++i) acc[u][i] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pacc[u][i] = 0u;
+      }
+      for (int k0 = 0; k0 < n; k0 += KB) {
+        uint4 q[KB][VPT];
+#pragma unroll
+        for (int j = 0; j < KB; ++j) {
+          const bool kj = k0 + j < n;
+          const uint4 *yr = reinterpret_cast<const uint4 *>(y + (int64_t)(kj ? s_row[k0 + j] : 0) * a.H);
+#pragma unroll
+          for (int u = 0; u < VPT; ++u) {
+            const int v = v0 + u * CT;
+            q[j][u] = (kj && v < nv) ? __ldg(yr + v) : make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < KB; ++j) {
+          if (k0 + j >= n) break;
+          const float w = s_w[k0 + j];
+          if constexpr (PACKED) {
+            const typename Pair<T>::T2 w2 = Pair<T>::splat(w);
+#pragma unroll
+            for (int u = 0; u < VPT; ++u) {
+              pacc[u][0] = mul_add2<T>(pacc[u][0], q[j][u].x, w2);
+              pacc[u][1] = mul_add2<T>(pacc[u][1], q[j][u].y, w2);
+              pacc[u][2] = mul_add2<T>(pacc[u][2], q[j][u].z, w2);
+              pacc[u][3] = mul_add2<T>(pacc[u][3], q[j][u].w, w2);
+            }
+          } else {
+#pragma unroll
+            for (int u = 0; u < VPT; ++u) {
+              float f[V];
+              rf::unpack16<T>(q[j][u], f);
+#pragma unroll
+              for (int i = 0; i < V; ++i) {
+                if (REF) acc[u][i] = rf::round_to<T>(__fadd_rn(acc[u][i], rf::round_to<T>(__fmul_rn(f[i], w))));
+                else acc[u][i] = fmaf(w, f[i], acc[u][i]);
+              }
+            }
+          }
         }
       }
-      if (sy) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(sy + t * a.H) + v);
-        float f[V];
-        rf::unpack16<T>(q, f);
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-          if (REF) acc[i] = rf::round_to<T>(__fadd_rn(acc[i], rf::round_to<T>(__fmul_rn(f[i], sscale))));
-          else acc[i] = fmaf(sscale, f[i], acc[i]);
+      for (int u = 0; u < VPT; ++u) {
+        const int v = v0 + u * CT;
+        if (v >= nv) continue;
+        float *ac = acc[u];
+        if constexpr (PACKED) rf::unpack16<T>(make_uint4(pacc[u][0], pacc[u][1], pacc[u][2], pacc[u][3]), ac);
+        if (sy) {
+          const uint4 q = __ldg(reinterpret_cast<const uint4 *>(sy + t * a.H) + v);
+          float f[V];
+          rf::unpack16<T>(q, f);
+#pragma unroll
+          for (int i = 0; i < V; ++i) {
+            if (REF) ac[i] = rf::round_to<T>(__fadd_rn(ac[i], rf::round_to<T>(__fmul_rn(f[i], sscale))));
+            else ac[i] = fmaf(sscale, f[i], ac[i]);
+          }
         }
-      }
-      if (res) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(res + t * a.H) + v);
-        float f[V];
-        rf::unpack16<T>(q, f);
+        if (res) {
+          const uint4 q = __ldg(reinterpret_cast<const uint4 *>(res + t * a.H) + v);
+          float f[V];
+          rf::unpack16<T>(q, f);
 #pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] = REF ? rf::round_to<T>(__fadd_rn(acc[i], f[i])) : acc[i] + f[i];
-      }
-      T *o = out + t * a.H + (int64_t)v * V;
-      if (a.accumulate) {
-        const uint4 q = *reinterpret_cast<const uint4 *>(o);
-        float f[V];
-        rf::unpack16<T>(q, f);
+          for (int i = 0; i < V; ++i) ac[i] = REF ? rf::round_to<T>(__fadd_rn(ac[i], f[i])) : ac[i] + f[i];
+        }
+        T *o = out + t * a.H + (int64_t)v * V;
+        if (a.accumulate) {
+          const uint4 q = *reinterpret_cast<const uint4 *>(o);
+          float f[V];
+          rf::unpack16<T>(q, f);
 #pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] = __fadd_rn(acc[i], f[i]);
+          for (int i = 0; i < V; ++i) ac[i] = __fadd_rn(ac[i], f[i]);
+        }
+        store16<T>(o, ac);
       }
-      store16<T>(o, acc);
     }
     __syncthreads();
   }

@@ -153,11 +153,12 @@ __global__ void __launch_bounds__(PT) permute_scatter(const int32_t *ids, int64_
     }
     if (threadIdx.x == 0) offsets_out[E] = used;
   }
-  // pad rows of the experts owned (e % nblk == b) by this block
-  for (int e = b; e < E; e += nblk) {
+  // pad rows of the experts owned (e % nblk == b) by this block, one expert
+  // per warp at a time
+  for (int e = b + warp * nblk; e < E; e += nblk * PW) {
     const int p0 = s_off[e] + s_tot[e];
     const int p1 = s_off[e] + (s_tot[e] + align - 1) / align * align;
-    for (int r = p0 + threadIdx.x; r < p1; r += PT) src_slot[r] = -1;
+    for (int r = p0 + lane; r < p1; r += 32) src_slot[r] = -1;
   }
   // 3. exclusive prefix over warps, seeded with the block's first row
   for (int e = threadIdx.x; e < E; e += PT) {

@@ -2,6 +2,7 @@
 (reframework/moe/__init__.py:8-18)."""
 
 from .fused import fused_experts, torch_fused_topk
+from .keys import translate_phimoe_keys
 from .moe_layer import CpuShuttle, FusedMoE
 from .offload_cache import ExpertOffloadCache, OffloadStats, Prediction
 

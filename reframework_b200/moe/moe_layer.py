@@ -43,6 +43,7 @@ import torch.nn as nn
 from .. import env
 from .. import kernels as K
 from .._lib import ACTIVATIONS, RfMoeError
+from .keys import expert_tensor
 from .offload_cache import ExpertOffloadCache, Prediction
 
 logger = logging.getLogger(__name__)
@@ -392,7 +393,9 @@ class FusedMoE(nn.Module):
         return result
 
     def load_state_dict(self, state_dict: Dict[str, torch.Tensor], *args, prefix: str = "", **kwargs) -> None:
-        """Copy HF-named tensors into the (bank-backed) parameters (moe_layer.py:644-660)."""
+        """Copy HF-named tensors into the (bank-backed) parameters (moe_layer.py:644-660).
+        Expert weights may also use the PhiMoE / Mixtral names ``w1`` / ``w3`` /
+        ``w2`` (checkpoint/loader.py:83-103)."""
         pre = f"{prefix}." if prefix else ""
         with torch.no_grad():
             g = f"{pre}gate.weight"
@@ -403,9 +406,9 @@ class FusedMoE(nn.Module):
                 p = f"{pre}experts.{e}"
                 for half, param in (("gate_proj", self.experts_w1[e][:I]), ("up_proj", self.experts_w1[e][I:]),
                                     ("down_proj", self.experts_w2[e])):
-                    key = f"{p}.{half}.weight"
-                    if key in state_dict:
-                        param.copy_(state_dict[key].detach().to(dtype=self.dtype))
+                    t = expert_tensor(state_dict, p, half)
+                    if t is not None:
+                        param.copy_(t.detach().to(dtype=self.dtype))
             if self.num_shared_experts:
                 Is = self.shared_intermediate_size
                 for s in range(self.num_shared_experts):

@@ -42,6 +42,7 @@ import torch.nn as nn
 
 from .. import kernels as K
 from .._lib import ACTIVATIONS, RfMoeError, check, lib
+from ..moe.keys import expert_tensor
 from ..moe.moe_layer import FusedMoE, _bank_view
 from . import dist as _dist
 from .eplb import Placement, place_experts, split_rows
@@ -544,9 +545,9 @@ class EPFusedMoE(nn.Module):
                 p = f"{pre}experts.{gg}"
                 for half, param in (("gate_proj", self.experts_w1[j][:I]), ("up_proj", self.experts_w1[j][I:]),
                                     ("down_proj", self.experts_w2[j])):
-                    key = f"{p}.{half}.weight"
-                    if key in state_dict:
-                        param.copy_(state_dict[key].detach().to(dtype=self.dtype))
+                    t = expert_tensor(state_dict, p, half)
+                    if t is not None:
+                        param.copy_(t.detach().to(dtype=self.dtype))
 
 
 @dataclass

@@ -26,4 +26,9 @@ struct GroupedGemmArgs {
 
 int launch_simt_grouped_gemm(const GroupedGemmArgs &g, bool gated, cudaStream_t st);
 
+// Dense out[M, ld_out] (fp32) = a[M, K] . w[N, K]^T on the tensor cores
+// (gemm_tc.cu); -1 when the shape or dtype is not handled there.
+int tc_dense_f32(const void *a, const void *w, float *out, int64_t M, int64_t N, int64_t Kdim,
+                 int64_t ld_out, int dtype, cudaStream_t st);
+
 }  // namespace rf

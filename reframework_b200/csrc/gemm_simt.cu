@@ -5,21 +5,80 @@
 // 16-bit shapes the TMA path cannot describe (rows not a multiple of 16 B).
 // Same contract as the tensor-core kernels: per listed expert e, rows
 // [offsets[e], offsets[e] + counts[e]) of `a` times the expert's weights.
-// 64x64 output tile per block, 16-deep k-steps through shared memory, each
-// thread 4x4 outputs (x2 for the gated kernel, which keeps gate and up tiles).
+// 64x64 output tile per block, 32-deep k-chunks through shared memory (16-byte
+// vector loads, the next chunk fetched into registers while the current one is
+// multiplied), each thread 4x4 outputs (x2 for the gated kernel, which keeps
+// gate and up tiles).
+#include <algorithm>
+#include <mutex>
+#include <string>
+#include <type_traits>
+
 #include "gemm.cuh"
 
 RF_DEVICE_ERROR_WORD();
 
 namespace {
 
-constexpr int BM = 64, BN = 64, BK = 16, NT = 256;
+constexpr int BM = 64, BN = 64, BK = 32, NT = 256;
 
-template <typename T, bool GATED>
+// Staging of one BK-deep chunk: the A tile (BM rows) and the weight tile(s)
+// (BN rows, x2 for the gated kernel) are read with 16-byte vectors along k
+// (VEC) or element by element, held raw in registers while the previous chunk
+// is multiplied, then stored transposed into shared memory.
+template <typename T, bool VEC>
+struct Stage {
+  static constexpr int E16 = 16 / sizeof(T);            // elements per 16-byte vector
+  static constexpr int PER = VEC ? E16 : 1;             // elements per load
+  static constexpr int LOADS = (BM * BK) / (NT * PER);  // loads per thread per tile
+  using Raw = typename std::conditional<VEC, uint4, float>::type;
+  Raw v[LOADS];
+  // element (r, kk) of load i of this thread
+  static __device__ __forceinline__ void coord(int i, int &r, int &kk) {
+    const int idx = threadIdx.x + i * NT;
+    r = idx / (BK / PER);
+    kk = (idx % (BK / PER)) * PER;
+  }
+  __device__ __forceinline__ void fetch(const T *base, int64_t ld, int rows, int kbeg, int kdim) {
+#pragma unroll
+    for (int i = 0; i < LOADS; ++i) {
+      int r, kk;
+      coord(i, r, kk);
+      const int k = kbeg + kk;
+      if constexpr (VEC) {
+        v[i] = (r < rows && k < kdim) ? __ldg(reinterpret_cast<const uint4 *>(base + r * ld + k))
+                                      : make_uint4(0u, 0u, 0u, 0u);
+      } else {
+        v[i] = (r < rows && k < kdim) ? rf::Cvt<T>::to_f(base[r * ld + k]) : 0.f;
+      }
+    }
+  }
+  __device__ __forceinline__ void store(float (*dst)[BM + 1]) const {
+#pragma unroll
+    for (int i = 0; i < LOADS; ++i) {
+      int r, kk;
+      coord(i, r, kk);
+      if constexpr (VEC) {
+        float f[8];
+        rf::unpack16<T>(v[i], f);
+#pragma unroll
+        for (int j = 0; j < PER; ++j) dst[kk + j][r] = f[j];
+      } else {
+        dst[kk][r] = v[i];
+      }
+    }
+  }
+};
+
+// One BM x BN output tile of one expert per block; thread (ty, tx) owns a
+// 4 x 4 patch (x2 for gated: gate and up).  Each output is one fp32 FMA chain
+// in ascending k.
+template <typename T, bool GATED, bool VEC>
 __global__ void __launch_bounds__(NT) simt_grouped_gemm(rf::GroupedGemmArgs p) {
-  __shared__ float sA[BK][BM + 4];
-  __shared__ float sG[BK][BN + 4];
-  __shared__ float sU[GATED ? BK : 1][GATED ? BN + 4 : 1];
+  __shared__ float sA[BK][BM + 1];
+  __shared__ float sG[BK][BN + 1];
+  __shared__ float sU[GATED ? BK : 1][GATED ? BN + 1 : 1];
+  static_assert(BM == BN, "staging assumes square tiles");
   const int g = blockIdx.y;
   const int e = p.groups ? p.groups[g] : g;
   if (e < 0 || e >= p.E) {
@@ -37,30 +96,27 @@ __global__ void __launch_bounds__(NT) simt_grouped_gemm(rf::GroupedGemmArgs p) {
     return;
   }
   const int n0 = blockIdx.x * BN;
-  const T *A = reinterpret_cast<const T *>(p.a);
+  const int ncols = min(BN, p.N - n0);
+  const T *A = reinterpret_cast<const T *>(p.a) + row0 * p.Kdim;
   const int64_t wstride = (int64_t)(GATED ? 2 : 1) * p.N * p.Kdim;
-  const T *W = reinterpret_cast<const T *>(p.w) + (int64_t)s * wstride;
+  const T *W = reinterpret_cast<const T *>(p.w) + (int64_t)s * wstride + (int64_t)n0 * p.Kdim;
   const T *Wu = W + (int64_t)p.N * p.Kdim;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
   float accg[4][4] = {}, accu[4][4] = {};
+  Stage<T, VEC> ra, rg, ru;
+  ra.fetch(A, p.Kdim, rows, 0, p.Kdim);
+  rg.fetch(W, p.Kdim, ncols, 0, p.Kdim);
+  if constexpr (GATED) ru.fetch(Wu, p.Kdim, ncols, 0, p.Kdim);
   for (int k0 = 0; k0 < p.Kdim; k0 += BK) {
-#pragma unroll
-    for (int i = 0; i < (BM * BK) / NT; ++i) {
-      const int idx = threadIdx.x + i * NT;
-      const int r = idx / BK, kk = idx % BK;
-      float v = 0.f;
-      if (r < rows && k0 + kk < p.Kdim) v = rf::Cvt<T>::to_f(A[(row0 + r) * p.Kdim + k0 + kk]);
-      sA[kk][r] = v;
-      const int n = r;
-      float gv = 0.f, uv = 0.f;
-      if (n0 + n < p.N && k0 + kk < p.Kdim) {
-        gv = rf::Cvt<T>::to_f(W[(int64_t)(n0 + n) * p.Kdim + k0 + kk]);
-        if (GATED) uv = rf::Cvt<T>::to_f(Wu[(int64_t)(n0 + n) * p.Kdim + k0 + kk]);
-      }
-      sG[kk][n] = gv;
-      if (GATED) sU[kk][n] = uv;
-    }
+    ra.store(sA);
+    rg.store(sG);
+    if constexpr (GATED) ru.store(sU);
     __syncthreads();
+    if (k0 + BK < p.Kdim) {
+      ra.fetch(A, p.Kdim, rows, k0 + BK, p.Kdim);
+      rg.fetch(W, p.Kdim, ncols, k0 + BK, p.Kdim);
+      if constexpr (GATED) ru.fetch(Wu, p.Kdim, ncols, k0 + BK, p.Kdim);
+    }
 #pragma unroll
     for (int kk = 0; kk < BK; ++kk) {
       float av[4], gv[4], uv[4];
@@ -95,16 +151,188 @@ __global__ void __launch_bounds__(NT) simt_grouped_gemm(rf::GroupedGemmArgs p) {
   }
 }
 
+// Skinny variant for experts with few rows (decode-sized groups): a block
+// covers SN output columns for every row of the expert, SR rows at a time;
+// thread (rg, c) owns column n0 + c for the RPT rows rg*RPT...  A 4-stage cp.async ring streams 32-deep k-chunks of the SN weight
+// rows (x2 gated) and of the SR activation rows into shared memory, both kept
+// k-contiguous ([col][k], [row][k]); the multiply reads 16-byte vectors along
+// k (weights: one per thread, activations: warp-wide broadcasts).  Each output
+// is the same ascending-k fp32 FMA chain as in the tiled kernel, so the two
+// kernels give the same bits.
+constexpr int SN = 64, SR = 16, SK = 32, SSTAGES = 4;
+constexpr int RPT = 4;                     // rows per thread
+constexpr int SNT = SN * (SR / RPT);       // threads per block
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool ok) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename T>
+struct SkinnyCfg {
+  static constexpr int E16 = 16 / (int)sizeof(T);   // elements per 16-byte vector
+  static constexpr int KV = SK / E16;               // vectors per row per chunk
+  static constexpr int LD = SK + E16;               // padded row length (elements), 16-byte multiple
+  static constexpr int ROW_BYTES = LD * (int)sizeof(T);
+};
+
+template <typename T, bool GATED>
+__global__ void __launch_bounds__(SNT) simt_skinny_gemm(rf::GroupedGemmArgs p) {
+  using C = SkinnyCfg<T>;
+  constexpr int NW = GATED ? 2 : 1;
+  constexpr int STAGE_BYTES = (NW * SN + SR) * C::ROW_BYTES;
+  extern __shared__ __align__(16) uint8_t s_raw[];
+  const int g = blockIdx.y;
+  const int e = p.groups ? p.groups[g] : g;
+  if (e < 0 || e >= p.E) {
+    if (threadIdx.x == 0) rf_report(RF_DEV_BAD_EXPERT_ID);
+    return;
+  }
+  const int cnt = p.counts[e];
+  if (cnt <= 0) return;
+  const int s = p.slot ? p.slot[e] : e;
+  if (s < 0 || s >= p.num_slots) {
+    if (threadIdx.x == 0) rf_report(RF_DEV_BAD_EXPERT_ID);
+    return;
+  }
+  const int n0 = blockIdx.x * SN;
+  const int c = threadIdx.x % SN, rg = threadIdx.x / SN;
+  const int64_t wstride = (int64_t)NW * p.N * p.Kdim;
+  const T *W = reinterpret_cast<const T *>(p.w) + (int64_t)s * wstride;
+  T *out = reinterpret_cast<T *>(p.out);
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(s_raw);
+  const int nchunks = (p.Kdim + SK - 1) / SK;
+  for (int m0 = 0; m0 < cnt; m0 += SR) {
+    const int rows = min(SR, cnt - m0);
+    const T *A = reinterpret_cast<const T *>(p.a) + ((int64_t)p.offsets[e] + m0) * p.Kdim;
+    // copies of chunk q into ring slot q % SSTAGES: rows [0, NW*SN) weights, then SR activation rows
+    auto issue = [&](int q) {
+      if (q < nchunks) {
+        const int k0 = q * SK;
+        const uint32_t st = sbase + (uint32_t)((q % SSTAGES) * STAGE_BYTES);
+        for (int v = threadIdx.x; v < (NW * SN + SR) * C::KV; v += SNT) {
+          const int row = v / C::KV, kv = v % C::KV, k = k0 + kv * C::E16;
+          const T *src;
+          bool ok;
+          if (row < NW * SN) {
+            const int m = row / SN, n = n0 + row % SN;
+            ok = n < p.N && k < p.Kdim;
+            src = ok ? W + ((int64_t)m * p.N + n) * p.Kdim + k : W;
+          } else {
+            const int r = row - NW * SN;
+            ok = r < rows && k < p.Kdim;
+            src = ok ? A + (int64_t)r * p.Kdim + k : A;
+          }
+          cp_async16(st + (uint32_t)(row * C::ROW_BYTES + kv * 16), src, ok);
+        }
+      }
+      cp_async_commit();  // one group per chunk slot, empty past the end
+    };
+    float accg[RPT], accu[GATED ? RPT : 1];
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) accg[r] = 0.f;
+#pragma unroll
+    for (int r = 0; r < (GATED ? RPT : 1); ++r) accu[r] = 0.f;
+#pragma unroll
+    for (int q = 0; q < SSTAGES - 1; ++q) issue(q);
+    for (int q = 0; q < nchunks; ++q) {
+      cp_async_wait<SSTAGES - 2>();
+      __syncthreads();  // chunk q landed for every thread; slot (q-1) % SSTAGES is free
+      issue(q + SSTAGES - 1);
+      const uint8_t *st = s_raw + (q % SSTAGES) * STAGE_BYTES;
+      const uint8_t *wg = st + c * C::ROW_BYTES;
+      const uint8_t *wu = st + (SN + c) * C::ROW_BYTES;
+      const uint8_t *xs = st + (NW * SN + rg * RPT) * C::ROW_BYTES;
+#pragma unroll
+      for (int kv = 0; kv < C::KV; ++kv) {
+        float fg[8], fu[8];
+        rf::unpack16<T>(*reinterpret_cast<const uint4 *>(wg + kv * 16), fg);
+        if constexpr (GATED) rf::unpack16<T>(*reinterpret_cast<const uint4 *>(wu + kv * 16), fu);
+#pragma unroll
+        for (int r = 0; r < RPT; ++r) {
+          float fx[8];
+          rf::unpack16<T>(*reinterpret_cast<const uint4 *>(xs + r * C::ROW_BYTES + kv * 16), fx);
+#pragma unroll
+          for (int j = 0; j < C::E16; ++j) {
+            accg[r] = fmaf(fx[j], fg[j], accg[r]);
+            if constexpr (GATED) accu[r] = fmaf(fx[j], fu[j], accu[r]);
+          }
+        }
+      }
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // the ring is reused by the next row chunk
+    const int n = n0 + c;
+    if (n < p.N) {
+      T *orow = out + ((int64_t)p.offsets[e] + m0 + rg * RPT) * p.N + n;
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) {
+        if (rg * RPT + r >= rows) break;
+        const float v = GATED ? rf::gated_elem<T>(p.act, accg[r], accu[GATED ? r : 0]) : accg[r];
+        orow[(int64_t)r * p.N] = rf::Cvt<T>::from_f(v);
+      }
+    }
+  }
+}
+
+template <typename T, bool GATED>
+int launch_skinny(const rf::GroupedGemmArgs &p, cudaStream_t st) {
+  constexpr int NW = GATED ? 2 : 1;
+  constexpr size_t smem = (size_t)SSTAGES * (NW * SN + SR) * SkinnyCfg<T>::ROW_BYTES;
+  auto kern = simt_skinny_gemm<T, GATED>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    if (smem > 48 * 1024)
+      attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
+  if (attr_err != cudaSuccess)
+    return rf::fail(RF_ERR_CUDA, std::string("CUDA-core grouped GEMM (skinny): ") + cudaGetErrorString(attr_err));
+  dim3 grid((p.N + SN - 1) / SN, p.n_groups);
+  kern<<<grid, SNT, smem, st>>>(p);
+  return rf::check_launch("CUDA-core grouped GEMM (skinny)");
+}
+
 template <bool GATED>
 int launch_t(const rf::GroupedGemmArgs &p, cudaStream_t st) {
   const int64_t mt = (p.rows_capacity + BM - 1) / BM;
   if (mt > 65535 || p.n_groups > 65535)
     return rf::fail(RF_ERR_UNSUPPORTED, "CUDA-core grouped GEMM: too many rows or groups");
   dim3 grid((p.N + BN - 1) / BN, p.n_groups, (unsigned)mt);
+  // 16-byte vector loads need every row start (and so Kdim * element size)
+  // and both base pointers 16-byte aligned
+  const bool vec = ((int64_t)p.Kdim * rf::dtype_size(p.dtype)) % 16 == 0 && (uintptr_t)p.a % 16 == 0 &&
+                   (uintptr_t)p.w % 16 == 0;
+  // few rows per expert (estimated from the row capacity the caller sized for
+  // the permute's padding): the skinny kernel
+  const int64_t groups = p.n_groups > 0 ? p.n_groups : 1;
+  int64_t pairs = p.rows_capacity - groups * 127;
+  if (pairs < 1) pairs = std::min<int64_t>(p.rows_capacity, groups);
+  if (vec && pairs < groups * 32 && p.N <= 65535 * (int64_t)SN) {
+    switch (p.dtype) {
+      case RF_F32: return launch_skinny<float, GATED>(p, st);
+      case RF_F16: return launch_skinny<__half, GATED>(p, st);
+      default: return launch_skinny<__nv_bfloat16, GATED>(p, st);
+    }
+  }
   switch (p.dtype) {
-    case RF_F32: simt_grouped_gemm<float, GATED><<<grid, NT, 0, st>>>(p); break;
-    case RF_F16: simt_grouped_gemm<__half, GATED><<<grid, NT, 0, st>>>(p); break;
-    default: simt_grouped_gemm<__nv_bfloat16, GATED><<<grid, NT, 0, st>>>(p); break;
+    case RF_F32:
+      if (vec) simt_grouped_gemm<float, GATED, true><<<grid, NT, 0, st>>>(p);
+      else simt_grouped_gemm<float, GATED, false><<<grid, NT, 0, st>>>(p);
+      break;
+    case RF_F16:
+      if (vec) simt_grouped_gemm<__half, GATED, true><<<grid, NT, 0, st>>>(p);
+      else simt_grouped_gemm<__half, GATED, false><<<grid, NT, 0, st>>>(p);
+      break;
+    default:
+      if (vec) simt_grouped_gemm<__nv_bfloat16, GATED, true><<<grid, NT, 0, st>>>(p);
+      else simt_grouped_gemm<__nv_bfloat16, GATED, false><<<grid, NT, 0, st>>>(p);
+      break;
   }
   return rf::check_launch("CUDA-core grouped GEMM");
 }

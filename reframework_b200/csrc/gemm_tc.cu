@@ -75,12 +75,14 @@ struct Cfg {
 };
 
 struct TcArgs {
-  const int32_t *offsets, *counts, *slot, *groups;
+  const int32_t *offsets, *counts, *slot, *groups;  // offsets == counts == NULL: one dense group
   int n_groups, E, num_slots;
+  int dense_rows; // rows of the dense group
   int Kdim;       // reduction length
   int N;          // output columns
   int n_tiles_n;  // n-blocks per expert
   void *out;
+  int64_t out_ld; // output row stride (elements)
   int act;
 };
 
@@ -222,7 +224,8 @@ __host__ __device__ constexpr uint32_t instr_desc() {
          ((uint32_t)(BM >> 4) << 24);
 }
 
-template <typename T, bool GATED, int ACT, int BN_>
+// OUTF32 (down kernel only): the accumulator is stored as fp32, unrounded.
+template <typename T, bool GATED, int ACT, int BN_, bool OUTF32 = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA32,
                     const __grid_constant__ CUtensorMap tmB, const TcArgs p) {
@@ -276,8 +279,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (e >= 0 && e < p.E) {
       s = p.slot ? p.slot[e] : e;
       if (s >= 0 && s < p.num_slots) {
-        row0 = p.offsets[e];
-        cnt = p.counts[e];
+        row0 = p.offsets ? p.offsets[e] : 0;
+        cnt = p.counts ? p.counts[e] : p.dense_rows;
         tiles = ((cnt + BM - 1) / BM) * p.n_tiles_n;
       } else {
         rf_report(RF_DEV_BAD_EXPERT_ID);
@@ -436,7 +439,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc_fence_after();
       const uint32_t tb = tmem_base + ((uint32_t)(wq * 32) << 16) + (uint32_t)(acc * BN);
       const bool row_ok = r < rows;
-      T *orow = out + (int64_t)(row0 + r) * p.N;
+      T *orow = out + (int64_t)(row0 + r) * p.out_ld;
       if (GATED) {
         const int n0 = nb * (BN / 2);
 #pragma unroll 1
@@ -460,6 +463,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               if (col < p.N)
                 *reinterpret_cast<uint4 *>(orow + col) =
                     make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+            }
+          }
+        }
+      } else if (OUTF32) {
+        // fp32 rows of out_ld (a multiple of 4) columns; columns in
+        // [N, out_ld) hold the zero products of the out-of-range weight rows
+        const int n0 = nb * BN;
+        float *orowf = reinterpret_cast<float *>(p.out) + (int64_t)(row0 + r) * p.out_ld;
+#pragma unroll 1
+        for (int c = part * 32; c < BN; c += 32 * EPI_SPLIT) {
+          uint32_t v32[32];
+          tmem_ld32(tb + c, v32);
+          tmem_ld_wait();
+          if (row_ok) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const int col = n0 + c + 4 * v;
+              if (col < p.out_ld)
+                *reinterpret_cast<uint4 *>(orowf + col) =
+                    make_uint4(v32[4 * v], v32[4 * v + 1], v32[4 * v + 2], v32[4 * v + 3]);
             }
           }
         }
@@ -558,6 +581,8 @@ int launch_tc_t(const rf::GroupedGemmArgs &g, const CUtensorMap &ma, const CUten
   p.N = g.N;
   p.n_tiles_n = GATED ? (g.N + BN / 2 - 1) / (BN / 2) : (g.N + BN - 1) / BN;
   p.out = g.out;
+  p.out_ld = g.N;
+  p.dense_rows = 0;
   p.act = g.act;
   kern<<<rf::num_sms(), NTHREADS, C::SMEM_BYTES, st>>>(ma, ma32, mb, p);
   return rf::check_launch(GATED ? "tensor-core gated GEMM" : "tensor-core down GEMM");
@@ -637,6 +662,78 @@ int try_tc(const rf::GroupedGemmArgs &g, bool gated, cudaStream_t st, int *rc) {
     *rc = launch_tc_dt<__half>(g, gated, bn, ma, ma32, mb, st);
   return 1;
 }
+
+template <typename T, int BN>
+int launch_dense(const CUtensorMap &ma, const CUtensorMap &ma32, const CUtensorMap &mb, const TcArgs &p,
+                 int64_t M, cudaStream_t st) {
+  using C = Cfg<BN>;
+  auto kern = tc_grouped_gemm<T, false, 0, BN, true>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess)
+    return rf::fail(RF_ERR_CUDA, std::string("tensor-core GEMM: ") + cudaGetErrorString(attr_err));
+  const int64_t tiles = (M + BM - 1) / BM * p.n_tiles_n;
+  const int grid = (int)std::min<int64_t>(tiles, rf::num_sms());
+  kern<<<grid, NTHREADS, C::SMEM_BYTES, st>>>(ma, ma32, mb, p);
+  return rf::check_launch("tensor-core dense GEMM (fp32 out)");
+}
+
+}  // namespace
+
+namespace rf {
+// out[m, n] = sum_k a[m, k] * w[n, k] for m < M, n < N, fp32 accumulation
+// on the tensor cores, stored unrounded as fp32 rows of ld_out (a multiple of
+// 4, >= N) columns.  a [M, K] and w [N, K] are 16-bit of the same dtype.
+// Returns -1 when the tensor-core path does not take the shape (the caller
+// then runs its CUDA-core code), else a status.  Each output is one fixed
+// sequence of MMAs over k, independent of M and of the other rows.
+int tc_dense_f32(const void *a, const void *w, float *out, int64_t M, int64_t N, int64_t Kdim,
+                 int64_t ld_out, int dtype, cudaStream_t st) {
+  if (g_gemm_impl == 1) return -1;
+  if (dtype != RF_BF16 && dtype != RF_F16) return -1;
+  if (M <= 0 || N <= 0 || Kdim % 8 || ld_out % 4 || ld_out < N || M >= ((int64_t)1 << 31) ||
+      Kdim >= (1 << 30) || N >= (1 << 30))
+    return -1;
+  if ((uintptr_t)a % 16 || (uintptr_t)w % 16 || (uintptr_t)out % 16) return -1;
+  if (!encode_fn()) return rf::fail(RF_ERR_CUDA, "tensor-core GEMM: cuTensorMapEncodeTiled is unavailable");
+  const int bn = N <= 64 ? 64 : N <= 128 ? 128 : 256;
+  CUtensorMap ma, ma32, mb;
+  const cuuint64_t dA[2] = {(cuuint64_t)Kdim, (cuuint64_t)M};
+  const cuuint64_t sAs[1] = {(cuuint64_t)Kdim * 2};
+  const cuuint32_t bA[2] = {BK, BM};
+  const cuuint32_t bA32[2] = {BK, BM_SMALL};
+  const cuuint64_t dB[3] = {(cuuint64_t)Kdim, (cuuint64_t)N, 1};
+  const cuuint64_t sB[2] = {(cuuint64_t)Kdim * 2, (cuuint64_t)N * Kdim * 2};
+  const cuuint32_t bB[3] = {BK, (cuuint32_t)bn, 1};
+  if (!(encode(&ma, dtype, 2, a, dA, sAs, bA) && encode(&ma32, dtype, 2, a, dA, sAs, bA32) &&
+        encode(&mb, dtype, 3, w, dB, sB, bB)))
+    return rf::fail(RF_ERR_CUDA, "tensor-core GEMM: cuTensorMapEncodeTiled rejected the operands");
+  TcArgs p{};
+  p.n_groups = 1;
+  p.E = 1;
+  p.num_slots = 1;
+  p.dense_rows = (int)M;
+  p.Kdim = (int)Kdim;
+  p.N = (int)N;
+  p.n_tiles_n = (int)((N + bn - 1) / bn);
+  p.out = out;
+  p.out_ld = ld_out;
+  p.act = 0;
+  if (dtype == RF_BF16) {
+    if (bn == 64) return launch_dense<__nv_bfloat16, 64>(ma, ma32, mb, p, M, st);
+    if (bn == 128) return launch_dense<__nv_bfloat16, 128>(ma, ma32, mb, p, M, st);
+    return launch_dense<__nv_bfloat16, 256>(ma, ma32, mb, p, M, st);
+  }
+  if (bn == 64) return launch_dense<__half, 64>(ma, ma32, mb, p, M, st);
+  if (bn == 128) return launch_dense<__half, 128>(ma, ma32, mb, p, M, st);
+  return launch_dense<__half, 256>(ma, ma32, mb, p, M, st);
+}
+}  // namespace rf
+
+namespace {
 
 int grouped_gemm(const void *a, const void *w, void *out, const int32_t *offsets,
                  const int32_t *counts, const int32_t *slot, const int32_t *groups,

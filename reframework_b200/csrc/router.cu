@@ -6,9 +6,14 @@
 //   dtype and/or biased), p = softmax(logits) in fp32, top-k of p (descending,
 //   ties to the lower expert id), w = p / sum(top-k p) when renormalising.
 //
-// Two launches:
-//   router_logits_kernel  tiled CUDA-core GEMM.  A block computes a tile of
-//       TT tokens x ET experts over one 256-wide slice of H (the slices give
+// Two launches.  The logits come from one of:
+//   the tensor cores (gemm_tc.cu, dense fp32-output mode) when x and the gate
+//       share a 16-bit dtype and a shared gate, if any, is the row right after
+//       the gate's E rows: one fp32 row of round_up(E', 4) logits per token,
+//       each a fixed sequence of MMAs over H (independent of T);
+//   router_logits_kernel  otherwise (fp32 layers): a tiled CUDA-core GEMM.
+//       A block computes a tile of TT tokens x ET experts over one 256-wide
+//       slice of H (the slices give
 //       parallelism when there are few tokens); x and gate chunks are staged
 //       in shared memory as fp32, so each gate element is read once per tile
 //       of TT tokens instead of once per token.  Each output is a sequential
@@ -20,7 +25,7 @@
 //       order (deterministic), applies rounding / bias, softmax, top-k,
 //       renormalisation or the entropy-adaptive rule, writes weights and ids.
 // The shared-expert gate (sigmoid(x . w_s)) is one more "expert" column.
-#include "common.cuh"
+#include "gemm.cuh"
 
 RF_DEVICE_ERROR_WORD();
 
@@ -198,7 +203,7 @@ __global__ void __launch_bounds__(THREADS) router_logits_kernel(LogitsArgs a) {
 }
 
 struct TopkArgs {
-  const float *partial;  // [splits][T][Ec]  (or the logits themselves when direct)
+  const float *partial;  // [splits][T][ld] fp32 partial logits (columns E.. include the shared gate)
   const void *x_logits;  // gate == NULL: x holds the [T,E] logits
   int x_dtype;
   const float *bias;
@@ -209,6 +214,7 @@ struct TopkArgs {
   float *logits_out;
   int64_t T;
   int E, Ec, K, ksplit;
+  int64_t ld;            // row stride of partial (>= Ec)
   int has_shared;
   int renormalize, round_dtype, entropy_k_min;
 };
@@ -247,7 +253,7 @@ __global__ void __launch_bounds__(TK_WARPS * 32) router_topk_kernel(TopkArgs a) 
     for (int e = lane; e < a.E; e += 32) {
       float v;
       if (a.partial) {
-        v = sum_slices(a.partial + t * a.Ec + e, a.T * a.Ec, a.ksplit);
+        v = sum_slices(a.partial + t * a.ld + e, a.T * a.ld, a.ksplit);
       } else {
         v = load_logit<TX>(a, t, e);
       }
@@ -261,7 +267,7 @@ __global__ void __launch_bounds__(TK_WARPS * 32) router_topk_kernel(TopkArgs a) 
       m = fmaxf(m, v);
     }
     if (a.has_shared && lane == 0) {
-      const float z = sum_slices(a.partial + t * a.Ec + a.E, a.T * a.Ec, a.ksplit);
+      const float z = sum_slices(a.partial + t * a.ld + a.E, a.T * a.ld, a.ksplit);
       a.shared_scale[t] = 1.0f / (1.0f + expf(-z));
     }
 #pragma unroll
@@ -381,9 +387,13 @@ void launch_logits_tg(const LogitsArgs &a, const Plan &p, int gate_dtype, cudaSt
 
 extern "C" size_t rf_moe_router_workspace_size(int64_t T, int64_t H, int64_t E, int has_shared_gate) {
   if (T <= 0 || H <= 0 || E <= 0) return 256;
-  const int Ec = (int)E + (has_shared_gate ? 1 : 0);
+  const int64_t Ec = E + (has_shared_gate ? 1 : 0);
   const size_t slices = (size_t)((H + SLICE - 1) / SLICE);
-  return slices * (size_t)T * (size_t)Ec * sizeof(float) + 256;
+  // CUDA-core path: per-slice partials; tensor-core path: one row of
+  // round_up(Ec, 4) logits per token
+  const size_t cuda_core = slices * (size_t)T * (size_t)Ec;
+  const size_t tensor = (size_t)T * (size_t)((Ec + 3) / 4 * 4);
+  return (cuda_core > tensor ? cuda_core : tensor) * sizeof(float) + 256;
 }
 
 extern "C" int rf_moe_router_topk(const void *x, int x_dtype, const void *gate, int gate_dtype,
@@ -427,6 +437,7 @@ extern "C" int rf_moe_router_topk(const void *x, int x_dtype, const void *gate, 
   b.Ec = Ec;
   b.K = (int)K;
   b.ksplit = 1;
+  b.ld = Ec;
   b.has_shared = shared_gate ? 1 : 0;
   b.renormalize = renormalize;
   b.round_dtype = round_dtype;
@@ -437,16 +448,35 @@ extern "C" int rf_moe_router_topk(const void *x, int x_dtype, const void *gate, 
     RF_CHECK_ARG(workspace && workspace_bytes >= need && ((uintptr_t)workspace % 16) == 0,
                  "rf_moe_router_topk: workspace too small (see rf_moe_router_workspace_size)");
     RF_CHECK_ARG(p.ttiles <= 0x7fffffff && p.slices <= 65535, "rf_moe_router_topk: too many tokens");
-    LogitsArgs a{x, gate, shared_gate, reinterpret_cast<float *>(workspace), T, (int)H, (int)E, Ec};
-    switch (x_dtype) {
-      case RF_F32: launch_logits_tg<float>(a, p, gate_dtype, st); break;
-      case RF_F16: launch_logits_tg<__half>(a, p, gate_dtype, st); break;
-      default: launch_logits_tg<__nv_bfloat16>(a, p, gate_dtype, st); break;
+    // Tensor cores when x and the gate share a 16-bit dtype and the shared
+    // gate (if any) is the row right after the gate's E rows: logits as one
+    // fp32 [T, ld] block, each a fixed MMA sequence over H (so, again, the
+    // same bits whatever T is).  Otherwise the CUDA-core slices.
+    const size_t esz = (size_t)rf::dtype_size(gate_dtype);
+    const bool adjacent = !shared_gate ||
+                          (const char *)shared_gate == (const char *)gate + (size_t)E * (size_t)H * esz;
+    const int64_t ld = (Ec + 3) / 4 * 4;
+    int rc = -1;
+    if (x_dtype == gate_dtype && adjacent && workspace_bytes >= (size_t)T * (size_t)ld * sizeof(float))
+      rc = rf::tc_dense_f32(x, gate, reinterpret_cast<float *>(workspace), T, Ec, H, ld, x_dtype, st);
+    if (rc > 0) return rc;
+    if (rc == 0) {
+      b.partial = reinterpret_cast<const float *>(workspace);
+      b.ksplit = 1;
+      b.ld = ld;
+    } else {
+      LogitsArgs a{x, gate, shared_gate, reinterpret_cast<float *>(workspace), T, (int)H, (int)E, Ec};
+      switch (x_dtype) {
+        case RF_F32: launch_logits_tg<float>(a, p, gate_dtype, st); break;
+        case RF_F16: launch_logits_tg<__half>(a, p, gate_dtype, st); break;
+        default: launch_logits_tg<__nv_bfloat16>(a, p, gate_dtype, st); break;
+      }
+      rc = rf::check_launch("rf_moe_router_topk(logits)");
+      if (rc) return rc;
+      b.partial = a.partial;
+      b.ksplit = p.slices;
+      b.ld = Ec;
     }
-    int rc = rf::check_launch("rf_moe_router_topk(logits)");
-    if (rc) return rc;
-    b.partial = a.partial;
-    b.ksplit = p.slices;
   }
   int64_t blocks = (T + TK_WARPS - 1) / TK_WARPS;
   const int64_t cap = (int64_t)rf::num_sms() * 8;

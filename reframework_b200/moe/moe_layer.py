@@ -100,6 +100,25 @@ def _bank_view(params: Sequence[torch.Tensor]) -> Optional[torch.Tensor]:
     return bank
 
 
+def adjacent_router_weights(owner, gate: torch.Tensor,
+                            shared_gate: Optional[torch.Tensor]) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """The router gate and, with a gated shared expert, its gate vector as the
+    row right after the gate's E rows of one [E+1, H] tensor cached on
+    ``owner._router_cat`` (the router then computes all E+1 logits in one
+    tensor-core GEMM).  Rebuilt when either parameter is edited or moved."""
+    g = gate.detach()
+    if shared_gate is None:
+        return g, None
+    sg = shared_gate.detach()
+    key = (g.data_ptr(), g._version, sg.data_ptr(), sg._version, g.dtype)
+    cached = getattr(owner, "_router_cat", None)
+    if cached is None or cached[0] != key:
+        cached = (key, torch.cat([g, sg.reshape(1, -1).to(g.dtype)], 0).contiguous())
+        owner._router_cat = cached
+    cat = cached[1]
+    return cat[:-1], cat[-1]
+
+
 class FusedMoE(nn.Module):
     """A routed MoE block: ``gate`` -> top-k -> grouped expert GEMMs -> combine."""
 
@@ -138,6 +157,7 @@ class FusedMoE(nn.Module):
             self.shared_w1 = self.shared_w2 = self.shared_gate = None
         self._bank_cache: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
         self._shared_cache: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
+        self._router_cat: Optional[Tuple[tuple, torch.Tensor]] = None
         self._cache: Optional[ExpertOffloadCache] = None
         self._cpu_split_enabled = False
         self._predictor: Optional[Prediction] = None
@@ -170,12 +190,14 @@ class FusedMoE(nn.Module):
     def _apply(self, fn, recurse=True):
         self._bank_cache = None
         self._shared_cache = None
+        self._router_cat = None
         return super()._apply(fn, recurse)
 
     def invalidate_banks(self) -> None:
         """Call after replacing an expert parameter's ``.data`` directly."""
         self._bank_cache = None
         self._shared_cache = None
+        self._router_cat = None
 
     def _resident_banks(self) -> Tuple[torch.Tensor, torch.Tensor]:
         c = self._bank_cache
@@ -260,12 +282,16 @@ class FusedMoE(nn.Module):
             return None
         return self.dtype
 
+    def _router_weights(self) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+        sg = self.shared_gate if self.num_shared_experts else None
+        return adjacent_router_weights(self, self.gate, sg)
+
     def _router(self, x2: torch.Tensor, *, ids32: bool, ids64: bool):
         ek = self.entropy_k_min if self.entropy_adaptive_k else 0
-        sg = self.shared_gate if self.num_shared_experts else None
-        return K.router_topk(x2, self.gate.detach(), self.top_k, renormalize=self.renormalize,
+        gate, sg = self._router_weights()
+        return K.router_topk(x2, gate, self.top_k, renormalize=self.renormalize,
                              bias=self.router_bias, round_dtype=self._round_dtype(), entropy_k_min=ek,
-                             shared_gate=None if sg is None else sg.detach(), ids32=ids32, ids64=ids64)
+                             shared_gate=sg, ids32=ids32, ids64=ids64)
 
     def _prep(self, x: torch.Tensor) -> torch.Tensor:
         if not x.is_cuda:

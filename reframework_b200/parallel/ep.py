@@ -43,7 +43,7 @@ import torch.nn as nn
 from .. import kernels as K
 from .._lib import ACTIVATIONS, RfMoeError, check, lib
 from ..moe.keys import expert_tensor
-from ..moe.moe_layer import FusedMoE, _bank_view
+from ..moe.moe_layer import FusedMoE, _bank_view, adjacent_router_weights
 from . import dist as _dist
 from .eplb import Placement, place_experts, split_rows
 
@@ -436,9 +436,10 @@ class EPFusedMoE(nn.Module):
             self.trace = []
         self._mark("start")
         if T > 0:
-            w, ids32, _, _, sscale = K.router_topk(x2, self.gate.detach(), Kk, renormalize=self.renormalize,
+            gate, sg = adjacent_router_weights(self, self.gate, self._shared_gate)
+            w, ids32, _, _, sscale = K.router_topk(x2, gate, Kk, renormalize=self.renormalize,
                                                    bias=self.router_bias, round_dtype=rdt, entropy_k_min=ek,
-                                                   shared_gate=self._shared_gate)
+                                                   shared_gate=sg)
             p = K.permute(ids32, E, align=1, x=x2)
             counts = p.counts
         else:

@@ -76,6 +76,49 @@ def test_router_shared_gate_sigmoid():
     torch.testing.assert_close(ss.cpu(), ref, rtol=1e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("E,H", [(8, 4096), (60, 2048), (64, 2048), (130, 512)])
+def test_router_tensor_core_path_matches_cuda_cores(E, H):
+    """16-bit gates run the logits on the tensor cores; the CUDA-core kernel
+    (forced with set_gemm_impl(1)) computes the same fp32 sums in another
+    order: logits agree to fp32 rounding, the shared gate too, and top-k only
+    differs where two probabilities are within that rounding."""
+    g = torch.Generator().manual_seed(E + H)
+    T = 333
+    x = torch.randn(T, H, generator=g).bfloat16().to(DEV)
+    cat = (torch.randn(E + 1, H, generator=g) * 0.02).bfloat16().to(DEV)
+    gate, sg = cat[:E], cat[E]            # adjacent: the tensor-core path
+    res = []
+    for impl in (0, 1):
+        _lib.set_gemm_impl(impl)
+        res.append(K.router_topk(x, gate, 4, shared_gate=sg, want_logits=True, ids64=True))
+    (w0, _, i0, l0, s0), (w1, _, i1, l1, s1) = res
+    scale = l1.abs().max().item()
+    assert (l0 - l1).abs().max().item() <= 1e-5 * scale
+    torch.testing.assert_close(s0, s1, rtol=1e-5, atol=1e-6)
+    p = torch.softmax(l1, -1)
+    kth = p.topk(5, -1).values
+    near_tie = (kth[:, 3] - kth[:, 4]) < 1e-5
+    same = (i0 == i1).all(1)
+    assert bool((same | near_tie).all())
+
+
+@pytest.mark.parametrize("dtype,E", [(torch.bfloat16, 61), (torch.float16, 8), (torch.float32, 61)])
+def test_router_is_batch_invariant(dtype, E):
+    """A token's logits, ids and weights do not depend on how many other tokens
+    share the call (tensor-core path for 16-bit, CUDA-core slices for fp32)."""
+    g = torch.Generator().manual_seed(7)
+    H = 1024
+    x = torch.randn(300, H, generator=g).to(dtype).to(DEV)
+    cat = (torch.randn(E + 1, H, generator=g) * 0.02).to(dtype).to(DEV)
+    full = K.router_topk(x, cat[:E], 4, shared_gate=cat[E], want_logits=True, ids64=True)
+    for lo, hi in ((0, 37), (123, 300), (5, 6)):
+        part = K.router_topk(x[lo:hi].contiguous(), cat[:E], 4, shared_gate=cat[E], want_logits=True,
+                             ids64=True)
+        for a, b in zip(full, part):
+            if a is not None:
+                assert torch.equal(a[lo:hi], b)
+
+
 @pytest.mark.parametrize("name", ["c1_tiny_fp32", "c2_mini_bf16", "c3_mini_bf16", "c4_mini_bf16", "fp16_default"])
 def test_permute_matches_reference_order(name):
     rec = load_golden(name)
@@ -260,6 +303,35 @@ def test_fp32_grouped_gemm_tolerance():
         hr = O.gated_act_and_mul("silu", xa @ w1[e].double().t())
         yr = hr @ w2[e].double().t()
         assert max_rel(y.cpu()[offs[e]:offs[e] + c], yr) < 1e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("counts", [[20, 0, 75, 33], [1, 2, 3, 17, 0, 16, 5, 40]])
+def test_simt_skinny_and_tiled_kernels_agree_bitwise(dtype, counts):
+    """The CUDA-core path picks its skinny kernel when the row capacity implies
+    few rows per expert and its tiled kernel otherwise; both run the same fp32
+    FMA chain per output, so a larger buffer (tiled) gives the same bits."""
+    _lib.set_gemm_impl(1)
+    g = torch.Generator().manual_seed(len(counts))
+    H, I = 512, 704
+    E = len(counts)
+    offs = _segments(counts)
+    a = torch.randn(offs[-1], H, generator=g).to(dtype).to(DEV)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.05).to(dtype).to(DEV)
+    w2 = (torch.randn(E, H, I, generator=g) * 0.05).to(dtype).to(DEV)
+    off_t = torch.tensor(offs, dtype=torch.int32, device=DEV)
+    cnt_t = torch.tensor(counts, dtype=torch.int32, device=DEV)
+    res = []
+    for extra in (0, 16384):  # capacity for few rows -> skinny; a large one -> tiled
+        rows = offs[-1] + extra
+        ap = torch.zeros(rows, H, dtype=dtype, device=DEV)
+        ap[:offs[-1]] = a
+        h = torch.zeros(rows, I, dtype=dtype, device=DEV)
+        y = torch.zeros(rows, H, dtype=dtype, device=DEV)
+        K.grouped_gemm_gated(ap, w1, off_t, cnt_t, h)
+        K.grouped_gemm_down(h, w2, off_t, cnt_t, y)
+        res.append((h[:offs[-1]], y[:offs[-1]]))
+    assert torch.equal(res[0][0], res[1][0]) and torch.equal(res[0][1], res[1][1])
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])

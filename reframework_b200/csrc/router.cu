@@ -13,8 +13,8 @@
 //       each a fixed sequence of MMAs over H (independent of T);
 //   router_logits_kernel  otherwise (fp32 layers): a tiled CUDA-core GEMM.
 //       A block computes a tile of TT tokens x ET experts over one 256-wide
-//       slice of H (the slices give
-//       parallelism when there are few tokens); x and gate chunks are staged
+//       slice of H (the slices give parallelism when there are few tokens);
+//       x and gate chunks are staged
 //       in shared memory as fp32, so each gate element is read once per tile
 //       of TT tokens instead of once per token.  Each output is a sequential
 //       fp32 FMA chain over its slice; slices go to a partials buffer.  The

@@ -28,6 +28,8 @@
  *                           chunk packing, for EP dispatch/combine)
  *   rf_moe_grouped_gemm_gated  reframework/moe/fused.py:81-82 (x @ w1[e].t(),
  *                           gated_act_and_mul) + reframework/layers/activation.py:15-59
+ *   rf_moe_grouped_gemm_gated_gather  the same with fused.py:80 (hidden_states[tok])
+ *                           folded into the operand load
  *   rf_moe_grouped_gemm_down   reframework/moe/fused.py:83 (inter @ w2[e].t())
  *   rf_moe_combine          reframework/moe/fused.py:84-86 (y * w, index_add_)
  *                           + reframework/layers/norm.py:43-53 (residual add, opt-in)
@@ -203,6 +205,28 @@ int rf_moe_grouped_gemm_gated(const void *a, const void *w1, void *h,
                               int64_t E, int64_t num_slots, int64_t rows_capacity,
                               int64_t H, int64_t I, int dtype, int activation,
                               rf_stream_t stream);
+
+/*
+ * K3 with the row gather fused into the operand load: the same h as
+ * rf_moe_grouped_gemm_gated computes from a = x_perm, but row r of the
+ * permuted layout is read straight from the token rows,
+ *   a[r] = x[src_slot[r] / topk]      (src_slot from rf_moe_permute; pad rows,
+ *                                       src_slot = -1, are never stored)
+ * with TMA tile::gather4 (four token rows per copy), so the expert-ordered
+ * activation copy (T*K rows) is neither written nor read.  x [x_rows, H].
+ * Tensor cores only (bf16/fp16, H % 8 == 0, I % 8 == 0, 16-byte aligned
+ * pointers); otherwise returns RF_ERR_UNSUPPORTED and the caller gathers with
+ * rf_moe_permute(..., x_perm) and calls rf_moe_grouped_gemm_gated.
+ * Replaces reframework/moe/fused.py:80-82 (hidden_states[tok] @ w1[e].t() +
+ * gated_act_and_mul).
+ */
+int rf_moe_grouped_gemm_gated_gather(const void *x, int64_t x_rows, const int32_t *src_slot,
+                                     int64_t topk, const void *w1, void *h,
+                                     const int32_t *expert_offsets, const int32_t *expert_counts,
+                                     const int32_t *expert_slot, const int32_t *groups,
+                                     int64_t n_groups, int64_t E, int64_t num_slots,
+                                     int64_t rows_capacity, int64_t H, int64_t I, int dtype,
+                                     int activation, rf_stream_t stream);
 
 /*
  * Selects the grouped-GEMM implementation for subsequent calls of this

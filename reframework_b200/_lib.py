@@ -49,6 +49,9 @@ _SIGNATURES = {
     "rf_moe_grouped_gemm_gated": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                          _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64,
                                          _int, _int, _c_void_p]),
+    "rf_moe_grouped_gemm_gated_gather": (_int, [_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p,
+                                                _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64,
+                                                _i64, _int, _int, _c_void_p]),
     "rf_moe_grouped_gemm_down": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                         _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64,
                                         _int, _c_void_p]),
@@ -121,5 +124,16 @@ def device_status() -> int:
     return code.value
 
 
+_gemm_impl = 0
+RF_ERR_UNSUPPORTED = 2
+
+
 def set_gemm_impl(impl: int) -> None:
+    global _gemm_impl
     check(lib().rf_moe_set_gemm_impl(int(impl)), "rf_moe_set_gemm_impl")
+    _gemm_impl = int(impl)
+
+
+def gemm_impl() -> int:
+    """The grouped-GEMM implementation selected by set_gemm_impl (0 = automatic)."""
+    return _gemm_impl

@@ -22,6 +22,11 @@ struct GroupedGemmArgs {
   int N;                         // output columns (I for gated, H for down)
   int dtype;
   int act;
+  // gather mode (gated, tensor cores only): `a` is [a_rows, Kdim] token rows
+  // and permuted row r reads a[gather_src[r] / gather_div] (-1: pad row)
+  const int32_t *gather_src = nullptr;
+  int gather_div = 1;
+  int64_t a_rows = 0;
 };
 
 int launch_simt_grouped_gemm(const GroupedGemmArgs &g, bool gated, cudaStream_t st);

@@ -84,6 +84,10 @@ struct TcArgs {
   void *out;
   int64_t out_ld; // output row stride (elements)
   int act;
+  // gather mode: A row r of the permuted layout is row gather_src[r] / gather_div
+  // of the tensor behind the A map (the token's activation row); -1 = pad row
+  const int32_t *gather_src;
+  int gather_div;
 };
 
 // ------------------------------------------------------------------ PTX
@@ -156,6 +160,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
       "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+// Four rows of a 2-D tensor (row indices r0..r3, one 64-column box each) into
+// four consecutive 128-byte smem rows (Blackwell tile::gather4; the tensor
+// map's box is 64 x 1).
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0,
+                                            int r0, int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_alloc(uint32_t holder, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(holder),
                "r"(ncols)
@@ -225,7 +240,9 @@ __host__ __device__ constexpr uint32_t instr_desc() {
 }
 
 // OUTF32 (down kernel only): the accumulator is stored as fp32, unrounded.
-template <typename T, bool GATED, int ACT, int BN_, bool OUTF32 = false>
+// GATHER: A rows are fetched from the token rows with TMA gather4 (no
+// expert-ordered activation copy in HBM).
+template <typename T, bool GATED, int ACT, int BN_, bool OUTF32 = false, bool GATHER = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA32,
                     const __grid_constant__ CUtensorMap tmB, const TcArgs p) {
@@ -340,45 +357,69 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        int row0, rows, nb, s;
-        decode(t, row0, rows, nb, s);
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(EMPTY(stage), phase ^ 1u, abort_flag)) {
-            ok = false;
-            break;
-          }
-          // a tile of at most 32 valid rows loads only those 32 A rows; the
-          // MMA still reads 128 (rows past the tile's count are never stored)
+    // lane 0 waits for a free stage, posts the expected bytes and issues the
+    // B (and, without gather, the A) copies; in gather mode lane i then
+    // fetches A rows 4i..4i+3 of the tile with one gather4
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      int row0, rows, nb, s;
+      decode(t, row0, rows, nb, s);
+      int src[4] = {0, 0, 0, 0};
+      int groups4 = 0;
+      if (GATHER) {
+        groups4 = (rows + 3) >> 2;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int r = 4 * lane + j;
+          const int sl = r < rows ? p.gather_src[row0 + r] : -1;
+          src[j] = sl >= 0 ? sl / p.gather_div : 0;  // pad rows read token 0; never stored
+        }
+      }
+      for (int kb = 0; kb < num_kb; ++kb) {
+        int go = 1;
+        if (lane == 0) go = mbar_wait(EMPTY(stage), phase ^ 1u, abort_flag) ? 1 : 0;
+        go = __shfl_sync(0xffffffffu, go, 0);
+        if (!go) {
+          ok = false;
+          break;
+        }
+        const uint32_t a_dst = smem_u32(sA + stage * A_BYTES);
+        const uint32_t b_dst = smem_u32(sB + stage * B_BYTES);
+        if (lane == 0) {
+          // a tile of at most 32 valid rows loads only those rows; the MMA
+          // still reads 128 (rows past the tile's count are never stored)
           const bool small = rows <= BM_SMALL;
-          mbar_expect_tx(FULL(stage), small ? STAGE_BYTES - A_BYTES + A_BYTES / (BM / BM_SMALL) : STAGE_BYTES);
-          const uint32_t a_dst = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_dst = smem_u32(sB + stage * B_BYTES);
-          tma_load_2d(a_dst, small ? &tmA32 : &tmA, FULL(stage), kb * BK, row0);
+          const uint32_t a_bytes =
+              GATHER ? (uint32_t)groups4 * 512u : (small ? (uint32_t)(A_BYTES / (BM / BM_SMALL)) : (uint32_t)A_BYTES);
+          mbar_expect_tx(FULL(stage), a_bytes + (uint32_t)B_BYTES);
+          if (!GATHER) tma_load_2d(a_dst, small ? &tmA32 : &tmA, FULL(stage), kb * BK, row0);
           if (GATED) {
             tma_load_3d(b_dst, &tmB, FULL(stage), kb * BK, nb * (BN / 2), 2 * s);
             tma_load_3d(b_dst + B_BYTES / 2, &tmB, FULL(stage), kb * BK, nb * (BN / 2), 2 * s + 1);
           } else {
             tma_load_3d(b_dst, &tmB, FULL(stage), kb * BK, nb * BN, s);
           }
-          ++issued;
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+        }
+        if (GATHER) {
+          __syncwarp();
+          if (lane < groups4)
+            tma_gather4(a_dst + (uint32_t)lane * 512u, &tmA, FULL(stage), kb * BK, src[0], src[1], src[2], src[3]);
+        }
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
-      if (!ok) {
-        // let the copies already issued land before the CTA can exit
-        const int first = issued > STAGES ? issued - STAGES : 0;
-        for (int j = first; j < issued; ++j)
-          mbar_wait_teardown(FULL(j % STAGES), (uint32_t)((j / STAGES) & 1));
-      }
+    }
+    if (!ok && lane == 0) {
+      // let the copies already issued land before the CTA can exit
+      const int first = issued > STAGES ? issued - STAGES : 0;
+      for (int j = first; j < issued; ++j)
+        mbar_wait_teardown(FULL(j % STAGES), (uint32_t)((j / STAGES) & 1));
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -557,11 +598,11 @@ bool encode(CUtensorMap *m, int dtype, int rank, const void *base, const cuuint6
   return r == CUDA_SUCCESS;
 }
 
-template <typename T, bool GATED, int ACT, int BN>
+template <typename T, bool GATED, int ACT, int BN, bool GATHER = false>
 int launch_tc_t(const rf::GroupedGemmArgs &g, const CUtensorMap &ma, const CUtensorMap &ma32,
                 const CUtensorMap &mb, cudaStream_t st) {
   using C = Cfg<BN>;
-  auto kern = tc_grouped_gemm<T, GATED, ACT, BN>;
+  auto kern = tc_grouped_gemm<T, GATED, ACT, BN, false, GATHER>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -584,6 +625,8 @@ int launch_tc_t(const rf::GroupedGemmArgs &g, const CUtensorMap &ma, const CUten
   p.out_ld = g.N;
   p.dense_rows = 0;
   p.act = g.act;
+  p.gather_src = g.gather_src;
+  p.gather_div = g.gather_div;
   kern<<<rf::num_sms(), NTHREADS, C::SMEM_BYTES, st>>>(ma, ma32, mb, p);
   return rf::check_launch(GATED ? "tensor-core gated GEMM" : "tensor-core down GEMM");
 }
@@ -592,6 +635,11 @@ template <typename T, int BN>
 int launch_tc_bn(const rf::GroupedGemmArgs &g, bool gated, const CUtensorMap &ma, const CUtensorMap &ma32,
                  const CUtensorMap &mb, cudaStream_t st) {
   if (!gated) return launch_tc_t<T, false, 0, BN>(g, ma, ma32, mb, st);
+  if (g.gather_src) {
+    if (g.act == RF_ACT_SILU) return launch_tc_t<T, true, RF_ACT_SILU, BN, true>(g, ma, ma32, mb, st);
+    if (g.act == RF_ACT_GELU) return launch_tc_t<T, true, RF_ACT_GELU, BN, true>(g, ma, ma32, mb, st);
+    return launch_tc_t<T, true, RF_ACT_GELU_TANH, BN, true>(g, ma, ma32, mb, st);
+  }
   if (g.act == RF_ACT_SILU) return launch_tc_t<T, true, RF_ACT_SILU, BN>(g, ma, ma32, mb, st);
   if (g.act == RF_ACT_GELU) return launch_tc_t<T, true, RF_ACT_GELU, BN>(g, ma, ma32, mb, st);
   return launch_tc_t<T, true, RF_ACT_GELU_TANH, BN>(g, ma, ma32, mb, st);
@@ -635,11 +683,21 @@ int try_tc(const rf::GroupedGemmArgs &g, bool gated, cudaStream_t st, int *rc) {
   }
   const int bn = pick_bn(g, gated);
   CUtensorMap ma, ma32, mb;
-  const cuuint64_t dA[2] = {(cuuint64_t)g.Kdim, (cuuint64_t)g.rows_capacity};
-  const cuuint64_t sAs[1] = {(cuuint64_t)g.Kdim * 2};
-  const cuuint32_t bA[2] = {BK, BM};
-  const cuuint32_t bA32[2] = {BK, BM_SMALL};
-  bool ok = encode(&ma, g.dtype, 2, g.a, dA, sAs, bA) && encode(&ma32, g.dtype, 2, g.a, dA, sAs, bA32);
+  bool ok;
+  if (g.gather_src) {
+    // token rows, fetched four at a time (box: 64 columns x 1 row)
+    const cuuint64_t dA[2] = {(cuuint64_t)g.Kdim, (cuuint64_t)g.a_rows};
+    const cuuint64_t sAs[1] = {(cuuint64_t)g.Kdim * 2};
+    const cuuint32_t bA1[2] = {BK, 1};
+    ok = encode(&ma, g.dtype, 2, g.a, dA, sAs, bA1);
+    ma32 = ma;
+  } else {
+    const cuuint64_t dA[2] = {(cuuint64_t)g.Kdim, (cuuint64_t)g.rows_capacity};
+    const cuuint64_t sAs[1] = {(cuuint64_t)g.Kdim * 2};
+    const cuuint32_t bA[2] = {BK, BM};
+    const cuuint32_t bA32[2] = {BK, BM_SMALL};
+    ok = encode(&ma, g.dtype, 2, g.a, dA, sAs, bA) && encode(&ma32, g.dtype, 2, g.a, dA, sAs, bA32);
+  }
   if (gated) {
     // w1 [S, 2N, K] viewed as [2S][N][K]: half 0 = gate rows, half 1 = up rows
     const cuuint64_t dB[3] = {(cuuint64_t)g.Kdim, (cuuint64_t)g.N, (cuuint64_t)(2 * g.num_slots)};
@@ -791,6 +849,51 @@ extern "C" int rf_moe_grouped_gemm_gated(const void *a, const void *w1, void *h,
   return grouped_gemm(a, w1, h, expert_offsets, expert_counts, expert_slot, groups, n_groups, E,
                       num_slots, rows_capacity, H, I, dtype, activation, true, stream,
                       "rf_moe_grouped_gemm_gated");
+}
+
+extern "C" int rf_moe_grouped_gemm_gated_gather(const void *x, int64_t x_rows, const int32_t *src_slot,
+                                                int64_t topk, const void *w1, void *h,
+                                                const int32_t *expert_offsets, const int32_t *expert_counts,
+                                                const int32_t *expert_slot, const int32_t *groups,
+                                                int64_t n_groups, int64_t E, int64_t num_slots,
+                                                int64_t rows_capacity, int64_t H, int64_t I, int dtype,
+                                                int activation, rf_stream_t stream) {
+  const char *nm = "rf_moe_grouped_gemm_gated_gather";
+  RF_CHECK_ARG(rf::valid_dtype(dtype), std::string(nm) + ": unknown dtype");
+  RF_CHECK_ARG(activation == RF_ACT_SILU || activation == RF_ACT_GELU || activation == RF_ACT_GELU_TANH,
+               std::string(nm) + ": unknown activation");
+  RF_CHECK_ARG(x_rows >= 1 && x_rows < ((int64_t)1 << 31) && topk >= 1, std::string(nm) + ": bad sizes");
+  RF_CHECK_ARG(E >= 1 && E <= 65535 && num_slots >= 1 && rows_capacity >= 0 && H >= 1 && I >= 1 &&
+                   H < (1 << 30) && I < (1 << 30) && rows_capacity < ((int64_t)1 << 31),
+               std::string(nm) + ": bad sizes");
+  RF_CHECK_ARG(x && src_slot && w1 && h && expert_offsets && expert_counts, std::string(nm) + ": null pointer");
+  const int64_t G = groups ? n_groups : E;
+  RF_CHECK_ARG(G >= 0 && G <= 65535, std::string(nm) + ": bad group count");
+  if (G == 0 || rows_capacity == 0) return RF_OK;
+  rf::GroupedGemmArgs g;
+  g.a = x;
+  g.w = w1;
+  g.out = h;
+  g.offsets = expert_offsets;
+  g.counts = expert_counts;
+  g.slot = expert_slot;
+  g.groups = groups;
+  g.n_groups = (int)G;
+  g.E = (int)E;
+  g.num_slots = (int)num_slots;
+  g.rows_capacity = rows_capacity;
+  g.Kdim = (int)H;
+  g.N = (int)I;
+  g.dtype = dtype;
+  g.act = activation;
+  g.gather_src = src_slot;
+  g.gather_div = (int)topk;
+  g.a_rows = x_rows;
+  int rc = RF_OK;
+  if (try_tc(g, true, (cudaStream_t)stream, &rc)) return rc;
+  return rf::fail(RF_ERR_UNSUPPORTED, std::string(nm) +
+                                          ": needs the tensor-core path (16-bit dtype, 16-byte aligned "
+                                          "rows); gather the rows with rf_moe_permute instead");
 }
 
 extern "C" int rf_moe_grouped_gemm_down(const void *h, const void *w2, void *y,

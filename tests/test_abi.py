@@ -39,6 +39,15 @@ def test_version_and_sizes():
     assert lib.rf_moe_router_workspace_size(64, 2048, 60, 1) >= 8 * 64 * 61 * 4
 
 
+def test_fused_gather_gemm_reports_unsupported_dtype():
+    """fp32 has no tensor-core path: the fused-gather GEMM declines (status 2)
+    without touching a GPU, and the caller gathers explicitly."""
+    lib = _lib.lib()
+    rc = lib.rf_moe_grouped_gemm_gated_gather(1 << 20, 4, 1 << 20, 2, 1 << 20, 1 << 20, 1 << 20, 1 << 20, None,
+                                              None, 0, 4, 4, 64, 64, 64, 0, 0, None)
+    assert rc == 2 and "tensor-core" in lib.rf_moe_last_error().decode()
+
+
 @pytest.mark.parametrize("call, needle", [
     (lambda L: L.rf_moe_router_topk(None, 2, None, 2, None, 4, 64, 8, 9, 1, -1, 0, None, None,
                                     None, None, None, None, None, 0, None), "K <="),

@@ -305,6 +305,26 @@ def test_fp32_grouped_gemm_tolerance():
         assert max_rel(y.cpu()[offs[e]:offs[e] + c], yr) < 1e-4
 
 
+@pytest.mark.parametrize("impl", [0, 2, 3, 4])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("T,topk,E", [(300, 2, 8), (64, 4, 60), (1000, 6, 16), (5, 1, 3)])
+def test_gated_gemm_with_fused_gather_is_bitwise_equal(impl, dtype, T, topk, E):
+    """The gated GEMM fetching token rows with TMA gather4 (no expert-ordered
+    copy) multiplies the same rows as the explicit gather + gated GEMM."""
+    _lib.set_gemm_impl(impl)
+    g = torch.Generator().manual_seed(T + topk + E)
+    H, I = 512, 384
+    x = torch.randn(T, H, generator=g).to(dtype).to(DEV)
+    ids = torch.stack([torch.randperm(E, generator=g)[:topk] for _ in range(T)]).int().to(DEV)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.05).to(dtype).to(DEV)
+    p = K.permute(ids, E, x=x)
+    ref = torch.zeros(p.rows_cap, I, dtype=dtype, device=DEV)
+    K.grouped_gemm_gated(p.x_perm, w1, p.offsets, p.counts, ref)
+    out = torch.zeros(p.rows_cap, I, dtype=dtype, device=DEV)
+    assert K.grouped_gemm_gated_gather(x, p.src_slot, topk, w1, p.offsets, p.counts, out)
+    assert torch.equal(out, ref)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("counts", [[20, 0, 75, 33], [1, 2, 3, 17, 0, 16, 5, 40]])
 def test_simt_skinny_and_tiled_kernels_agree_bitwise(dtype, counts):

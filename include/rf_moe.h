@@ -33,6 +33,7 @@
  *   rf_moe_grouped_gemm_down   reframework/moe/fused.py:83 (inter @ w2[e].t())
  *   rf_moe_combine          reframework/moe/fused.py:84-86 (y * w, index_add_)
  *                           + reframework/layers/norm.py:43-53 (residual add, opt-in)
+ *   rf_moe_combine_rmsnorm  the same + the next RMSNorm (norm.py:27-53)
  */
 #ifndef RF_MOE_H
 #define RF_MOE_H
@@ -299,6 +300,24 @@ int rf_moe_combine(const void *y, const int32_t *row_of_slot, const float *topk_
                    int64_t T, int64_t K, int64_t H, int dtype,
                    const void *shared_y, const float *shared_scale, const void *residual,
                    int accumulate, int mode, void *out, rf_stream_t stream);
+
+/*
+ * K5 with the decoder's next RMSNorm fused into its epilogue
+ * (reframework/layers/norm.py:43-53, RMSNorm.forward_add_residual):
+ *   residual_out[t] = combine(t) + residual[t]   (as rf_moe_combine, in `dtype`;
+ *                                                  residual may be NULL)
+ *   normed_out[t]   = r * (mean(r^2) + eps).sqrt().reciprocal() * norm_weight
+ *                     (+ norm_bias)              with r = residual_out[t] in fp32,
+ *                                                  each step rounded to fp32 as in
+ *                                                  norm.py:27-35, stored in `dtype`
+ * norm_weight / norm_bias: fp32 [H] (bias may be NULL).  The row mean is one
+ * fixed-order block reduction per token.  The outputs must not alias.
+ */
+int rf_moe_combine_rmsnorm(const void *y, const int32_t *row_of_slot, const float *topk_weights,
+                           int64_t T, int64_t K, int64_t H, int dtype,
+                           const void *shared_y, const float *shared_scale, const void *residual,
+                           int mode, const float *norm_weight, const float *norm_bias, float eps,
+                           void *residual_out, void *normed_out, rf_stream_t stream);
 
 #ifdef __cplusplus
 }

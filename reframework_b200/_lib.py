@@ -57,6 +57,9 @@ _SIGNATURES = {
                                         _int, _c_void_p]),
     "rf_moe_combine": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p,
                               _c_void_p, _c_void_p, _int, _int, _c_void_p, _c_void_p]),
+    "rf_moe_combine_rmsnorm": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p,
+                                      _c_void_p, _c_void_p, _int, _c_void_p, _c_void_p, ctypes.c_float,
+                                      _c_void_p, _c_void_p, _c_void_p]),
     "rf_moe_ep_plan": (_int, [_c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_void_p, _c_void_p,
                               ctypes.c_int32, ctypes.c_int32, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
 }

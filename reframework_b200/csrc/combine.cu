@@ -37,6 +37,12 @@ struct CombineArgs {
   int K, H;
   int accumulate;
   int mode;
+  // fused RMSNorm (norm_out != NULL): `out` receives the new residual row
+  // r = combine + residual and norm_out = r / sqrt(mean(r^2) + eps) * w (+ b)
+  void *norm_out;
+  const float *norm_w;
+  const float *norm_b;
+  float eps;
 };
 
 template <typename T>
@@ -90,13 +96,14 @@ __device__ __forceinline__ uint32_t mul_add2(uint32_t acc, uint32_t y, typename 
   return *reinterpret_cast<const uint32_t *>(&r);
 }
 
-template <typename T, bool REF>
+template <typename T, bool REF, bool NORM>
 __global__ void __launch_bounds__(CT) combine_kernel(CombineArgs a) {
   constexpr int V = 16 / sizeof(T);  // elements per 16-byte vector
   constexpr bool PACKED = REF && sizeof(T) == 2;
   __shared__ int s_row[KMAX];
   __shared__ float s_w[KMAX];
   __shared__ int s_n;
+  __shared__ float s_red[CT / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const T *y = reinterpret_cast<const T *>(a.y);
   const T *sy = reinterpret_cast<const T *>(a.shared_y);
@@ -135,6 +142,7 @@ __global__ void __launch_bounds__(CT) combine_kernel(CombineArgs a) {
     __syncthreads();
     const int n = s_n;
     const float sscale = (sy && a.shared_scale) ? a.shared_scale[t] : 1.0f;
+    float ss = 0.f;  // NORM: sum of squares of the stored residual row (this thread's part)
     for (int v0 = threadIdx.x; v0 < nv; v0 += CT * VPT) {
       float acc[VPT][V];
       uint32_t pacc[VPT][4];
@@ -216,6 +224,44 @@ __global__ void __launch_bounds__(CT) combine_kernel(CombineArgs a) {
           for (int i = 0; i < V; ++i) ac[i] = __fadd_rn(ac[i], f[i]);
         }
         store16<T>(o, ac);
+        if constexpr (NORM) {
+#pragma unroll
+          for (int i = 0; i < V; ++i) {
+            const float r = rf::round_to<T>(ac[i]);  // the value stored above
+            ss = fmaf(r, r, ss);
+          }
+        }
+      }
+    }
+    if constexpr (NORM) {
+      // norm.py:27-35 on the stored row: x32 * (mean(x32^2) + eps).sqrt().reciprocal() * w (+ b)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < CT / 32; ++w) tot += s_red[w];
+      const float inv = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(tot, (float)a.H), a.eps));
+      T *nout = reinterpret_cast<T *>(a.norm_out);
+      for (int v0 = threadIdx.x; v0 < nv; v0 += CT * VPT) {
+#pragma unroll
+        for (int u = 0; u < VPT; ++u) {
+          const int v = v0 + u * CT;
+          if (v >= nv) continue;
+          // this thread stored these vectors of `out` in the first sweep
+          const uint4 q = *reinterpret_cast<const uint4 *>(out + t * a.H + (int64_t)v * V);
+          float f[V];
+          rf::unpack16<T>(q, f);
+#pragma unroll
+          for (int i = 0; i < V; ++i) {
+            const int col = v * V + i;
+            float z = __fmul_rn(__fmul_rn(f[i], inv), a.norm_w[col]);
+            if (a.norm_b) z = __fadd_rn(z, a.norm_b[col]);
+            f[i] = z;
+          }
+          store16<T>(nout + t * a.H + (int64_t)v * V, f);
+        }
       }
     }
     __syncthreads();
@@ -224,8 +270,13 @@ __global__ void __launch_bounds__(CT) combine_kernel(CombineArgs a) {
 
 template <typename T>
 void launch_t(const CombineArgs &a, int blocks, cudaStream_t st) {
-  if (a.mode == RF_COMBINE_REFERENCE) combine_kernel<T, true><<<blocks, CT, 0, st>>>(a);
-  else combine_kernel<T, false><<<blocks, CT, 0, st>>>(a);
+  if (a.norm_out) {
+    if (a.mode == RF_COMBINE_REFERENCE) combine_kernel<T, true, true><<<blocks, CT, 0, st>>>(a);
+    else combine_kernel<T, false, true><<<blocks, CT, 0, st>>>(a);
+    return;
+  }
+  if (a.mode == RF_COMBINE_REFERENCE) combine_kernel<T, true, false><<<blocks, CT, 0, st>>>(a);
+  else combine_kernel<T, false, false><<<blocks, CT, 0, st>>>(a);
 }
 
 }  // namespace
@@ -245,7 +296,7 @@ extern "C" int rf_moe_combine(const void *y, const int32_t *row_of_slot, const f
                "rf_moe_combine: buffers must be 16-byte aligned");
   if (T == 0) return RF_OK;
   CombineArgs a{y, row_of_slot, topk_weights, shared_y, shared_scale, residual, out, T, (int)K, (int)H,
-                accumulate, mode};
+                accumulate, mode, nullptr, nullptr, nullptr, 0.f};
   int64_t blocks = T;
   const int64_t cap = (int64_t)rf::num_sms() * 16;
   if (blocks > cap) blocks = cap;
@@ -256,4 +307,37 @@ extern "C" int rf_moe_combine(const void *y, const int32_t *row_of_slot, const f
     default: launch_t<__nv_bfloat16>(a, (int)blocks, st); break;
   }
   return rf::check_launch("rf_moe_combine");
+}
+
+extern "C" int rf_moe_combine_rmsnorm(const void *y, const int32_t *row_of_slot, const float *topk_weights,
+                                      int64_t T, int64_t K, int64_t H, int dtype, const void *shared_y,
+                                      const float *shared_scale, const void *residual, int mode,
+                                      const float *norm_weight, const float *norm_bias, float eps,
+                                      void *residual_out, void *normed_out, rf_stream_t stream) {
+  RF_CHECK_ARG(rf::valid_dtype(dtype), "rf_moe_combine_rmsnorm: unknown dtype");
+  RF_CHECK_ARG(mode == RF_COMBINE_REFERENCE || mode == RF_COMBINE_FP32, "rf_moe_combine_rmsnorm: unknown mode");
+  RF_CHECK_ARG(T >= 0 && K >= 1 && K <= KMAX && H > 0 && H < ((int64_t)1 << 30),
+               "rf_moe_combine_rmsnorm: bad sizes (K <= 16)");
+  RF_CHECK_ARG((H * (int64_t)rf::dtype_size(dtype)) % 16 == 0,
+               "rf_moe_combine_rmsnorm: H * element size must be a multiple of 16 bytes");
+  RF_CHECK_ARG(eps >= 0.f, "rf_moe_combine_rmsnorm: eps must be >= 0");
+  RF_CHECK_ARG(T == 0 || (y && row_of_slot && topk_weights && residual_out && normed_out && norm_weight),
+               "rf_moe_combine_rmsnorm: null pointer");
+  RF_CHECK_ARG((uintptr_t)y % 16 == 0 && (uintptr_t)residual_out % 16 == 0 && (uintptr_t)normed_out % 16 == 0 &&
+                   (uintptr_t)shared_y % 16 == 0 && (uintptr_t)residual % 16 == 0,
+               "rf_moe_combine_rmsnorm: buffers must be 16-byte aligned");
+  RF_CHECK_ARG(normed_out != residual_out, "rf_moe_combine_rmsnorm: the two outputs must not alias");
+  if (T == 0) return RF_OK;
+  CombineArgs a{y, row_of_slot, topk_weights, shared_y, shared_scale, residual, residual_out, T, (int)K, (int)H,
+                0, mode, normed_out, norm_weight, norm_bias, eps};
+  int64_t blocks = T;
+  const int64_t cap = (int64_t)rf::num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (dtype) {
+    case RF_F32: launch_t<float>(a, (int)blocks, st); break;
+    case RF_F16: launch_t<__half>(a, (int)blocks, st); break;
+    default: launch_t<__nv_bfloat16>(a, (int)blocks, st); break;
+  }
+  return rf::check_launch("rf_moe_combine_rmsnorm");
 }

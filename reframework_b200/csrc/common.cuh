@@ -148,7 +148,7 @@ __device__ __forceinline__ float gated_elem(int act, float g, float u) {
 // rf_report(code) that sets it (first error wins), and registers its reader.
 #define RF_DEVICE_ERROR_WORD()                                                        \
   static __device__ int rf_tu_error_word;                                             \
-  static __device__ __forceinline__ void rf_report(int code) {                        \
+  [[maybe_unused]] static __device__ __forceinline__ void rf_report(int code) {       \
     atomicCAS(&rf_tu_error_word, 0, code);                                            \
   }                                                                                   \
   static int rf_tu_read_clear() {                                                     \

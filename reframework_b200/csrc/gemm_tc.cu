@@ -364,7 +364,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint32_t phase = 0;
     int issued = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+    // without gather only lane 0 works (no per-k-block warp shuffle)
+    for (int t = blockIdx.x; t < total && ok && (GATHER || lane == 0); t += gridDim.x) {
       int row0, rows, nb, s;
       decode(t, row0, rows, nb, s);
       int src[4] = {0, 0, 0, 0};
@@ -381,7 +382,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int kb = 0; kb < num_kb; ++kb) {
         int go = 1;
         if (lane == 0) go = mbar_wait(EMPTY(stage), phase ^ 1u, abort_flag) ? 1 : 0;
-        go = __shfl_sync(0xffffffffu, go, 0);
+        if constexpr (GATHER) go = __shfl_sync(0xffffffffu, go, 0);
         if (!go) {
           ok = false;
           break;

@@ -189,15 +189,30 @@ def grouped_gemm_down(h: torch.Tensor, w2: torch.Tensor, offsets: torch.Tensor, 
 def combine(y: torch.Tensor, row_of_slot: torch.Tensor, weights: torch.Tensor, out: torch.Tensor, *,
             shared_y: Optional[torch.Tensor] = None, shared_scale: Optional[torch.Tensor] = None,
             residual: Optional[torch.Tensor] = None, accumulate: bool = False,
-            precise: bool = False) -> torch.Tensor:
+            precise: bool = False, norm: Optional[Tuple[torch.Tensor, Optional[torch.Tensor], float]] = None,
+            norm_out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``out[t] = sum_k w[t,k] y[row(t,k)] (+ shared, residual)``.  Default: the
-    reference's rounding points and order; ``precise=True``: fp32 accumulation."""
-    dev = _require_cuda(y, row_of_slot, weights, out, shared_y, shared_scale, residual)
+    reference's rounding points and order; ``precise=True``: fp32 accumulation.
+    ``norm=(weight, bias or None, eps)``: ``out`` is the new residual and
+    ``norm_out`` receives its RMSNorm (reframework/layers/norm.py:43-53)."""
+    dev = _require_cuda(y, row_of_slot, weights, out, shared_y, shared_scale, residual, norm_out)
     T, K = weights.shape
     H = out.shape[1]
     weights = weights.contiguous()
     if weights.dtype != torch.float32:
         weights = weights.float()
+    mode = _lib.COMBINE_FP32 if precise else _lib.COMBINE_REFERENCE
+    if norm is not None:
+        if accumulate or norm_out is None:
+            raise ValueError("combine with norm needs norm_out and no accumulate")
+        nw, nb, eps = norm
+        nw = nw.to(device=dev, dtype=torch.float32).contiguous()
+        nb = None if nb is None else nb.to(device=dev, dtype=torch.float32).contiguous()
+        rc = lib().rf_moe_combine_rmsnorm(ptr(y), ptr(row_of_slot), ptr(weights), T, K, H, dtype_code(out.dtype),
+                                          ptr(shared_y), ptr(shared_scale), ptr(residual), mode, ptr(nw), ptr(nb),
+                                          float(eps), ptr(out), ptr(norm_out), stream_of(dev))
+        check(rc, "rf_moe_combine_rmsnorm")
+        return out
     rc = lib().rf_moe_combine(ptr(y), ptr(row_of_slot), ptr(weights), T, K, H, dtype_code(out.dtype),
                               ptr(shared_y), ptr(shared_scale), ptr(residual), int(bool(accumulate)),
                               _lib.COMBINE_FP32 if precise else _lib.COMBINE_REFERENCE, ptr(out), stream_of(dev))
@@ -239,8 +254,11 @@ def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, weights: to
                 ids32: torch.Tensor, *, activation: str = "silu", shared_y: Optional[torch.Tensor] = None,
                 shared_scale: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
                 out: Optional[torch.Tensor] = None, slot: Optional[torch.Tensor] = None,
-                num_experts: Optional[int] = None, precise: bool = False) -> torch.Tensor:
-    """Permute -> grouped gated GEMM -> grouped down GEMM -> combine (routing given)."""
+                num_experts: Optional[int] = None, precise: bool = False,
+                norm: Optional[Tuple[torch.Tensor, Optional[torch.Tensor], float]] = None,
+                norm_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Permute -> grouped gated GEMM -> grouped down GEMM -> combine (routing given).
+    With ``norm`` the combine also writes the RMSNorm of its output to ``norm_out``."""
     T, H = x.shape
     E = num_experts if num_experts is not None else w1.shape[0]
     I = w2.shape[2]
@@ -255,4 +273,4 @@ def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, weights: to
     if out is None:
         out = torch.empty(T, H, dtype=x.dtype, device=x.device)
     return combine(y, p.row_of_slot, weights, out, shared_y=shared_y, shared_scale=shared_scale,
-                   residual=residual, precise=precise)
+                   residual=residual, precise=precise, norm=norm, norm_out=norm_out)

@@ -312,32 +312,49 @@ class FusedMoE(nn.Module):
 
     # ------------------------------------------------------------------ forward
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        out, _ = self._forward_impl(x, residual, None)
+        return self._shape_like(out, x)
+
+    def forward_add_residual(self, x: torch.Tensor, residual: torch.Tensor,
+                             norm) -> Tuple[torch.Tensor, torch.Tensor]:
+        """The layer with the decoder's next ``RMSNorm.forward_add_residual``
+        fused into its combine (reframework/layers/norm.py:43-53):
+        ``residual = moe(x) + residual; x = norm(residual)``; returns
+        ``(normed, residual)``.  ``norm`` is an RMSNorm (``weight`` [H],
+        ``eps``, optional ``bias``), applied in fp32 as norm.py:27-35 does."""
+        bias = getattr(norm, "bias", None)
+        spec = (norm.weight.detach(), None if bias is None else bias.detach(), float(norm.eps))
+        res, normed = self._forward_impl(x, residual, spec)
+        return self._shape_like(normed, x), self._shape_like(res, x)
+
+    def _shape_like(self, out: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        if out.dtype != x.dtype:
+            out = out.to(x.dtype)
+        if x.dim() <= 2:
+            return out
+        return out.reshape(x.shape)
+
+    def _forward_impl(self, x: torch.Tensor, residual: Optional[torch.Tensor], norm):
         x2 = self._prep(x)
-        T = x2.shape[0]
         res2 = None
         if residual is not None:
             res2 = residual.reshape(-1, self.hidden_size).to(self.dtype).contiguous()
+        normed = None if norm is None else torch.empty_like(x2)
         w, ids32, _, _, sscale = self._router(x2, ids32=True, ids64=False)
         shared_y = None
         sb = self._shared_banks()
         if sb is not None:
             shared_y = K.dense_gated_mlp(x2, sb[0], sb[1], self.activation)
         if self.uses_offload:
-            out = self._forward_offload(x2, w, ids32, shared_y, sscale, res2)
+            out = self._forward_offload(x2, w, ids32, shared_y, sscale, res2, norm, normed)
         else:
             w1b, w2b = self._resident_banks()
             out = K.moe_experts(x2, w1b, w2b, w, ids32, activation=self.activation,
                                 shared_y=shared_y, shared_scale=sscale, residual=res2,
-                                precise=self.precise_combine)
-        if out.dtype != x.dtype:
-            out = out.to(x.dtype)
-        if x.dim() == 1:
-            return out
-        if x.dim() == 2:
-            return out
-        return out.reshape(x.shape)
+                                precise=self.precise_combine, norm=norm, norm_out=normed)
+        return out, normed
 
-    def _forward_offload(self, x2, w, ids32, shared_y, sscale, res2):
+    def _forward_offload(self, x2, w, ids32, shared_y, sscale, res2, norm=None, normed=None):
         """Exact streaming forward through the cache's device slots.
 
         Resident routed experts run first (one grouped launch); each missing
@@ -388,7 +405,7 @@ class FusedMoE(nn.Module):
         cache._evict((), soft)  # only trims a pool that had to grow past capacity
         out = torch.empty(T, H, dtype=x2.dtype, device=dev)
         K.combine(y, p.row_of_slot, w, out, shared_y=shared_y, shared_scale=sscale, residual=res2,
-                  precise=self.precise_combine)
+                  precise=self.precise_combine, norm=norm, norm_out=normed)
         if self._predictor is not None:
             self._predictor.record_step(active, is_prefill=(T > 1), forward_ms=self._since_last_step_ms(),
                                         inflight_bytes=(self._shuttle.inflight_bytes()

@@ -255,3 +255,48 @@ def test_graph_capture_matches_eager(name):
     assert torch.equal(g(x2), eager2)
     with pytest.raises(ValueError):
         g(x[:-1])
+
+
+class _RMSNorm:
+    """The parameters of reframework/layers/norm.py:18-24 (weight, eps, optional bias)."""
+
+    def __init__(self, H, eps, bias, dtype, seed):
+        g = torch.Generator().manual_seed(seed)
+        self.weight = (1.0 + 0.1 * torch.randn(H, generator=g)).to(dtype).to(DEV)
+        self.bias = (0.05 * torch.randn(H, generator=g)).to(dtype).to(DEV) if bias else None
+        self.eps = eps
+
+    def reference(self, r):
+        """norm.py:27-35 in torch fp32, op by op."""
+        x32 = r.to(torch.float32)
+        norm = x32.pow(2).mean(-1, keepdim=True).add(self.eps).sqrt().reciprocal()
+        out = x32 * norm
+        out = out * self.weight.to(torch.float32)
+        if self.bias is not None:
+            out = out + self.bias.to(torch.float32)
+        return out.to(r.dtype)
+
+
+@pytest.mark.parametrize("name,bias", [("c2_mini_bf16", False), ("c3_mini_bf16", True), ("fp16_default", False),
+                                       ("c1_tiny_fp32", True)])
+def test_forward_add_residual_fuses_the_next_rmsnorm(name, bias):
+    """forward_add_residual == (norm(moe(x) + r), moe(x) + r): the new residual
+    is bit-identical to the unfused forward(x, residual=r); the normed rows match
+    norm.py's fp32 restatement up to the order of the row sum."""
+    rec = load_golden(name)
+    cfg = golden_config(rec)
+    d = generate(cfg)
+    moe = build_layer(cfg, d, harness=rec["mode"] == "harness")
+    x = d["x"].to(DEV)
+    g = torch.Generator().manual_seed(3)
+    r = torch.randn(x.shape, generator=g).to(x.dtype).to(DEV)
+    norm = _RMSNorm(cfg.hidden, 1e-6, bias, cfg.dtype, seed=4)
+    with torch.no_grad():
+        normed, res = moe.forward_add_residual(x, r, norm)
+        res_ref = moe(x, residual=r)
+    assert torch.equal(res, res_ref)
+    ref = norm.reference(res_ref)
+    assert max_rel(normed, ref) < (1e-5 if cfg.dtype == torch.float32 else 1e-2)
+    if cfg.dtype != torch.float32:
+        same = (normed == ref).float().mean().item()
+        assert same > 0.98, f"only {same:.3f} of the normed values bit-identical"

@@ -256,9 +256,12 @@ def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, weights: to
                 out: Optional[torch.Tensor] = None, slot: Optional[torch.Tensor] = None,
                 num_experts: Optional[int] = None, precise: bool = False,
                 norm: Optional[Tuple[torch.Tensor, Optional[torch.Tensor], float]] = None,
-                norm_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                norm_out: Optional[torch.Tensor] = None,
+                before_combine: Optional[torch.cuda.Event] = None) -> torch.Tensor:
     """Permute -> grouped gated GEMM -> grouped down GEMM -> combine (routing given).
-    With ``norm`` the combine also writes the RMSNorm of its output to ``norm_out``."""
+    With ``norm`` the combine also writes the RMSNorm of its output to ``norm_out``.
+    ``before_combine``: an event (e.g. the shared experts on a side stream)
+    the combine waits for; everything before it does not."""
     T, H = x.shape
     E = num_experts if num_experts is not None else w1.shape[0]
     I = w2.shape[2]
@@ -272,5 +275,7 @@ def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, weights: to
     grouped_gemm_down(h, w2, p.offsets, p.counts, y, slot=slot)
     if out is None:
         out = torch.empty(T, H, dtype=x.dtype, device=x.device)
+    if before_combine is not None:
+        torch.cuda.current_stream(x.device).wait_event(before_combine)
     return combine(y, p.row_of_slot, weights, out, shared_y=shared_y, shared_scale=shared_scale,
                    residual=residual, precise=precise, norm=norm, norm_out=norm_out)

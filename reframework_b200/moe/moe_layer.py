@@ -340,10 +340,25 @@ class FusedMoE(nn.Module):
         if residual is not None:
             res2 = residual.reshape(-1, self.hidden_size).to(self.dtype).contiguous()
         normed = None if norm is None else torch.empty_like(x2)
-        w, ids32, _, _, sscale = self._router(x2, ids32=True, ids64=False)
         shared_y = None
+        shared_done = None
         sb = self._shared_banks()
-        if sb is not None:
+        if sb is not None and not self.uses_offload:
+            # The shared experts depend only on x: run them on a side stream so
+            # they overlap the router, permute and gather (a few small kernels),
+            # and join before the combine.  (Decode: the shared down projection
+            # has few tiles and would otherwise leave most SMs idle.)
+            cur = torch.cuda.current_stream(x2.device)
+            side = self._side_stream(x2.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                shared_y = K.dense_gated_mlp(x2, sb[0], sb[1], self.activation)
+                shared_done = torch.cuda.Event()
+                shared_done.record(side)
+            x2.record_stream(side)
+            shared_y.record_stream(cur)
+        w, ids32, _, _, sscale = self._router(x2, ids32=True, ids64=False)
+        if sb is not None and self.uses_offload:
             shared_y = K.dense_gated_mlp(x2, sb[0], sb[1], self.activation)
         if self.uses_offload:
             out = self._forward_offload(x2, w, ids32, shared_y, sscale, res2, norm, normed)
@@ -351,8 +366,15 @@ class FusedMoE(nn.Module):
             w1b, w2b = self._resident_banks()
             out = K.moe_experts(x2, w1b, w2b, w, ids32, activation=self.activation,
                                 shared_y=shared_y, shared_scale=sscale, residual=res2,
-                                precise=self.precise_combine, norm=norm, norm_out=normed)
+                                precise=self.precise_combine, norm=norm, norm_out=normed,
+                                before_combine=shared_done)
         return out, normed
+
+    def _side_stream(self, device: torch.device) -> torch.cuda.Stream:
+        s = getattr(self, "_side", None)
+        if s is None or s.device != device:
+            s = self._side = torch.cuda.Stream(device=device)
+        return s
 
     def _forward_offload(self, x2, w, ids32, shared_y, sscale, res2, norm=None, normed=None):
         """Exact streaming forward through the cache's device slots.

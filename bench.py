@@ -223,10 +223,12 @@ def e2e_run(fwd, xh, steps, dev):
     return t0.elapsed_time(t1)
 
 
-LAUNCHES_PER_FORWARD = 7  # router, permute x3 (histogram, scatter, gather), gated GEMM, down GEMM, combine
-# EP: router, permute x3, regroup gather, gated GEMM, down GEMM, return gather, combine (+ send-order
-# and un-permute gathers when replicas split an expert); NCCL's own kernels are not counted
-EP_LAUNCHES_PER_FORWARD = 9
+# router x2 (tensor-core logits, top-k), permute x3 (histogram, scatter, gather), gated GEMM, down GEMM, combine
+LAUNCHES_PER_FORWARD = 8
+# EP over peer memory: router x2, permute x2 (histogram, scatter), dispatch push + wait, regroup gather,
+# gated GEMM, down GEMM, return push + wait, combine (+ the un-permute gather when replicas split an
+# expert); NCCL's own kernels (the counts all-gather) are not counted
+EP_LAUNCHES_PER_FORWARD = 12
 
 
 def run_gpu(args):
@@ -342,7 +344,7 @@ def run_gpu(args):
                 "ms_per_step": ms_e2e, "api": "FusedMoE.forward" if world == 1 else "EPFusedMoE.forward",
                 "pipeline": "H2D of step i+1 and D2H of step i on two copy streams overlap step i's forward"},
         "gpu_launches": args.steps * (LAUNCHES_PER_FORWARD if world == 1 else
-                                      EP_LAUNCHES_PER_FORWARD + (2 if layer.last_plan.send_index is not None else 0)),
+                                      EP_LAUNCHES_PER_FORWARD + (1 if layer.last_plan.send_index is not None else 0)),
         "clocks": clk,
     }
     if stage_fn:
@@ -372,6 +374,7 @@ def run_gpu(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(cfg, layer, budget_s=args.cpu_budget)
     if world > 1:
+        layer.close()  # peer buffers (collective)
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

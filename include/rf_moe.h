@@ -34,6 +34,8 @@
  *   rf_moe_combine          reframework/moe/fused.py:84-86 (y * w, index_add_)
  *                           + reframework/layers/norm.py:43-53 (residual add, opt-in)
  *   rf_moe_combine_rmsnorm  the same + the next RMSNorm (norm.py:27-53)
+ *   rf_moe_ep_push_rows / rf_moe_ep_wait  reframework/parallel/dist.py:194-206
+ *                           (EP dispatch / return all-to-all) as NVLink stores
  */
 #ifndef RF_MOE_H
 #define RF_MOE_H
@@ -277,6 +279,45 @@ int rf_moe_ep_plan(const int32_t *counts, int32_t R, int32_t E, int32_t rank,
                    const int32_t *slot_experts, const int32_t *slot_offsets, int32_t align,
                    int32_t rounds, int64_t *send_splits, int64_t *recv_splits,
                    int32_t *packed, int64_t packed_capacity, int64_t *layout);
+
+/*
+ * M[s * R + d] = rows rank s sends to rank d this step: the all-to-all matrix
+ * of the split rf_moe_ep_plan computes (same arguments).  With it every rank
+ * knows where its rows land in every peer's receive buffer.
+ */
+int rf_moe_ep_pair_rows(const int32_t *counts, int32_t R, int32_t E, const int32_t *slot_experts,
+                        const int32_t *slot_offsets, int32_t rounds, int64_t *pair_rows);
+
+/*
+ * Peer-visible device memory (CUDA IPC): rf_moe_peer_alloc allocates `bytes`
+ * (zeroed) and writes a 64-byte handle; a process on another GPU of the node
+ * maps it with rf_moe_peer_open and unmaps with rf_moe_peer_close; the owner
+ * releases it with rf_moe_peer_free (after every peer closed it).
+ */
+int rf_moe_peer_alloc(size_t bytes, void **ptr, void *handle);
+int rf_moe_peer_open(const void *handle, void **ptr);
+int rf_moe_peer_close(void *ptr);
+int rf_moe_peer_free(void *ptr);
+
+/*
+ * EP row exchange over NVLink peer memory — replaces the dispatch and return
+ * all-to-alls (reframework/parallel/dist.py:194-206) of the token-dispatch EP
+ * layer with one-sided stores:
+ *   for each of this rank's rows i in [chunk_off[d], chunk_off[d+1]):
+ *     j   = idx1 ? idx1[i] : i;   row = idx2 ? idx2[j] / div : j
+ *     dst[d][dst_row0[d] + i - chunk_off[d]] = src[row]      (row_bytes each)
+ *   then *flag[d] = epoch for every d (release, system scope) once all rows of
+ *   the launch are visible.  dst/flag: R device pointers (peer mappings or
+ *   this rank's own buffers), passed by value (R <= 64); done: a zeroed
+ *   uint32 of this rank.
+ * rf_moe_ep_wait: stream-ordered wait until flags[0..R) all equal epoch
+ * (bounded: after 2 s it sets RF_DEV_WAIT_TIMEOUT and returns).
+ */
+int rf_moe_ep_push_rows(const void *src, int64_t row_bytes, const int32_t *idx1, const int32_t *idx2,
+                        int64_t div, int32_t R, int32_t me, const int64_t *chunk_off,
+                        const int64_t *dst_row0, void *const *dst, int32_t *const *flag, int32_t epoch,
+                        uint32_t *done, rf_stream_t stream);
+int rf_moe_ep_wait(const int32_t *flags, int32_t R, int32_t epoch, rf_stream_t stream);
 
 /* Summation modes of rf_moe_combine. */
 #define RF_COMBINE_REFERENCE 0  /* the reference's rounding points and order */

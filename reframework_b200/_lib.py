@@ -60,6 +60,16 @@ _SIGNATURES = {
     "rf_moe_combine_rmsnorm": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p,
                                       _c_void_p, _c_void_p, _int, _c_void_p, _c_void_p, ctypes.c_float,
                                       _c_void_p, _c_void_p, _c_void_p]),
+    "rf_moe_ep_pair_rows": (_int, [_c_void_p, ctypes.c_int32, ctypes.c_int32, _c_void_p, _c_void_p,
+                                   ctypes.c_int32, _c_void_p]),
+    "rf_moe_peer_alloc": (_int, [ctypes.c_size_t, ctypes.POINTER(_c_void_p), _c_void_p]),
+    "rf_moe_peer_open": (_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "rf_moe_peer_close": (_int, [_c_void_p]),
+    "rf_moe_peer_free": (_int, [_c_void_p]),
+    "rf_moe_ep_push_rows": (_int, [_c_void_p, _i64, _c_void_p, _c_void_p, _i64, ctypes.c_int32, ctypes.c_int32,
+                                   _c_void_p, _c_void_p, _c_void_p, _c_void_p, ctypes.c_int32, _c_void_p,
+                                   _c_void_p]),
+    "rf_moe_ep_wait": (_int, [_c_void_p, ctypes.c_int32, ctypes.c_int32, _c_void_p]),
     "rf_moe_ep_plan": (_int, [_c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_void_p, _c_void_p,
                               ctypes.c_int32, ctypes.c_int32, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
 }

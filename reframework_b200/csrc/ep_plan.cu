@@ -52,36 +52,48 @@ void waterfill(int64_t n, const std::vector<int64_t> &base, std::vector<int64_t>
   for (int pos = 0; pos < m; ++pos) out[order[pos]] = give[pos];
 }
 
-}  // namespace
+// Holders, water-filled per-holder quotas and the row runs of one step: the
+// deterministic split every rank derives from the global counts.
+struct Split {
+  int R = 0, E = 0;
+  std::vector<int64_t> quota, lo, sbase;  // [E * R]
+  const int32_t *counts = nullptr;
+  // rows of source rank `src`'s pairs for expert e that holder h computes
+  // (and their offset inside src's run of e)
+  int64_t piece(int e, int src, int h, int64_t *offset) const {
+    const int64_t qlo = lo[(int64_t)e * R + h], qhi = qlo + quota[(int64_t)e * R + h];
+    const int64_t slo = sbase[(int64_t)e * R + src], shi = slo + counts[(int64_t)src * E + e];
+    const int64_t a = std::max(qlo, slo), b = std::min(qhi, shi);
+    if (offset) *offset = a - slo;
+    return std::max<int64_t>(0, b - a);
+  }
+};
 
-extern "C" int rf_moe_ep_plan(const int32_t *counts, int32_t R, int32_t E, int32_t rank,
-                              const int32_t *slot_experts, const int32_t *slot_offsets, int32_t align,
-                              int32_t rounds, int64_t *send_splits, int64_t *recv_splits,
-                              int32_t *packed, int64_t packed_capacity, int64_t *layout) {
-  RF_CHECK_ARG(counts && slot_experts && slot_offsets && send_splits && recv_splits && layout,
-               "rf_moe_ep_plan: null pointer");
-  RF_CHECK_ARG(R >= 1 && E >= 1 && rank >= 0 && rank < R && align >= 1 && rounds >= 0,
-               "rf_moe_ep_plan: bad sizes");
+// Returns RF_OK or an argument error (recorded).
+int build_split(const int32_t *counts, int32_t R, int32_t E, const int32_t *slot_experts,
+                const int32_t *slot_offsets, int32_t rounds, Split &sp) {
   // ---- holders of every expert, in rank order
   std::vector<std::vector<int>> holders(E);
   for (int r = 0; r < R; ++r) {
-    RF_CHECK_ARG(slot_offsets[r] <= slot_offsets[r + 1], "rf_moe_ep_plan: slot_offsets not ascending");
+    RF_CHECK_ARG(slot_offsets[r] <= slot_offsets[r + 1], "EP split: slot_offsets not ascending");
     for (int s = slot_offsets[r]; s < slot_offsets[r + 1]; ++s) {
       const int e = slot_experts[s];
-      RF_CHECK_ARG(e >= 0 && e < E, "rf_moe_ep_plan: slot expert out of range");
+      RF_CHECK_ARG(e >= 0 && e < E, "EP split: slot expert out of range");
       holders[e].push_back(r);
     }
   }
   std::vector<int64_t> total(E, 0);
   for (int r = 0; r < R; ++r)
     for (int e = 0; e < E; ++e) {
-      RF_CHECK_ARG(counts[(int64_t)r * E + e] >= 0, "rf_moe_ep_plan: negative count");
+      RF_CHECK_ARG(counts[(int64_t)r * E + e] >= 0, "EP split: negative count");
       total[e] += counts[(int64_t)r * E + e];
     }
   for (int e = 0; e < E; ++e)
-    RF_CHECK_ARG(!holders[e].empty() || total[e] == 0, "rf_moe_ep_plan: routed expert held by no rank");
+    RF_CHECK_ARG(!holders[e].empty() || total[e] == 0, "EP split: routed expert held by no rank");
   // ---- per-holder quota
-  std::vector<int64_t> quota((int64_t)E * R, 0), load(R, 0);
+  std::vector<int64_t> &quota = sp.quota;
+  quota.assign((int64_t)E * R, 0);
+  std::vector<int64_t> load(R, 0);
   std::vector<int> replicated;
   for (int e = 0; e < E; ++e) {
     const auto &hs = holders[e];
@@ -118,7 +130,9 @@ extern "C" int rf_moe_ep_plan(const int32_t *counts, int32_t R, int32_t E, int32
     if (!changed) break;
   }
   // ---- runs: holder h of expert e covers global rows [lo, lo + quota) (rank order)
-  std::vector<int64_t> lo((int64_t)E * R, 0), sbase((int64_t)E * R, 0);
+  std::vector<int64_t> &lo = sp.lo, &sbase = sp.sbase;
+  lo.assign((int64_t)E * R, 0);
+  sbase.assign((int64_t)E * R, 0);
   for (int e = 0; e < E; ++e) {
     int64_t acc = 0, src = 0;
     for (int r = 0; r < R; ++r) {
@@ -128,13 +142,28 @@ extern "C" int rf_moe_ep_plan(const int32_t *counts, int32_t R, int32_t E, int32
       src += counts[(int64_t)r * E + e];
     }
   }
-  auto piece = [&](int e, int src, int h, int64_t *offset) -> int64_t {
-    const int64_t qlo = lo[(int64_t)e * R + h], qhi = qlo + quota[(int64_t)e * R + h];
-    const int64_t slo = sbase[(int64_t)e * R + src], shi = slo + counts[(int64_t)src * E + e];
-    const int64_t a = std::max(qlo, slo), b = std::min(qhi, shi);
-    if (offset) *offset = a - slo;
-    return std::max<int64_t>(0, b - a);
-  };
+  sp.R = R;
+  sp.E = E;
+  sp.counts = counts;
+  return RF_OK;
+}
+
+}  // namespace
+
+extern "C" int rf_moe_ep_plan(const int32_t *counts, int32_t R, int32_t E, int32_t rank,
+                              const int32_t *slot_experts, const int32_t *slot_offsets, int32_t align,
+                              int32_t rounds, int64_t *send_splits, int64_t *recv_splits,
+                              int32_t *packed, int64_t packed_capacity, int64_t *layout) {
+  RF_CHECK_ARG(counts && slot_experts && slot_offsets && send_splits && recv_splits && layout,
+               "rf_moe_ep_plan: null pointer");
+  RF_CHECK_ARG(R >= 1 && E >= 1 && rank >= 0 && rank < R && align >= 1 && rounds >= 0,
+               "rf_moe_ep_plan: bad sizes");
+  Split sp;
+  {
+    const int rc = build_split(counts, R, E, slot_experts, slot_offsets, rounds, sp);
+    if (rc) return rc;
+  }
+  auto piece = [&](int e, int src, int h, int64_t *offset) -> int64_t { return sp.piece(e, src, h, offset); };
   // ---- send side
   std::vector<int64_t> seg_start(E, 0);
   for (int e = 1; e < E; ++e) seg_start[e] = seg_start[e - 1] + counts[(int64_t)rank * E + e - 1];
@@ -220,5 +249,24 @@ extern "C" int rf_moe_ep_plan(const int32_t *counts, int32_t R, int32_t E, int32
         posrow[pc.first + i] = (int32_t)p;
       }
   }
+  return RF_OK;
+}
+
+// M[s * R + d] = rows rank s sends to rank d this step (the all-to-all
+// matrix), derived from the same split as rf_moe_ep_plan: a rank can then
+// address its rows directly in a peer's receive buffer.
+extern "C" int rf_moe_ep_pair_rows(const int32_t *counts, int32_t R, int32_t E, const int32_t *slot_experts,
+                                   const int32_t *slot_offsets, int32_t rounds, int64_t *pair_rows) {
+  RF_CHECK_ARG(counts && slot_experts && slot_offsets && pair_rows, "rf_moe_ep_pair_rows: null pointer");
+  RF_CHECK_ARG(R >= 1 && E >= 1 && rounds >= 0, "rf_moe_ep_pair_rows: bad sizes");
+  Split sp;
+  const int rc = build_split(counts, R, E, slot_experts, slot_offsets, rounds, sp);
+  if (rc) return rc;
+  for (int src = 0; src < R; ++src)
+    for (int d = 0; d < R; ++d) {
+      int64_t n = 0;
+      for (int sl = slot_offsets[d]; sl < slot_offsets[d + 1]; ++sl) n += sp.piece(slot_experts[sl], src, d, nullptr);
+      pair_rows[(int64_t)src * R + d] = n;
+    }
   return RF_OK;
 }

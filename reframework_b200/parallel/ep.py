@@ -41,7 +41,8 @@ import torch.distributed as tdist
 import torch.nn as nn
 
 from .. import kernels as K
-from .._lib import ACTIVATIONS, RfMoeError, check, lib
+from .. import _lib as _lib_mod
+from .._lib import ACTIVATIONS, RfMoeError, check, dtype_code, lib, stream_of
 from ..moe.keys import expert_tensor
 from ..moe.moe_layer import FusedMoE, _bank_view, adjacent_router_weights
 from . import dist as _dist
@@ -211,6 +212,10 @@ class EPFusedMoE(nn.Module):
         self._slot_arrays = None
         self.split_rounds = 4         # water-filling passes of the per-step row split
         self.native_planner = True    # False: the numpy planner (same result, slower)
+        # rows cross NVLink as one-sided stores into peer buffers (one push
+        # kernel + a bounded flag wait per direction); False: NCCL all-to-alls
+        self.p2p = True
+        self._px = None
 
     # --------------------------------------------------------------- build
     @classmethod
@@ -382,6 +387,32 @@ class EPFusedMoE(nn.Module):
         slot[1].record()
         return out
 
+    def _pair_rows(self, cnt: np.ndarray) -> np.ndarray:
+        """The step's all-to-all matrix M[s, d] (rows s sends d), native."""
+        R, E = cnt.shape
+        cnt32 = np.ascontiguousarray(cnt, dtype=np.int32)
+        if self._slot_arrays is None or self._slot_arrays[0] is not self.placement:
+            flat = np.ascontiguousarray([e for s in self.placement.slots for e in s], dtype=np.int32)
+            offs = np.ascontiguousarray(np.cumsum([0] + [len(s) for s in self.placement.slots]), dtype=np.int32)
+            self._slot_arrays = (self.placement, flat, offs)
+        _, flat, offs = self._slot_arrays
+        M = np.zeros(R * R, dtype=np.int64)
+        check(lib().rf_moe_ep_pair_rows(cnt32.ctypes.data, R, E, flat.ctypes.data, offs.ctypes.data,
+                                        self.split_rounds, M.ctypes.data), "rf_moe_ep_pair_rows")
+        return M.reshape(R, R)
+
+    def _exchange(self):
+        if self._px is None:
+            from .p2p import PeerExchange
+            self._px = PeerExchange(self.ep_rank, self.ep_size, self.gate.device, self._pg())
+        return self._px
+
+    def close(self) -> None:
+        """Release the peer buffers (collective: every rank, after its last forward)."""
+        if self._px is not None:
+            self._px.close()
+            self._px = None
+
     def _native_plan(self, cnt: np.ndarray, n_mine: int):
         """Exchange plan from the native planner (rf_moe_ep_plan), written
         straight into a pinned buffer.  Returns (plan, pinned slot, layout)."""
@@ -435,12 +466,14 @@ class EPFusedMoE(nn.Module):
         if self.trace is not None:
             self.trace = []
         self._mark("start")
+        use_p2p = self.p2p and dev.type == "cuda"
         if T > 0:
             gate, sg = adjacent_router_weights(self, self.gate, self._shared_gate)
             w, ids32, _, _, sscale = K.router_topk(x2, gate, Kk, renormalize=self.renormalize,
                                                    bias=self.router_bias, round_dtype=rdt, entropy_k_min=ek,
                                                    shared_gate=sg)
-            p = K.permute(ids32, E, align=1, x=x2)
+            # the peer push reads token rows through src_slot: no permuted copy
+            p = K.permute(ids32, E, align=1, x=None if use_p2p else x2)
             counts = p.counts
         else:
             counts = torch.zeros(E, dtype=torch.int32, device=dev)
@@ -478,6 +511,9 @@ class EPFusedMoE(nn.Module):
         self.last_plan = plan
         gidx, inv, off, lc = views[:4]
         self._mark("plan+index copy")
+        if use_p2p:
+            return self._exchange_p2p(x2, res2, p if T > 0 else None, plan, views,
+                                      w if T > 0 else None, sscale if T > 0 else None, cnt)
         # (3) dispatch (rows reordered by destination only when replicas split an expert)
         if T == 0:
             send_rows = torch.empty(0, H, dtype=x2.dtype, device=dev)
@@ -494,14 +530,8 @@ class EPFusedMoE(nn.Module):
         if plan.recv_total > 0:
             xl = torch.empty(plan.rows_capacity, H, dtype=x2.dtype, device=dev)
             K.gather_rows(recv, gidx, xl)
-            w1b, w2b = self._gemm_banks()
-            h = torch.empty(plan.rows_capacity, I, dtype=x2.dtype, device=dev)
             self._mark("regroup gather")
-            K.grouped_gemm_gated(xl, w1b, off, lc, h, activation=self.activation)
-            self._mark("gated GEMM")
-            y = torch.empty(plan.rows_capacity, H, dtype=x2.dtype, device=dev)
-            K.grouped_gemm_down(h, w2b, off, lc, y)
-            self._mark("down GEMM")
+            y = self._expert_gemms(xl, plan, off, lc)
             K.gather_rows(y, inv, y_send)
         self._mark("return gather")
         # (5) return trip + combine on the token's rank
@@ -518,6 +548,74 @@ class EPFusedMoE(nn.Module):
             shared_y = K.dense_gated_mlp(x2, self._shared[0], self._shared[1], self.activation)
         out = K.combine(y_back, p.row_of_slot, w, out, shared_y=shared_y, shared_scale=sscale, residual=res2,
                         precise=self.precise_combine)
+        self._mark("unpermute+shared+combine")
+        return out
+
+    def _expert_gemms(self, xl: torch.Tensor, plan, off: torch.Tensor, lc: torch.Tensor) -> torch.Tensor:
+        """Grouped gated + down GEMMs over this rank's slot-major rows."""
+        I, H = self.intermediate_size, xl.shape[1]
+        w1b, w2b = self._gemm_banks()
+        h = torch.empty(plan.rows_capacity, I, dtype=xl.dtype, device=xl.device)
+        K.grouped_gemm_gated(xl, w1b, off, lc, h, activation=self.activation)
+        self._mark("gated GEMM")
+        y = torch.empty(plan.rows_capacity, H, dtype=xl.dtype, device=xl.device)
+        K.grouped_gemm_down(h, w2b, off, lc, y)
+        self._mark("down GEMM")
+        return y
+
+    def _exchange_p2p(self, x2, res2, p, plan, views, w, sscale, cnt) -> torch.Tensor:
+        """Steps 3-5 over peer memory: push token rows into the experts' ranks,
+        compute, push results back into the tokens' ranks, combine."""
+        from .p2p import DISPATCH, RETURN, matrix_offsets
+        dev = x2.device
+        T, H = x2.shape
+        Kk = self.top_k
+        gidx, inv, off, lc = views[:4]
+        row_bytes = H * x2.element_size()
+        M = self._pair_rows(cnt)
+        px = self._exchange()
+        px.ensure(int(M.sum(0).max()), int(M.sum(1).max()), row_bytes)
+        send_off, dst_row0, recv_off, back_row0 = matrix_offsets(M, self.ep_rank)
+        px.next_epoch()
+        px.push(DISPATCH, x2, send_off, dst_row0,
+                idx1=views[4] if (p is not None and plan.send_index is not None) else None,
+                idx2=None if p is None else p.src_slot, div=Kk)
+        self._mark("dispatch push")
+        px.wait(DISPATCH)
+        self._mark("dispatch wait")
+        st = stream_of(dev)
+        y = None
+        if plan.recv_total > 0:
+            xl = torch.empty(plan.rows_capacity, H, dtype=x2.dtype, device=dev)
+            check(lib().rf_moe_gather_rows(px.recv_ptr(), gidx.data_ptr(), 1, plan.rows_capacity, None, row_bytes,
+                                           xl.data_ptr(), st), "rf_moe_gather_rows")
+            self._mark("regroup gather")
+            y = self._expert_gemms(xl, plan, off, lc)
+        px.push(RETURN, y if y is not None else x2[:0], recv_off, back_row0,
+                idx1=inv if plan.recv_total > 0 else None)
+        self._mark("return push")
+        px.wait(RETURN)
+        self._mark("return wait")
+        out = torch.empty(T, H, dtype=x2.dtype, device=dev)
+        if T == 0:
+            return out
+        y_back = px.back_ptr()  # T*K rows in this rank's send order
+        keep = None
+        if plan.send_index is not None:  # back to the expert-major permuted order
+            keep = torch.empty(T * Kk, H, dtype=x2.dtype, device=dev)
+            check(lib().rf_moe_gather_rows(y_back, views[5].data_ptr(), 1, T * Kk, None, row_bytes,
+                                           keep.data_ptr(), st), "rf_moe_gather_rows")
+            y_back = keep.data_ptr()
+        shared_y = None
+        if self._shared is not None:
+            shared_y = K.dense_gated_mlp(x2, self._shared[0], self._shared[1], self.activation)
+        wf = w.contiguous()
+        mode = _lib_mod.COMBINE_FP32 if self.precise_combine else _lib_mod.COMBINE_REFERENCE
+        check(lib().rf_moe_combine(y_back, p.row_of_slot.data_ptr(), wf.data_ptr(), T, Kk, H,
+                                   dtype_code(x2.dtype), None if shared_y is None else shared_y.data_ptr(),
+                                   None if sscale is None else sscale.data_ptr(),
+                                   None if res2 is None else res2.data_ptr(), 0, mode, out.data_ptr(), st),
+              "rf_moe_combine")
         self._mark("unpermute+shared+combine")
         return out
 

@@ -155,6 +155,35 @@ def test_native_planner_matches_numpy_planner(seed):
             assert np.array_equal(seg(5)[seg(4)], np.arange(seg(4).size))
 
 
+@pytest.mark.parametrize("seed", range(8))
+def test_pair_rows_matrix_matches_every_ranks_plan(seed):
+    """rf_moe_ep_pair_rows: row s = rank s's send splits, column d = rank d's
+    receive splits (so one-sided pushes land where the all-to-all would put them)."""
+    from reframework_b200 import _lib
+    rng = np.random.default_rng(100 + seed)
+    R = int(rng.integers(1, 9))
+    E = int(rng.integers(R, 3 * R + 3))
+    shards = [shard_range(E, R, r) for r in range(R)]
+    cnt = np.stack([rng.multinomial(int(rng.integers(0, 300)), rng.dirichlet(np.full(E, 0.5)))
+                    for _ in range(R)]).astype(np.int32)
+    pl = place_experts(cnt.sum(0) + 1, shards, int(rng.integers(0, 3)))
+    flat = np.ascontiguousarray([e for s in pl.slots for e in s], dtype=np.int32)
+    offs = np.ascontiguousarray(np.cumsum([0] + [len(s) for s in pl.slots]), dtype=np.int32)
+    M = np.zeros(R * R, np.int64)
+    assert _lib.lib().rf_moe_ep_pair_rows(cnt.ctypes.data, R, E, flat.ctypes.data, offs.ctypes.data, 4,
+                                          M.ctypes.data) == 0
+    M = M.reshape(R, R)
+    for rank in range(R):
+        send = np.zeros(R, np.int64)
+        recv = np.zeros(R, np.int64)
+        lay = np.zeros(15, np.int64)
+        buf = np.zeros(4 * int(cnt.sum()) + 2048, np.int32)
+        assert _lib.lib().rf_moe_ep_plan(cnt.ctypes.data, R, E, rank, flat.ctypes.data, offs.ctypes.data, 128, 4,
+                                         send.ctypes.data, recv.ctypes.data, buf.ctypes.data, buf.size,
+                                         lay.ctypes.data) == 0
+        assert np.array_equal(M[rank], send) and np.array_equal(M[:, rank], recv)
+
+
 def test_native_planner_reports_small_buffer():
     from reframework_b200 import _lib
     cnt = np.array([[5, 3], [2, 7]], np.int32)

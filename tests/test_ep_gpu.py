@@ -66,6 +66,7 @@ def test_ep_single_rank_matches_fused(cuda_ok):
         assert max_rel(b, rec["out"]) < 1e-2
         assert ep.last_plan.recv_total == cfg.tokens * cfg.top_k
         assert _lib.device_status() == 0
+        ep.close()
     finally:
         D.destroy()
 
@@ -91,11 +92,18 @@ full = _build(cfg, d, dev)
 x = d["x"].to(dev)
 with torch.no_grad():
     ref = full(x)
-    rep = EPFusedMoE.from_full(full, world, rank, token_sharded=False)(x)   # reference contract
+    ep_rep = EPFusedMoE.from_full(full, world, rank, token_sharded=False)
+    rep = ep_rep(x)   # reference contract
     T = x.shape[0]
     lo, hi = T * rank // world, T * (rank + 1) // world
-    shard = EPFusedMoE.from_full(full, world, rank, token_sharded=True)(x[lo:hi])
+    ep_sh = EPFusedMoE.from_full(full, world, rank, token_sharded=True)
+    shard = ep_sh(x[lo:hi])          # rows cross NVLink as peer stores
+    ep_nc = EPFusedMoE.from_full(full, world, rank, token_sharded=True)
+    ep_nc.p2p = False
+    nccl = ep_nc(x[lo:hi])           # rows through NCCL all-to-alls
+    again = ep_sh(x[lo:hi])          # second step on the same peer buffers
 assert torch.equal(shard, ref[lo:hi]), "token-sharded rows differ from the single-process layer"
+assert torch.equal(nccl, shard) and torch.equal(again, shard), "peer-memory and NCCL exchanges differ"
 assert torch.equal(rep, ref), "replicated-contract output differs"
 assert max_rel(rep, rec["out"]) < 1e-2
 # redundant experts: replica weights fetched from their owners, rows of an
@@ -107,6 +115,10 @@ with torch.no_grad():
     assert sum(len(s) for s in pl.slots) > cfg.experts  # at least one replica somewhere
     bal = ep(x[lo:hi])
 assert torch.equal(bal, ref[lo:hi]), "rebalanced EP output differs"
+from reframework_b200 import _lib
+assert _lib.device_status() == 0, "a kernel set the device error word"
+for m in (ep_rep, ep_sh, ep_nc, ep):
+    m.close()
 D.barrier()
 D.destroy()
 print("rank", rank, "ok")

@@ -319,6 +319,47 @@ int rf_moe_ep_push_rows(const void *src, int64_t row_bytes, const int32_t *idx1,
                         uint32_t *done, rf_stream_t stream);
 int rf_moe_ep_wait(const int32_t *flags, int32_t R, int32_t epoch, rf_stream_t stream);
 
+/*
+ * The same exchange planned on the device (no host synchronisation per step).
+ * rf_moe_ep_devplan runs the split of rf_moe_ep_plan on the GPU from the
+ * all-gathered counts [R][E] (device) and the placement (slot_experts /
+ * slot_offsets, device copies of the host arrays; S = this rank's slot count,
+ * n_slots = all slots) into `workspace` (rf_moe_ep_devplan_workspace_size
+ * bytes): small tables — send pieces, per-peer offsets, the receive table and
+ * the slot-major GEMM segments.  recv_capacity / rows_capacity bound what the
+ * row kernels may write; a plan exceeding them is flagged (device error word)
+ * and moves no rows.
+ *   rf_moe_ep_devplan_push     dir 0: this rank's routed token rows (src = x,
+ *                              src_slot from rf_moe_permute, div = K; both may
+ *                              be NULL when this rank has no tokens) into the
+ *                              experts' ranks' receive buffers; dir 1: the GEMM
+ *                              output rows back into the tokens' ranks' return
+ *                              buffers; then flags as rf_moe_ep_push_rows
+ *   rf_moe_ep_devplan_regroup  receive buffer -> slot-major GEMM rows
+ *   rf_moe_ep_devplan_compose  row_of_slot -> row in this rank's return buffer
+ *                              (the combine reads the return buffer directly)
+ * rf_moe_ep_devplan_layout: byte offsets inside the workspace of
+ *   [0] int32 segment offsets [S+1], [1] int32 segment counts [S] (grouped
+ *   GEMM arguments), [2] int32 overflow, [3] int64 recv_total, [4] int64 n_send,
+ *   [5] workspace bytes, [6] int64 send_off [R+1], [7] int64 dst_row0 [R],
+ *   [8] int64 recv_off [R+1], [9] int64 back_row0 [R], [10] int32 identity,
+ *   [11] int64 rows used.
+ */
+size_t rf_moe_ep_devplan_workspace_size(int32_t R, int32_t E, int32_t S, int32_t n_slots);
+int rf_moe_ep_devplan_layout(int32_t R, int32_t E, int32_t S, int32_t n_slots, int64_t *out);
+int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_experts, const int32_t *slot_offsets,
+                      int32_t R, int32_t E, int32_t me, int32_t S, int32_t n_slots, int32_t align,
+                      int32_t rounds, int64_t recv_capacity, int64_t rows_capacity, void *workspace,
+                      size_t ws_bytes, rf_stream_t stream);
+int rf_moe_ep_devplan_push(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
+                           int32_t dir, const void *src, const int32_t *src_slot, int64_t div,
+                           int64_t row_bytes, void *const *dst, int32_t *const *flag, int32_t epoch,
+                           uint32_t *done, rf_stream_t stream);
+int rf_moe_ep_devplan_regroup(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
+                              const void *recv, void *xl, int64_t row_bytes, rf_stream_t stream);
+int rf_moe_ep_devplan_compose(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
+                              const int32_t *row_of_slot, int64_t n, int32_t *out, rf_stream_t stream);
+
 /* Summation modes of rf_moe_combine. */
 #define RF_COMBINE_REFERENCE 0  /* the reference's rounding points and order */
 #define RF_COMBINE_FP32 1       /* fp32 accumulation, one rounding */

@@ -1,0 +1,584 @@
+// Expert-parallel exchange planned on the device: no host synchronisation in
+// the EP forward.
+//
+// rf_moe_ep_plan (ep_plan.cu) derives every rank's split from the global
+// [R, E] counts on the host, which costs a device->host copy, host work and an
+// upload each step.  The planner kernel below runs the same deterministic
+// integer algorithm on the GPU from the all-gathered counts (one block: the
+// water-filling and sorts are tiny and run in thread 0; the table loops are
+// spread over the block) and writes small tables instead of per-row maps:
+//   * send pieces: send positions [pos_k, pos_{k+1}) carry permuted rows
+//     [src_k, ...) — the send order, grouped by destination rank;
+//   * per-destination send bounds and the first row of this rank's chunk in
+//     every destination's receive buffer; per-source receive bounds and the
+//     first row of each returned chunk in its source's return buffer;
+//   * the receive table c[s][j] (rows from source s for local slot j) with its
+//     prefix sums and the aligned slot-major segments of the local GEMM rows.
+// The row kernels (push, regroup, return, un-permute) locate each row with a
+// binary search in those tables.  Bit-for-bit the same plan as the host
+// planner: tests compare the two.
+#include <cstddef>
+#include <string>
+
+#include "common.cuh"
+
+RF_DEVICE_ERROR_WORD();
+
+namespace {
+
+constexpr int MAXR = 64;
+constexpr int MAXS = 1024;   // slots (experts + replicas) one rank holds
+constexpr int MAXP = 4096;   // send pieces of one rank
+
+}  // namespace
+
+// Fixed-size part of the device plan (tables sized by R and S follow it in
+// the same buffer: cs_prefix [R][S+1], cj_prefix [S][R+1], int64 each).
+struct RfEpDevPlan {
+  int64_t send_off[MAXR + 1];   // this rank's rows for destination d: send positions [send_off[d], send_off[d+1])
+  int64_t dst_row0[MAXR];       // ... landing at this row of d's receive buffer
+  int64_t recv_off[MAXR + 1];   // rows from source s: receive rows [recv_off[s], recv_off[s+1])
+  int64_t back_row0[MAXR];      // returned to s at this row of s's return buffer
+  int64_t piece_pos[MAXP + 1];  // send pieces (send order)
+  int64_t piece_src[MAXP];
+  int32_t piece_by_src[MAXP];   // piece indices ordered by piece_src (for the inverse lookup)
+  int32_t loff32[MAXS + 1];     // int32 copies of loff / lcount for the grouped GEMMs
+  int32_t lcount32[MAXS];
+  int64_t loff[MAXS + 1];       // local slot segments (aligned) and their row counts
+  int64_t lcount[MAXS];
+  int64_t n_send, recv_total, rows_used;
+  int32_t R, E, S, me, n_pieces, identity, overflow, pad_;
+};
+
+namespace {
+
+__device__ void waterfill_dev(int64_t n, const int64_t *base, int m, int64_t *out, int *order, int64_t *loads,
+                              int64_t *give) {
+  for (int i = 0; i < m; ++i) order[i] = i;
+  for (int i = 1; i < m; ++i) {  // stable insertion sort by base
+    const int v = order[i];
+    int j = i;
+    while (j > 0 && base[order[j - 1]] > base[v]) {
+      order[j] = order[j - 1];
+      --j;
+    }
+    order[j] = v;
+  }
+  for (int i = 0; i < m; ++i) loads[i] = base[order[i]];
+  int k = m;
+  auto prefix = [&](int kk) {
+    int64_t s = 0;
+    for (int i = 0; i < kk; ++i) s += loads[i];
+    return s;
+  };
+  while (k > 1 && n + prefix(k) <= loads[k - 1] * (int64_t)k) --k;
+  const int64_t level = (n + prefix(k)) / k;
+  int64_t used = 0;
+  for (int i = 0; i < m; ++i) give[i] = 0;
+  for (int i = 0; i < k; ++i) {
+    give[i] = level - loads[i] > 0 ? level - loads[i] : 0;
+    used += give[i];
+  }
+  int64_t rem = n - used;
+  for (int i = 0; rem > 0; ++i, --rem) give[i % k] += 1;
+  for (int pos = 0; pos < m; ++pos) out[order[pos]] = give[pos];
+}
+
+struct PlanScratch {  // global scratch of the planner (E x R tables)
+  int64_t *quota, *lo, *sbase, *total, *load;
+  int32_t *repl;
+};
+
+}  // namespace
+
+namespace {
+
+struct PlannerArgs {
+  const int32_t *counts;        // [R][E]
+  const int32_t *slot_experts;  // [total slots]
+  const int32_t *slot_offsets;  // [R+1]
+  int R, E, me, align, rounds;
+  int64_t recv_capacity, rows_capacity;  // buffers the row kernels may fill
+  RfEpDevPlan *plan;
+  int64_t *cs_prefix;           // [R][S+1]
+  int64_t *cj_prefix;           // [S][R+1]
+  PlanScratch sc;               // quota/lo/sbase [E*R], total [E], load [R], repl [E]
+  int64_t *M;                   // [R][R]
+  int32_t *hoff, *hlist;        // holders CSR: [E+1], [total slots]
+};
+
+__device__ int64_t piece_dev(const PlannerArgs &a, int e, int src, int h, int64_t *offset) {
+  const int R = a.R;
+  const int64_t qlo = a.sc.lo[(int64_t)e * R + h], qhi = qlo + a.sc.quota[(int64_t)e * R + h];
+  const int64_t slo = a.sc.sbase[(int64_t)e * R + src], shi = slo + a.counts[(int64_t)src * a.E + e];
+  const int64_t lo = qlo > slo ? qlo : slo, hi = qhi < shi ? qhi : shi;
+  if (offset) *offset = lo - slo;
+  return hi - lo > 0 ? hi - lo : 0;
+}
+
+__global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
+  const int R = a.R, E = a.E, me = a.me;
+  RfEpDevPlan *P = a.plan;
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) {
+    s_bad = 0;
+    int64_t *quota = a.sc.quota, *lo = a.sc.lo, *sbase = a.sc.sbase, *total = a.sc.total, *load = a.sc.load;
+    // holders of every expert, in rank order (CSR)
+    for (int e = 0; e <= E; ++e) a.hoff[e] = 0;
+    for (int r = 0; r < R; ++r)
+      for (int s = a.slot_offsets[r]; s < a.slot_offsets[r + 1]; ++s) {
+        const int e = a.slot_experts[s];
+        if (e < 0 || e >= E) s_bad = 1;
+        else a.hoff[e + 1] += 1;
+      }
+    for (int e = 0; e < E; ++e) a.hoff[e + 1] += a.hoff[e];
+    for (int e = 0; e < E; ++e) total[e] = 0;
+    for (int e = 0; e < E; ++e) a.sc.repl[e] = a.hoff[e];  // fill cursors
+    for (int r = 0; r < R && !s_bad; ++r)
+      for (int s = a.slot_offsets[r]; s < a.slot_offsets[r + 1]; ++s) a.hlist[a.sc.repl[a.slot_experts[s]]++] = r;
+    for (int r = 0; r < R; ++r)
+      for (int e = 0; e < E; ++e) {
+        const int32_t c = a.counts[(int64_t)r * E + e];
+        if (c < 0) s_bad = 1;
+        total[e] += c;
+      }
+    for (int e = 0; e < E; ++e)
+      if (a.hoff[e + 1] == a.hoff[e] && total[e] != 0) s_bad = 1;
+    // per-holder quota
+    int nrep = 0;
+    for (int64_t i = 0; i < (int64_t)E * R; ++i) quota[i] = 0;
+    for (int r = 0; r < R; ++r) load[r] = 0;
+    for (int e = 0; e < E && !s_bad; ++e) {
+      const int h0 = a.hoff[e], k = a.hoff[e + 1] - h0;
+      if (k == 0) continue;
+      if (k == 1) {
+        quota[(int64_t)e * R + a.hlist[h0]] = total[e];
+      } else {
+        a.sc.repl[nrep++] = e;
+        for (int i = 0; i < k; ++i) quota[(int64_t)e * R + a.hlist[h0 + i]] = total[e] / k + (i < total[e] % k ? 1 : 0);
+      }
+    }
+    for (int e = 0; e < E; ++e)
+      for (int r = 0; r < R; ++r) load[r] += quota[(int64_t)e * R + r];
+    for (int i = 1; i < nrep; ++i) {  // stable sort of the replicated experts by total, descending
+      const int v = a.sc.repl[i];
+      int j = i;
+      while (j > 0 && total[a.sc.repl[j - 1]] < total[v]) {
+        a.sc.repl[j] = a.sc.repl[j - 1];
+        --j;
+      }
+      a.sc.repl[j] = v;
+    }
+    int64_t base[MAXR], nq[MAXR], loads[MAXR], give[MAXR];
+    int order[MAXR];
+    for (int it = 0; it < a.rounds && !s_bad; ++it) {
+      bool changed = false;
+      for (int ri = 0; ri < nrep; ++ri) {
+        const int e = a.sc.repl[ri], h0 = a.hoff[e], k = a.hoff[e + 1] - h0;
+        if (k > MAXR) {
+          s_bad = 1;
+          break;
+        }
+        for (int i = 0; i < k; ++i) base[i] = load[a.hlist[h0 + i]] - quota[(int64_t)e * R + a.hlist[h0 + i]];
+        waterfill_dev(total[e], base, k, nq, order, loads, give);
+        for (int i = 0; i < k; ++i) {
+          int64_t &q = quota[(int64_t)e * R + a.hlist[h0 + i]];
+          if (q != nq[i]) {
+            load[a.hlist[h0 + i]] += nq[i] - q;
+            q = nq[i];
+            changed = true;
+          }
+        }
+      }
+      if (!changed) break;
+    }
+    // runs: holder h of expert e covers global rows [lo, lo + quota) (rank order)
+    for (int e = 0; e < E; ++e) {
+      int64_t acc = 0, src = 0;
+      for (int r = 0; r < R; ++r) {
+        lo[(int64_t)e * R + r] = acc;
+        acc += quota[(int64_t)e * R + r];
+        sbase[(int64_t)e * R + r] = src;
+        src += a.counts[(int64_t)r * E + e];
+      }
+    }
+  }
+  __syncthreads();
+  if (s_bad) {
+    if (threadIdx.x == 0) {
+      P->overflow = 1;
+      rf_report(RF_DEV_BAD_EXPERT_ID);
+    }
+    return;
+  }
+  // the all-to-all matrix M[s][d], one (s, d) pair per thread
+  for (int t = threadIdx.x; t < R * R; t += blockDim.x) {
+    const int s = t / R, d = t % R;
+    int64_t n = 0;
+    for (int sl = a.slot_offsets[d]; sl < a.slot_offsets[d + 1]; ++sl) n += piece_dev(a, a.slot_experts[sl], s, d, nullptr);
+    a.M[t] = n;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  // ---- this rank's tables
+  int bad = 0;
+  P->R = R;
+  P->E = E;
+  P->me = me;
+  const int s0 = a.slot_offsets[me], S = a.slot_offsets[me + 1] - s0;
+  if (S > MAXS || R > MAXR) bad = 1;
+  P->S = S;
+  // send side: pieces in destination order, each destination's slots in order
+  int64_t pos = 0;
+  int np = 0, identity = 1;
+  P->send_off[0] = 0;
+  for (int d = 0; d < R && !bad; ++d) {
+    for (int sl = a.slot_offsets[d]; sl < a.slot_offsets[d + 1]; ++sl) {
+      const int e = a.slot_experts[sl];
+      int64_t off = 0;
+      const int64_t ln = piece_dev(a, e, me, d, &off);
+      if (ln > 0) {
+        if (np >= MAXP) {
+          bad = 1;
+          break;
+        }
+        int64_t start = 0;  // first permuted row of expert e = rows of lower experts
+        for (int e2 = 0; e2 < e; ++e2) start += a.counts[(int64_t)me * E + e2];
+        start += off;
+        if (start != pos) identity = 0;
+        P->piece_pos[np] = pos;
+        P->piece_src[np] = start;
+        ++np;
+        pos += ln;
+      }
+    }
+    P->send_off[d + 1] = pos;
+  }
+  P->piece_pos[np] = pos;
+  P->n_pieces = np;
+  for (int k = 0; k < np; ++k) P->piece_by_src[k] = k;
+  for (int k = 1; k < np; ++k) {  // insertion sort by source row (pieces are disjoint)
+    const int v = P->piece_by_src[k];
+    int i = k;
+    while (i > 0 && P->piece_src[P->piece_by_src[i - 1]] > P->piece_src[v]) {
+      P->piece_by_src[i] = P->piece_by_src[i - 1];
+      --i;
+    }
+    P->piece_by_src[i] = v;
+  }
+  P->identity = identity;
+  P->n_send = pos;
+  // offsets inside the peers' buffers
+  for (int d = 0; d < R; ++d) {
+    int64_t below = 0, back = 0;
+    for (int s = 0; s < me; ++s) below += a.M[(int64_t)s * R + d];  // earlier sources' rows to d
+    P->dst_row0[d] = below;
+    for (int dd = 0; dd < me; ++dd) back += a.M[(int64_t)d * R + dd];  // d's rows to lower ranks
+    P->back_row0[d] = back;
+  }
+  // receive side: c[s][j], source bounds, slot segments and both prefix tables
+  P->recv_off[0] = 0;
+  for (int j = 0; j < S; ++j) P->lcount[j] = 0;
+  for (int s = 0; s < R && !bad; ++s) {
+    int64_t run = 0;
+    for (int j = 0; j < S; ++j) {
+      a.cs_prefix[(int64_t)s * (S + 1) + j] = run;
+      const int64_t c = piece_dev(a, a.slot_experts[s0 + j], s, me, nullptr);
+      a.cj_prefix[(int64_t)j * (R + 1) + s] = P->lcount[j];
+      P->lcount[j] += c;
+      run += c;
+    }
+    a.cs_prefix[(int64_t)s * (S + 1) + S] = run;
+    P->recv_off[s + 1] = P->recv_off[s] + run;
+  }
+  for (int j = 0; j < S; ++j) a.cj_prefix[(int64_t)j * (R + 1) + R] = P->lcount[j];
+  P->loff[0] = 0;
+  for (int j = 0; j < S; ++j) P->loff[j + 1] = P->loff[j] + (P->lcount[j] + a.align - 1) / a.align * a.align;
+  for (int j = 0; j <= S; ++j) P->loff32[j] = (int32_t)P->loff[j];
+  for (int j = 0; j < S; ++j) P->lcount32[j] = (int32_t)P->lcount[j];
+  P->recv_total = P->recv_off[R];
+  P->rows_used = P->loff[S];
+  if (P->recv_total > a.recv_capacity || P->rows_used > a.rows_capacity) bad = 1;
+  P->overflow = bad;
+  if (bad) rf_report(RF_DEV_BAD_EXPERT_ID);
+}
+
+}  // namespace
+
+namespace {
+
+// One 16-byte-aligned workspace per EP layer: the plan, its two prefix tables
+// and the planner's scratch.
+struct Layout {
+  size_t plan, cs, cj, quota, lo, sbase, total, load, repl, M, hoff, hlist, bytes;
+};
+
+size_t up16(size_t v) { return (v + 15) / 16 * 16; }
+
+Layout layout_of(int64_t R, int64_t E, int64_t S, int64_t nslots) {
+  Layout L;
+  size_t o = 0;
+  L.plan = o; o = up16(o + sizeof(RfEpDevPlan));
+  L.cs = o; o = up16(o + (size_t)R * (S + 1) * 8);
+  L.cj = o; o = up16(o + (size_t)S * (R + 1) * 8);
+  L.quota = o; o = up16(o + (size_t)E * R * 8);
+  L.lo = o; o = up16(o + (size_t)E * R * 8);
+  L.sbase = o; o = up16(o + (size_t)E * R * 8);
+  L.total = o; o = up16(o + (size_t)E * 8);
+  L.load = o; o = up16(o + (size_t)R * 8);
+  L.repl = o; o = up16(o + (size_t)E * 4);
+  L.M = o; o = up16(o + (size_t)R * R * 8);
+  L.hoff = o; o = up16(o + (size_t)(E + 1) * 4);
+  L.hlist = o; o = up16(o + (size_t)(nslots > 0 ? nslots : 1) * 4);
+  L.bytes = o;
+  return L;
+}
+
+// largest k in [0, n) with a[k] <= v (a ascending, a[0] <= v)
+__device__ __forceinline__ int find_le(const int64_t *a, int n, int64_t v) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (a[mid] <= v) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void copy_row(uint4 *t, const uint4 *s, int64_t vecs, int lane) {
+  int64_t v = lane;
+  for (; v + 96 < vecs; v += 128) {
+    const uint4 q0 = __ldg(s + v), q1 = __ldg(s + v + 32), q2 = __ldg(s + v + 64), q3 = __ldg(s + v + 96);
+    t[v] = q0;
+    t[v + 32] = q1;
+    t[v + 64] = q2;
+    t[v + 96] = q3;
+  }
+  for (; v < vecs; v += 32) t[v] = __ldg(s + v);
+}
+
+__device__ __forceinline__ void st_release_sys_dp(int32_t *p, int32_t v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+struct PlanPushArgs {
+  const RfEpDevPlan *plan;
+  const int64_t *cs, *cj;       // prefix tables of the plan
+  const uint8_t *src;
+  const int32_t *src_slot;      // dispatch: permuted row -> pair index (t*K+k)
+  int64_t div, row_bytes;
+  int R, S, ret;                // ret: 0 dispatch, 1 return
+  int32_t epoch;
+  uint32_t *done;
+  uint8_t *dst[MAXR];
+  int32_t *flag[MAXR];
+};
+
+// Dispatch (ret = 0): send positions i -> token rows, into the destinations'
+// receive buffers.  Return (ret = 1): receive rows q -> their local GEMM rows
+// of `src` (= y), into the sources' return buffers.  Either way the last block
+// raises this rank's flag in every peer, also when the plan overflowed (then
+// no row is written and the device error word is already set).
+__global__ void __launch_bounds__(256) plan_push_kernel(const __grid_constant__ PlanPushArgs a) {
+  const RfEpDevPlan *P = a.plan;
+  const int lane = threadIdx.x & 31;
+  const int R = a.R, S = a.S;
+  const int64_t vecs = a.row_bytes / 16;
+  const int64_t n = P->overflow ? 0 : (a.ret ? P->recv_total : P->n_send);
+  const int64_t nwarps = (int64_t)gridDim.x * 8;
+  for (int64_t i = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); i < n; i += nwarps) {
+    int64_t srow, drow;
+    int d;
+    if (!a.ret) {
+      const int k = find_le(P->piece_pos, P->n_pieces, i);
+      const int64_t j = P->piece_src[k] + (i - P->piece_pos[k]);
+      srow = (int64_t)a.src_slot[j] / a.div;
+      d = find_le(P->send_off, R, i);
+      drow = P->dst_row0[d] + (i - P->send_off[d]);
+    } else {
+      d = find_le(P->recv_off, R, i);
+      const int64_t q2 = i - P->recv_off[d];
+      const int64_t *cs = a.cs + (int64_t)d * (S + 1);
+      const int j = find_le(cs, S, q2);
+      srow = P->loff[j] + a.cj[(int64_t)j * (R + 1) + d] + (q2 - cs[j]);
+      drow = P->back_row0[d] + q2;
+    }
+    copy_row(reinterpret_cast<uint4 *>(a.dst[d] + drow * a.row_bytes),
+             reinterpret_cast<const uint4 *>(a.src + srow * a.row_bytes), vecs, lane);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const uint32_t prev = atomicAdd(a.done, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int d = 0; d < R; ++d) st_release_sys_dp(a.flag[d], a.epoch);
+      *a.done = 0u;
+    }
+  }
+}
+
+// Local GEMM rows (slot-major, aligned segments) from the receive buffer;
+// pad rows are left untouched (their GEMM outputs are never stored).
+__global__ void __launch_bounds__(256) plan_regroup_kernel(const RfEpDevPlan *P, const int64_t *cs_all,
+                                                           const int64_t *cj_all, const uint8_t *recv, uint8_t *xl,
+                                                           int64_t row_bytes, int R, int S) {
+  const int lane = threadIdx.x & 31;
+  const int64_t vecs = row_bytes / 16;
+  const int64_t n = P->overflow ? 0 : P->rows_used;
+  const int64_t nwarps = (int64_t)gridDim.x * 8;
+  for (int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); r < n; r += nwarps) {
+    const int j = find_le(P->loff, S, r);
+    const int64_t k = r - P->loff[j];
+    if (k >= P->lcount[j]) continue;
+    const int64_t *cj = cj_all + (int64_t)j * (R + 1);
+    const int s = find_le(cj, R, k);
+    const int64_t q = P->recv_off[s] + cs_all[(int64_t)s * (S + 1) + j] + (k - cj[s]);
+    copy_row(reinterpret_cast<uint4 *>(xl + r * row_bytes), reinterpret_cast<const uint4 *>(recv + q * row_bytes),
+             vecs, lane);
+  }
+}
+
+// row_of_slot (permuted row per (t, k)) -> that row's position in the return
+// buffer (= its send position); -1 stays -1.
+__global__ void plan_compose_kernel(const RfEpDevPlan *P, const int32_t *row_of_slot, int64_t n, int32_t *out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t j = row_of_slot[i];
+    if (j < 0 || P->overflow) {
+      out[i] = -1;
+      continue;
+    }
+    int lo = 0, hi = P->n_pieces - 1;  // last piece (in source order) starting at or before j
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (P->piece_src[P->piece_by_src[mid]] <= j) lo = mid;
+      else hi = mid - 1;
+    }
+    const int k = P->piece_by_src[lo];
+    out[i] = (int32_t)(P->piece_pos[k] + (j - P->piece_src[k]));
+  }
+}
+
+}  // namespace
+
+extern "C" size_t rf_moe_ep_devplan_workspace_size(int32_t R, int32_t E, int32_t S, int32_t n_slots) {
+  if (R < 1 || E < 1 || S < 0 || n_slots < 0) return 0;
+  return layout_of(R, E, S, n_slots).bytes;
+}
+
+extern "C" int rf_moe_ep_devplan_layout(int32_t R, int32_t E, int32_t S, int32_t n_slots, int64_t *out) {
+  RF_CHECK_ARG(out && R >= 1 && E >= 1 && S >= 0 && n_slots >= 0, "rf_moe_ep_devplan_layout: bad arguments");
+  const Layout L = layout_of(R, E, S, n_slots);
+  out[0] = (int64_t)(L.plan + offsetof(RfEpDevPlan, loff32));    // int32 [S+1] GEMM segment offsets
+  out[1] = (int64_t)(L.plan + offsetof(RfEpDevPlan, lcount32));  // int32 [S]   GEMM segment counts
+  out[2] = (int64_t)(L.plan + offsetof(RfEpDevPlan, overflow));  // int32       overflow flag
+  out[3] = (int64_t)(L.plan + offsetof(RfEpDevPlan, recv_total));
+  out[4] = (int64_t)(L.plan + offsetof(RfEpDevPlan, n_send));
+  out[5] = (int64_t)L.bytes;
+  out[6] = (int64_t)(L.plan + offsetof(RfEpDevPlan, send_off));   // int64 [R+1]
+  out[7] = (int64_t)(L.plan + offsetof(RfEpDevPlan, dst_row0));   // int64 [R]
+  out[8] = (int64_t)(L.plan + offsetof(RfEpDevPlan, recv_off));   // int64 [R+1]
+  out[9] = (int64_t)(L.plan + offsetof(RfEpDevPlan, back_row0));  // int64 [R]
+  out[10] = (int64_t)(L.plan + offsetof(RfEpDevPlan, identity));  // int32
+  out[11] = (int64_t)(L.plan + offsetof(RfEpDevPlan, rows_used)); // int64
+  return RF_OK;
+}
+
+extern "C" int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_experts, const int32_t *slot_offsets,
+                                 int32_t R, int32_t E, int32_t me, int32_t S, int32_t n_slots, int32_t align,
+                                 int32_t rounds, int64_t recv_capacity, int64_t rows_capacity, void *workspace,
+                                 size_t ws_bytes, rf_stream_t stream) {
+  RF_CHECK_ARG(counts && slot_experts && slot_offsets && workspace, "rf_moe_ep_devplan: null pointer");
+  RF_CHECK_ARG(R >= 1 && R <= MAXR && E >= 1 && me >= 0 && me < R && S >= 0 && S <= MAXS && align >= 1 &&
+                   rounds >= 0,
+               "rf_moe_ep_devplan: bad sizes (R <= 64, slots per rank <= 1024)");
+  const Layout L = layout_of(R, E, S, n_slots);
+  RF_CHECK_ARG(ws_bytes >= L.bytes && (uintptr_t)workspace % 16 == 0, "rf_moe_ep_devplan: workspace too small");
+  uint8_t *w = reinterpret_cast<uint8_t *>(workspace);
+  PlannerArgs a;
+  a.counts = counts;
+  a.slot_experts = slot_experts;
+  a.slot_offsets = slot_offsets;
+  a.R = R;
+  a.E = E;
+  a.me = me;
+  a.align = align;
+  a.rounds = rounds;
+  a.recv_capacity = recv_capacity;
+  a.rows_capacity = rows_capacity;
+  a.plan = reinterpret_cast<RfEpDevPlan *>(w + L.plan);
+  a.cs_prefix = reinterpret_cast<int64_t *>(w + L.cs);
+  a.cj_prefix = reinterpret_cast<int64_t *>(w + L.cj);
+  a.sc.quota = reinterpret_cast<int64_t *>(w + L.quota);
+  a.sc.lo = reinterpret_cast<int64_t *>(w + L.lo);
+  a.sc.sbase = reinterpret_cast<int64_t *>(w + L.sbase);
+  a.sc.total = reinterpret_cast<int64_t *>(w + L.total);
+  a.sc.load = reinterpret_cast<int64_t *>(w + L.load);
+  a.sc.repl = reinterpret_cast<int32_t *>(w + L.repl);
+  a.M = reinterpret_cast<int64_t *>(w + L.M);
+  a.hoff = reinterpret_cast<int32_t *>(w + L.hoff);
+  a.hlist = reinterpret_cast<int32_t *>(w + L.hlist);
+  ep_planner_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(a);
+  return rf::check_launch("rf_moe_ep_devplan");
+}
+
+// dir 0: dispatch (src = token rows x, src_slot/div map send positions to them);
+// dir 1: return (src = the local GEMM output rows).
+extern "C" int rf_moe_ep_devplan_push(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
+                                      int32_t dir, const void *src, const int32_t *src_slot, int64_t div,
+                                      int64_t row_bytes, void *const *dst, int32_t *const *flag, int32_t epoch,
+                                      uint32_t *done, rf_stream_t stream) {
+  RF_CHECK_ARG(workspace && dst && flag && done && (dir == 0 || dir == 1), "rf_moe_ep_devplan_push: bad arguments");
+  RF_CHECK_ARG(R >= 1 && R <= MAXR && row_bytes > 0 && row_bytes % 16 == 0 && div >= 1,
+               "rf_moe_ep_devplan_push: bad sizes");
+  RF_CHECK_ARG((uintptr_t)src % 16 == 0, "rf_moe_ep_devplan_push: source must be 16-byte aligned");
+  const Layout L = layout_of(R, E, S, n_slots);
+  const uint8_t *w = reinterpret_cast<const uint8_t *>(workspace);
+  PlanPushArgs a;
+  a.plan = reinterpret_cast<const RfEpDevPlan *>(w + L.plan);
+  a.cs = reinterpret_cast<const int64_t *>(w + L.cs);
+  a.cj = reinterpret_cast<const int64_t *>(w + L.cj);
+  a.src = reinterpret_cast<const uint8_t *>(src);
+  a.src_slot = src_slot;
+  a.div = div;
+  a.row_bytes = row_bytes;
+  a.R = R;
+  a.S = S;
+  a.ret = dir;
+  a.epoch = epoch;
+  a.done = done;
+  for (int d = 0; d < R; ++d) {
+    RF_CHECK_ARG(flag[d], "rf_moe_ep_devplan_push: missing flag");
+    a.dst[d] = reinterpret_cast<uint8_t *>(dst[d]);
+    a.flag[d] = flag[d];
+  }
+  plan_push_kernel<<<rf::num_sms() * 4, 256, 0, (cudaStream_t)stream>>>(a);
+  return rf::check_launch("rf_moe_ep_devplan_push");
+}
+
+extern "C" int rf_moe_ep_devplan_regroup(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
+                                         const void *recv, void *xl, int64_t row_bytes, rf_stream_t stream) {
+  RF_CHECK_ARG(workspace && recv && xl && R >= 1 && R <= MAXR && row_bytes % 16 == 0,
+               "rf_moe_ep_devplan_regroup: bad arguments");
+  const Layout L = layout_of(R, E, S, n_slots);
+  const uint8_t *w = reinterpret_cast<const uint8_t *>(workspace);
+  if (S == 0) return RF_OK;
+  plan_regroup_kernel<<<rf::num_sms() * 4, 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const RfEpDevPlan *>(w + L.plan), reinterpret_cast<const int64_t *>(w + L.cs),
+      reinterpret_cast<const int64_t *>(w + L.cj), reinterpret_cast<const uint8_t *>(recv),
+      reinterpret_cast<uint8_t *>(xl), row_bytes, R, S);
+  return rf::check_launch("rf_moe_ep_devplan_regroup");
+}
+
+extern "C" int rf_moe_ep_devplan_compose(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
+                                         const int32_t *row_of_slot, int64_t n, int32_t *out, rf_stream_t stream) {
+  RF_CHECK_ARG(workspace && (n == 0 || (row_of_slot && out)), "rf_moe_ep_devplan_compose: bad arguments");
+  if (n == 0) return RF_OK;
+  const Layout L = layout_of(R, E, S, n_slots);
+  const uint8_t *w = reinterpret_cast<const uint8_t *>(workspace);
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > (int64_t)rf::num_sms() * 8) blocks = (int64_t)rf::num_sms() * 8;
+  plan_compose_kernel<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const RfEpDevPlan *>(w + L.plan), row_of_slot, n, out);
+  return rf::check_launch("rf_moe_ep_devplan_compose");
+}

@@ -19,6 +19,25 @@ def header_functions():
     return sorted(set(re.findall(r"\b(rf_moe_[a-z0-9_]+)\s*\(", src)))
 
 
+def header_arity():
+    """{function: number of parameters} from the prototypes in rf_moe.h."""
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\b(rf_moe_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", src):
+        params = params.strip()
+        out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_bindings_match_header_arity():
+    """Every binding passes exactly as many arguments as the C prototype takes."""
+    arity = header_arity()
+    assert arity, "no prototypes parsed"
+    for name, (_, argtypes) in _lib._SIGNATURES.items():
+        assert len(argtypes) == arity[name], f"{name}: ctypes {len(argtypes)} args, header {arity[name]}"
+
+
 def test_library_exports_every_declared_symbol():
     lib = _lib.lib()
     names = header_functions()

@@ -143,3 +143,118 @@ def test_ep_two_ranks_match_single_process(cuda_ok):
         outs.append(out)
     for r, (p, out) in enumerate(zip(procs, outs)):
         assert p.returncode == 0, f"rank {r} failed:\n{out[-3000:]}"
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_device_plan_matches_host_plan_and_round_trips(cuda_ok, seed):
+    """rf_moe_ep_devplan == rf_moe_ep_plan / rf_moe_ep_pair_rows for every rank,
+    and dispatch -> regroup -> return -> compose through the device plan hands
+    every (token, slot) its own row back.  R ranks are emulated on one GPU with
+    separate buffers; only the push kernels run (nothing waits here)."""
+    import ctypes
+    import numpy as np
+    from reframework_b200 import _lib
+    from reframework_b200 import kernels as K
+    from reframework_b200.parallel.ep import shard_range
+    from reframework_b200.parallel.eplb import place_experts
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(seed)
+    R = int(rng.integers(1, 7))
+    E = int(rng.integers(R, 3 * R + 4))
+    topk = int(rng.integers(1, min(E, 4) + 1))
+    H = 64
+    shards = [shard_range(E, R, r) for r in range(R)]
+    Ts = [int(rng.integers(0, 200)) for _ in range(R)]
+    xs, perms = [], []
+    g = torch.Generator().manual_seed(seed)
+    for r in range(R):
+        xs.append(torch.randn(Ts[r], H, generator=g).bfloat16().to(dev))
+        ids = torch.stack([torch.randperm(E, generator=g)[:topk] for _ in range(Ts[r])]) if Ts[r] else \
+            torch.zeros(0, topk, dtype=torch.int64)
+        perms.append(K.permute(ids.int().to(dev), E, align=1))
+    cnt = torch.stack([p.counts for p in perms]).contiguous()
+    cnt_np = cnt.cpu().numpy().astype(np.int32)
+    pl = place_experts(cnt_np.sum(0) + 1, shards, int(rng.integers(0, 3)))
+    flat = np.ascontiguousarray([e for s in pl.slots for e in s], dtype=np.int32)
+    offs = np.ascontiguousarray(np.cumsum([0] + [len(s) for s in pl.slots]), dtype=np.int32)
+    flat_d, offs_d = torch.from_numpy(flat).to(dev), torch.from_numpy(offs).to(dev)
+    M = np.zeros(R * R, np.int64)
+    assert L.rf_moe_ep_pair_rows(cnt_np.ctypes.data, R, E, flat.ctypes.data, offs.ctypes.data, 4, M.ctypes.data) == 0
+    M = M.reshape(R, R)
+    row_bytes = H * 2
+    st = torch.cuda.current_stream(dev).cuda_stream
+    nslots = int(flat.size)
+    cap_recv = max(sum(Ts) * topk, 1)
+    recv = [torch.zeros(cap_recv, H, dtype=torch.bfloat16, device=dev) for _ in range(R)]
+    back = [torch.zeros(max(Ts[r] * topk, 1), H, dtype=torch.bfloat16, device=dev) for r in range(R)]
+    ctrl = [torch.zeros(2 * R + 4, dtype=torch.int32, device=dev) for _ in range(R)]
+    ws, lay = [], []
+    for me in range(R):
+        S = len(pl.slots[me])
+        nb = L.rf_moe_ep_devplan_workspace_size(R, E, S, nslots)
+        w = torch.zeros(nb, dtype=torch.uint8, device=dev)
+        lo = np.zeros(12, np.int64)
+        assert L.rf_moe_ep_devplan_layout(R, E, S, nslots, lo.ctypes.data) == 0
+        rows_cap = cap_recv + S * 128
+        assert L.rf_moe_ep_devplan(cnt.data_ptr(), flat_d.data_ptr(), offs_d.data_ptr(), R, E, me, S, nslots, 128, 4,
+                                   cap_recv, rows_cap, w.data_ptr(), nb, st) == 0
+        ws.append(w)
+        lay.append(lo)
+    torch.cuda.synchronize()
+    for me in range(R):
+        S = len(pl.slots[me])
+        wb, lo = ws[me].cpu().numpy(), lay[me]
+        i64 = lambda off, n: wb[off:off + 8 * n].view(np.int64)
+        i32 = lambda off, n: wb[off:off + 4 * n].view(np.int32)
+        send = np.zeros(R, np.int64)
+        recvs = np.zeros(R, np.int64)
+        hl = np.zeros(15, np.int64)
+        buf = np.zeros(4 * int(cnt_np.sum()) + 4096, np.int32)
+        assert L.rf_moe_ep_plan(cnt_np.ctypes.data, R, E, me, flat.ctypes.data, offs.ctypes.data, 128, 4,
+                                send.ctypes.data, recvs.ctypes.data, buf.ctypes.data, buf.size, hl.ctypes.data) == 0
+        assert i32(lo[2], 1)[0] == 0, "device plan overflowed"
+        assert np.array_equal(i64(lo[6], R + 1), np.concatenate([[0], np.cumsum(send)]))
+        assert np.array_equal(i64(lo[8], R + 1), np.concatenate([[0], np.cumsum(recvs)]))
+        assert np.array_equal(i64(lo[7], R), M[:me].sum(0) if me else np.zeros(R))
+        assert np.array_equal(i64(lo[9], R), M[:, :me].sum(1) if me else np.zeros(R))
+        seg = lambda i: buf[hl[2 * i]:hl[2 * i] + hl[2 * i + 1]]
+        assert np.array_equal(i32(lo[0], S + 1), seg(2)) and np.array_equal(i32(lo[1], S), seg(3))
+        assert i32(lo[10], 1)[0] == hl[13] and i64(lo[11], 1)[0] == hl[12]
+
+    def ptrs(ts):
+        return (ctypes.c_void_p * R)(*[t.data_ptr() for t in ts])
+
+    done = torch.zeros(R, dtype=torch.int32, device=dev)
+    for me in range(R):  # dispatch pushes
+        S = len(pl.slots[me])
+        flags = (ctypes.c_void_p * R)(*[ctrl[d].data_ptr() + 4 * me for d in range(R)])
+        src = xs[me] if Ts[me] else recv[me][:0]
+        assert L.rf_moe_ep_devplan_push(ws[me].data_ptr(), R, E, S, nslots, 0, src.data_ptr(),
+                                        perms[me].src_slot.data_ptr(), topk, row_bytes, ptrs(recv), flags, 7,
+                                        done.data_ptr() + 4 * me, st) == 0
+    ys = []
+    for me in range(R):  # regroup; the "experts" return their input rows
+        S = len(pl.slots[me])
+        xl = torch.zeros(cap_recv + S * 128, H, dtype=torch.bfloat16, device=dev)
+        assert L.rf_moe_ep_devplan_regroup(ws[me].data_ptr(), R, E, S, nslots, recv[me].data_ptr(), xl.data_ptr(),
+                                           row_bytes, st) == 0
+        ys.append(xl)
+    for me in range(R):  # return pushes
+        S = len(pl.slots[me])
+        flags = (ctypes.c_void_p * R)(*[ctrl[d].data_ptr() + 4 * (R + me) for d in range(R)])
+        assert L.rf_moe_ep_devplan_push(ws[me].data_ptr(), R, E, S, nslots, 1, ys[me].data_ptr(), None, 1, row_bytes,
+                                        ptrs(back), flags, 7, done.data_ptr() + 4 * me, st) == 0
+    for me in range(R):
+        if Ts[me] == 0:
+            continue
+        S = len(pl.slots[me])
+        pos = torch.empty(Ts[me] * topk, dtype=torch.int32, device=dev)
+        assert L.rf_moe_ep_devplan_compose(ws[me].data_ptr(), R, E, S, nslots, perms[me].row_of_slot.data_ptr(),
+                                           Ts[me] * topk, pos.data_ptr(), st) == 0
+        got = back[me][pos.long()]
+        want = xs[me].repeat_interleave(topk, 0)
+        assert torch.equal(got, want), f"rank {me}: rows did not come back"
+    torch.cuda.synchronize()
+    assert all(bool((c[:2 * R] == 7).all()) for c in ctrl), "every rank raised its flags in every peer"
+    assert _lib.device_status() == 0

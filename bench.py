@@ -225,10 +225,19 @@ def e2e_run(fwd, xh, steps, dev):
 
 # router x2 (tensor-core logits, top-k), permute x3 (histogram, scatter, gather), gated GEMM, down GEMM, combine
 LAUNCHES_PER_FORWARD = 8
-# EP over peer memory: router x2, permute x2 (histogram, scatter), dispatch push + wait, regroup gather,
-# gated GEMM, down GEMM, return push + wait, combine (+ the un-permute gather when replicas split an
-# expert); NCCL's own kernels (the counts all-gather) are not counted
-EP_LAUNCHES_PER_FORWARD = 12
+# EP, exchange planned on the device and carried over peer memory: router x2, permute x2 (histogram,
+# scatter), planner, dispatch push + wait, regroup gather, gated GEMM, down GEMM, return push + wait,
+# combine; NCCL's own kernels (the counts all-gather) are not counted
+EP_LAUNCHES_PER_FORWARD = 13
+
+
+def ep_launches(layer) -> int:
+    """Launches of one EP forward (host-planned exchange: no planner kernel, and
+    one more gather when replicas reorder the sent rows)."""
+    if layer.p2p and layer.device_plan:
+        return EP_LAUNCHES_PER_FORWARD
+    plan = layer.last_plan
+    return EP_LAUNCHES_PER_FORWARD - 1 + (1 if plan is not None and plan.send_index is not None else 0)
 
 
 def run_gpu(args):
@@ -343,8 +352,7 @@ def run_gpu(args):
                 "d2h_bytes_per_step": x.numel() * x.element_size(),
                 "ms_per_step": ms_e2e, "api": "FusedMoE.forward" if world == 1 else "EPFusedMoE.forward",
                 "pipeline": "H2D of step i+1 and D2H of step i on two copy streams overlap step i's forward"},
-        "gpu_launches": args.steps * (LAUNCHES_PER_FORWARD if world == 1 else
-                                      EP_LAUNCHES_PER_FORWARD + (1 if layer.last_plan.send_index is not None else 0)),
+        "gpu_launches": args.steps * (LAUNCHES_PER_FORWARD if world == 1 else ep_launches(layer)),
         "clocks": clk,
     }
     if stage_fn:

@@ -334,10 +334,12 @@ int rf_moe_ep_wait(const int32_t *flags, int32_t R, int32_t epoch, rf_stream_t s
  *                              be NULL when this rank has no tokens) into the
  *                              experts' ranks' receive buffers; dir 1: the GEMM
  *                              output rows back into the tokens' ranks' return
- *                              buffers; then flags as rf_moe_ep_push_rows
+ *                              buffers, each at its permuted row there (the
+ *                              token rank's rf_moe_permute layout, align 1), so
+ *                              rf_moe_combine reads the return buffer through
+ *                              that permute's row_of_slot; then flags as
+ *                              rf_moe_ep_push_rows
  *   rf_moe_ep_devplan_regroup  receive buffer -> slot-major GEMM rows
- *   rf_moe_ep_devplan_compose  row_of_slot -> row in this rank's return buffer
- *                              (the combine reads the return buffer directly)
  * rf_moe_ep_devplan_layout: byte offsets inside the workspace of
  *   [0] int32 segment offsets [S+1], [1] int32 segment counts [S] (grouped
  *   GEMM arguments), [2] int32 overflow, [3] int64 recv_total, [4] int64 n_send,
@@ -357,8 +359,6 @@ int rf_moe_ep_devplan_push(const void *workspace, int32_t R, int32_t E, int32_t 
                            uint32_t *done, rf_stream_t stream);
 int rf_moe_ep_devplan_regroup(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
                               const void *recv, void *xl, int64_t row_bytes, rf_stream_t stream);
-int rf_moe_ep_devplan_compose(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
-                              const int32_t *row_of_slot, int64_t n, int32_t *out, rf_stream_t stream);
 
 /* Summation modes of rf_moe_combine. */
 #define RF_COMBINE_REFERENCE 0  /* the reference's rounding points and order */

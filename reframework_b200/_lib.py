@@ -78,8 +78,6 @@ _SIGNATURES = {
                                                                             _c_void_p, _c_void_p, ctypes.c_int32,
                                                                             _c_void_p, _c_void_p]),
     "rf_moe_ep_devplan_regroup": (_int, [_c_void_p] + [ctypes.c_int32] * 4 + [_c_void_p, _c_void_p, _i64, _c_void_p]),
-    "rf_moe_ep_devplan_compose": (_int, [_c_void_p] + [ctypes.c_int32] * 4 + [_c_void_p, _i64, _c_void_p,
-                                                                               _c_void_p]),
     "rf_moe_ep_plan": (_int, [_c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_void_p, _c_void_p,
                               ctypes.c_int32, ctypes.c_int32, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
 }

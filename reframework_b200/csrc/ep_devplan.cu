@@ -10,13 +10,16 @@
 //   * send pieces: send positions [pos_k, pos_{k+1}) carry permuted rows
 //     [src_k, ...) — the send order, grouped by destination rank;
 //   * per-destination send bounds and the first row of this rank's chunk in
-//     every destination's receive buffer; per-source receive bounds and the
-//     first row of each returned chunk in its source's return buffer;
+//     every destination's receive buffer; per-source receive bounds;
 //   * the receive table c[s][j] (rows from source s for local slot j) with its
-//     prefix sums and the aligned slot-major segments of the local GEMM rows.
-// The row kernels (push, regroup, return, un-permute) locate each row with a
-// binary search in those tables.  Bit-for-bit the same plan as the host
-// planner: tests compare the two.
+//     prefix sums, the aligned slot-major segments of the local GEMM rows, and
+//     p[s][j], the source's permuted row of the first of those rows.
+// The row kernels (push, regroup, return) locate each row with a binary
+// search in those tables.  The return push writes every result row at its
+// permuted (expert-major) row in the source's return buffer, so the combine
+// reads the rows through the permute's own row_of_slot and sums each token's
+// rows in ascending expert order, whichever rank computed them.  Bit-for-bit
+// the same split as the host planner: tests compare the two.
 #include <cstddef>
 #include <string>
 
@@ -33,15 +36,15 @@ constexpr int MAXP = 4096;   // send pieces of one rank
 }  // namespace
 
 // Fixed-size part of the device plan (tables sized by R and S follow it in
-// the same buffer: cs_prefix [R][S+1], cj_prefix [S][R+1], int64 each).
+// the same buffer: cs_prefix [R][S+1], cj_prefix [S][R+1], pstart [R][S],
+// int64 each).
 struct RfEpDevPlan {
   int64_t send_off[MAXR + 1];   // this rank's rows for destination d: send positions [send_off[d], send_off[d+1])
   int64_t dst_row0[MAXR];       // ... landing at this row of d's receive buffer
   int64_t recv_off[MAXR + 1];   // rows from source s: receive rows [recv_off[s], recv_off[s+1])
-  int64_t back_row0[MAXR];      // returned to s at this row of s's return buffer
+  int64_t back_row0[MAXR];      // rows of s's earlier destinations (the host plan's return offset)
   int64_t piece_pos[MAXP + 1];  // send pieces (send order)
   int64_t piece_src[MAXP];
-  int32_t piece_by_src[MAXP];   // piece indices ordered by piece_src (for the inverse lookup)
   int32_t loff32[MAXS + 1];     // int32 copies of loff / lcount for the grouped GEMMs
   int32_t lcount32[MAXS];
   int64_t loff[MAXS + 1];       // local slot segments (aligned) and their row counts
@@ -102,6 +105,8 @@ struct PlannerArgs {
   RfEpDevPlan *plan;
   int64_t *cs_prefix;           // [R][S+1]
   int64_t *cj_prefix;           // [S][R+1]
+  int64_t *pstart;              // [R][S]: permuted row in source s of its first row for slot j
+  int64_t *cpre;                // [R][E+1]: rows of source s routed to experts below e
   PlanScratch sc;               // quota/lo/sbase [E*R], total [E], load [R], repl [E]
   int64_t *M;                   // [R][R]
   int32_t *hoff, *hlist;        // holders CSR: [E+1], [total slots]
@@ -211,12 +216,18 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
     }
     return;
   }
-  // the all-to-all matrix M[s][d], one (s, d) pair per thread
+  // the all-to-all matrix M[s][d], one (s, d) pair per thread, and every
+  // source's expert-major row starts (its permuted layout, align 1)
   for (int t = threadIdx.x; t < R * R; t += blockDim.x) {
     const int s = t / R, d = t % R;
     int64_t n = 0;
     for (int sl = a.slot_offsets[d]; sl < a.slot_offsets[d + 1]; ++sl) n += piece_dev(a, a.slot_experts[sl], s, d, nullptr);
     a.M[t] = n;
+  }
+  for (int s = threadIdx.x; s < R; s += blockDim.x) {
+    int64_t *c = a.cpre + (int64_t)s * (E + 1);
+    c[0] = 0;
+    for (int e = 0; e < E; ++e) c[e + 1] = c[e] + a.counts[(int64_t)s * E + e];
   }
   __syncthreads();
   if (threadIdx.x != 0) return;
@@ -242,9 +253,7 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
           bad = 1;
           break;
         }
-        int64_t start = 0;  // first permuted row of expert e = rows of lower experts
-        for (int e2 = 0; e2 < e; ++e2) start += a.counts[(int64_t)me * E + e2];
-        start += off;
+        const int64_t start = a.cpre[(int64_t)me * (E + 1) + e] + off;  // its first permuted row
         if (start != pos) identity = 0;
         P->piece_pos[np] = pos;
         P->piece_src[np] = start;
@@ -256,16 +265,6 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
   }
   P->piece_pos[np] = pos;
   P->n_pieces = np;
-  for (int k = 0; k < np; ++k) P->piece_by_src[k] = k;
-  for (int k = 1; k < np; ++k) {  // insertion sort by source row (pieces are disjoint)
-    const int v = P->piece_by_src[k];
-    int i = k;
-    while (i > 0 && P->piece_src[P->piece_by_src[i - 1]] > P->piece_src[v]) {
-      P->piece_by_src[i] = P->piece_by_src[i - 1];
-      --i;
-    }
-    P->piece_by_src[i] = v;
-  }
   P->identity = identity;
   P->n_send = pos;
   // offsets inside the peers' buffers
@@ -283,7 +282,10 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
     int64_t run = 0;
     for (int j = 0; j < S; ++j) {
       a.cs_prefix[(int64_t)s * (S + 1) + j] = run;
-      const int64_t c = piece_dev(a, a.slot_experts[s0 + j], s, me, nullptr);
+      const int e = a.slot_experts[s0 + j];
+      int64_t off = 0;
+      const int64_t c = piece_dev(a, e, s, me, &off);
+      a.pstart[(int64_t)s * S + j] = c > 0 ? a.cpre[(int64_t)s * (E + 1) + e] + off : 0;
       a.cj_prefix[(int64_t)j * (R + 1) + s] = P->lcount[j];
       P->lcount[j] += c;
       run += c;
@@ -310,7 +312,7 @@ namespace {
 // One 16-byte-aligned workspace per EP layer: the plan, its two prefix tables
 // and the planner's scratch.
 struct Layout {
-  size_t plan, cs, cj, quota, lo, sbase, total, load, repl, M, hoff, hlist, bytes;
+  size_t plan, cs, cj, ps, cpre, quota, lo, sbase, total, load, repl, M, hoff, hlist, bytes;
 };
 
 size_t up16(size_t v) { return (v + 15) / 16 * 16; }
@@ -321,6 +323,8 @@ Layout layout_of(int64_t R, int64_t E, int64_t S, int64_t nslots) {
   L.plan = o; o = up16(o + sizeof(RfEpDevPlan));
   L.cs = o; o = up16(o + (size_t)R * (S + 1) * 8);
   L.cj = o; o = up16(o + (size_t)S * (R + 1) * 8);
+  L.ps = o; o = up16(o + (size_t)R * (S > 0 ? S : 1) * 8);
+  L.cpre = o; o = up16(o + (size_t)R * (E + 1) * 8);
   L.quota = o; o = up16(o + (size_t)E * R * 8);
   L.lo = o; o = up16(o + (size_t)E * R * 8);
   L.sbase = o; o = up16(o + (size_t)E * R * 8);
@@ -363,7 +367,7 @@ __device__ __forceinline__ void st_release_sys_dp(int32_t *p, int32_t v) {
 
 struct PlanPushArgs {
   const RfEpDevPlan *plan;
-  const int64_t *cs, *cj;       // prefix tables of the plan
+  const int64_t *cs, *cj, *ps;  // prefix tables and permuted row starts of the plan
   const uint8_t *src;
   const int32_t *src_slot;      // dispatch: permuted row -> pair index (t*K+k)
   int64_t div, row_bytes;
@@ -376,7 +380,8 @@ struct PlanPushArgs {
 
 // Dispatch (ret = 0): send positions i -> token rows, into the destinations'
 // receive buffers.  Return (ret = 1): receive rows q -> their local GEMM rows
-// of `src` (= y), into the sources' return buffers.  Either way the last block
+// of `src` (= y), into the sources' return buffers at the source's permuted
+// row of each.  Either way the last block
 // raises this rank's flag in every peer, also when the plan overflowed (then
 // no row is written and the device error word is already set).
 __global__ void __launch_bounds__(256) plan_push_kernel(const __grid_constant__ PlanPushArgs a) {
@@ -401,7 +406,7 @@ __global__ void __launch_bounds__(256) plan_push_kernel(const __grid_constant__ 
       const int64_t *cs = a.cs + (int64_t)d * (S + 1);
       const int j = find_le(cs, S, q2);
       srow = P->loff[j] + a.cj[(int64_t)j * (R + 1) + d] + (q2 - cs[j]);
-      drow = P->back_row0[d] + q2;
+      drow = a.ps[(int64_t)d * S + j] + (q2 - cs[j]);
     }
     copy_row(reinterpret_cast<uint4 *>(a.dst[d] + drow * a.row_bytes),
              reinterpret_cast<const uint4 *>(a.src + srow * a.row_bytes), vecs, lane);
@@ -436,26 +441,6 @@ __global__ void __launch_bounds__(256) plan_regroup_kernel(const RfEpDevPlan *P,
     const int64_t q = P->recv_off[s] + cs_all[(int64_t)s * (S + 1) + j] + (k - cj[s]);
     copy_row(reinterpret_cast<uint4 *>(xl + r * row_bytes), reinterpret_cast<const uint4 *>(recv + q * row_bytes),
              vecs, lane);
-  }
-}
-
-// row_of_slot (permuted row per (t, k)) -> that row's position in the return
-// buffer (= its send position); -1 stays -1.
-__global__ void plan_compose_kernel(const RfEpDevPlan *P, const int32_t *row_of_slot, int64_t n, int32_t *out) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int32_t j = row_of_slot[i];
-    if (j < 0 || P->overflow) {
-      out[i] = -1;
-      continue;
-    }
-    int lo = 0, hi = P->n_pieces - 1;  // last piece (in source order) starting at or before j
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (P->piece_src[P->piece_by_src[mid]] <= j) lo = mid;
-      else hi = mid - 1;
-    }
-    const int k = P->piece_by_src[lo];
-    out[i] = (int32_t)(P->piece_pos[k] + (j - P->piece_src[k]));
   }
 }
 
@@ -509,6 +494,8 @@ extern "C" int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_expe
   a.plan = reinterpret_cast<RfEpDevPlan *>(w + L.plan);
   a.cs_prefix = reinterpret_cast<int64_t *>(w + L.cs);
   a.cj_prefix = reinterpret_cast<int64_t *>(w + L.cj);
+  a.pstart = reinterpret_cast<int64_t *>(w + L.ps);
+  a.cpre = reinterpret_cast<int64_t *>(w + L.cpre);
   a.sc.quota = reinterpret_cast<int64_t *>(w + L.quota);
   a.sc.lo = reinterpret_cast<int64_t *>(w + L.lo);
   a.sc.sbase = reinterpret_cast<int64_t *>(w + L.sbase);
@@ -538,6 +525,7 @@ extern "C" int rf_moe_ep_devplan_push(const void *workspace, int32_t R, int32_t 
   a.plan = reinterpret_cast<const RfEpDevPlan *>(w + L.plan);
   a.cs = reinterpret_cast<const int64_t *>(w + L.cs);
   a.cj = reinterpret_cast<const int64_t *>(w + L.cj);
+  a.ps = reinterpret_cast<const int64_t *>(w + L.ps);
   a.src = reinterpret_cast<const uint8_t *>(src);
   a.src_slot = src_slot;
   a.div = div;
@@ -568,17 +556,4 @@ extern "C" int rf_moe_ep_devplan_regroup(const void *workspace, int32_t R, int32
       reinterpret_cast<const int64_t *>(w + L.cj), reinterpret_cast<const uint8_t *>(recv),
       reinterpret_cast<uint8_t *>(xl), row_bytes, R, S);
   return rf::check_launch("rf_moe_ep_devplan_regroup");
-}
-
-extern "C" int rf_moe_ep_devplan_compose(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
-                                         const int32_t *row_of_slot, int64_t n, int32_t *out, rf_stream_t stream) {
-  RF_CHECK_ARG(workspace && (n == 0 || (row_of_slot && out)), "rf_moe_ep_devplan_compose: bad arguments");
-  if (n == 0) return RF_OK;
-  const Layout L = layout_of(R, E, S, n_slots);
-  const uint8_t *w = reinterpret_cast<const uint8_t *>(workspace);
-  int64_t blocks = (n + 255) / 256;
-  if (blocks > (int64_t)rf::num_sms() * 8) blocks = (int64_t)rf::num_sms() * 8;
-  plan_compose_kernel<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const RfEpDevPlan *>(w + L.plan), row_of_slot, n, out);
-  return rf::check_launch("rf_moe_ep_devplan_compose");
 }

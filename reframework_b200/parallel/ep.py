@@ -216,6 +216,14 @@ class EPFusedMoE(nn.Module):
         # kernel + a bounded flag wait per direction); False: NCCL all-to-alls
         self.p2p = True
         self._px = None
+        # with p2p: plan the exchange on the device (no host synchronisation
+        # per step); False: the native host planner
+        self.device_plan = True
+        # device plan: buffers hold max_tokens_per_rank tokens from every rank
+        # (None: the largest first-step token count over the ranks)
+        self.max_tokens_per_rank: Optional[int] = None
+        self._dp = None
+        self.last_counts_dev: Optional[torch.Tensor] = None
 
     # --------------------------------------------------------------- build
     @classmethod
@@ -274,6 +282,8 @@ class EPFusedMoE(nn.Module):
         holders so that the ranks' row counts even out.
         """
         if load is None:
+            if self.last_counts is None and self.last_counts_dev is not None:
+                self.last_counts = self.last_counts_dev.cpu().numpy()
             if self.last_counts is None:
                 raise RuntimeError("rebalance() needs a load estimate or a previous forward")
             load = self.last_counts.sum(axis=0)
@@ -478,6 +488,9 @@ class EPFusedMoE(nn.Module):
         else:
             counts = torch.zeros(E, dtype=torch.int32, device=dev)
         self._mark("route+permute")
+        if use_p2p and self.device_plan:
+            return self._forward_devplan(x2, res2, p if T > 0 else None, w if T > 0 else None,
+                                         sscale if T > 0 else None, counts)
         # (2) counts exchange -> the same plan on every rank
         gathered = [torch.empty_like(counts) for _ in range(self.ep_size)]
         tdist.all_gather(gathered, counts, group=pg)
@@ -554,14 +567,115 @@ class EPFusedMoE(nn.Module):
     def _expert_gemms(self, xl: torch.Tensor, plan, off: torch.Tensor, lc: torch.Tensor) -> torch.Tensor:
         """Grouped gated + down GEMMs over this rank's slot-major rows."""
         I, H = self.intermediate_size, xl.shape[1]
+        rows = xl.shape[0]
         w1b, w2b = self._gemm_banks()
-        h = torch.empty(plan.rows_capacity, I, dtype=xl.dtype, device=xl.device)
+        h = torch.empty(rows, I, dtype=xl.dtype, device=xl.device)
         K.grouped_gemm_gated(xl, w1b, off, lc, h, activation=self.activation)
         self._mark("gated GEMM")
-        y = torch.empty(plan.rows_capacity, H, dtype=xl.dtype, device=xl.device)
+        y = torch.empty(rows, H, dtype=xl.dtype, device=xl.device)
         K.grouped_gemm_down(h, w2b, off, lc, y)
         self._mark("down GEMM")
         return y
+
+    def _devplan_state(self, T: int, row_bytes: int):
+        """Device slot arrays, plan workspace and peer buffers for the device
+        plan (rebuilt when the placement changes).  The first call agrees on the
+        per-rank token bound (collective)."""
+        import ctypes
+        dev = self.gate.device
+        R, E, Kk = self.ep_size, self.num_experts, self.top_k
+        if self.max_tokens_per_rank is None:
+            t = torch.tensor([T], dtype=torch.int64, device=dev)
+            tdist.all_reduce(t, op=tdist.ReduceOp.MAX, group=self._pg())
+            self.max_tokens_per_rank = max(int(t.item()), 1)
+        if T > self.max_tokens_per_rank:
+            raise RfMoeError(f"EPFusedMoE: {T} tokens on this rank exceed max_tokens_per_rank="
+                             f"{self.max_tokens_per_rank}; set it (on every rank) before the first forward")
+        st = self._dp
+        if st is None or st["placement"] is not self.placement:
+            flat = np.ascontiguousarray([e for s_ in self.placement.slots for e in s_], dtype=np.int32)
+            offs = np.ascontiguousarray(np.cumsum([0] + [len(s_) for s_ in self.placement.slots]), dtype=np.int32)
+            S, nslots = len(self.placement.slots[self.ep_rank]), int(flat.size)
+            nb = int(lib().rf_moe_ep_devplan_workspace_size(R, E, S, nslots))
+            lay = np.zeros(12, dtype=np.int64)
+            check(lib().rf_moe_ep_devplan_layout(R, E, S, nslots, lay.ctypes.data), "rf_moe_ep_devplan_layout")
+            ws = torch.zeros(nb, dtype=torch.uint8, device=dev)
+            st = self._dp = {
+                "placement": self.placement, "S": S, "nslots": nslots, "ws": ws,
+                "flat": torch.from_numpy(flat).to(dev), "offs": torch.from_numpy(offs).to(dev),
+                "seg_off": ws[lay[0]:lay[0] + 4 * (S + 1)].view(torch.int32),
+                "seg_cnt": ws[lay[1]:lay[1] + 4 * max(S, 1)].view(torch.int32)[:S],
+            }
+        recv_cap = R * self.max_tokens_per_rank * Kk
+        st["recv_cap"] = recv_cap
+        st["rows_cap"] = recv_cap + st["S"] * (K.ALIGN - 1)
+        px = self._exchange()
+        px.ensure(recv_cap, self.max_tokens_per_rank * Kk, row_bytes)
+        return st, px
+
+    def _forward_devplan(self, x2, res2, p, w, sscale, counts) -> torch.Tensor:
+        """The EP forward with the exchange planned on the device: counts
+        all-gather (device), planner kernel, peer pushes, bounded waits — no
+        host synchronisation in the step."""
+        import ctypes
+        from .p2p import DISPATCH, RETURN
+        dev = x2.device
+        T, H = x2.shape
+        R, E, Kk = self.ep_size, self.num_experts, self.top_k
+        row_bytes = H * x2.element_size()
+        stt, px = self._devplan_state(T, row_bytes)
+        S, nslots, ws = stt["S"], stt["nslots"], stt["ws"]
+        cnt = torch.empty(R, E, dtype=torch.int32, device=dev)
+        tdist.all_gather_into_tensor(cnt, counts.contiguous(), group=self._pg())
+        self.last_counts_dev, self.last_counts, self.last_plan = cnt, None, None
+        self._mark("counts all_gather")
+        st = stream_of(dev)
+        check(lib().rf_moe_ep_devplan(cnt.data_ptr(), stt["flat"].data_ptr(), stt["offs"].data_ptr(), R, E,
+                                      self.ep_rank, S, nslots, K.ALIGN, self.split_rounds, stt["recv_cap"],
+                                      stt["rows_cap"], ws.data_ptr(), ws.numel(), st), "rf_moe_ep_devplan")
+        self._mark("device plan")
+        epoch = px.next_epoch()
+        ctrl = px.peer[2]
+        flags0 = (ctypes.c_void_p * R)(*[ctrl[d] + 4 * (DISPATCH * R + self.ep_rank) for d in range(R)])
+        flags1 = (ctypes.c_void_p * R)(*[ctrl[d] + 4 * (RETURN * R + self.ep_rank) for d in range(R)])
+        done = px.own[2].ptr + 2 * R * 4
+        check(lib().rf_moe_ep_devplan_push(ws.data_ptr(), R, E, S, nslots, 0, x2.data_ptr() if T else None,
+                                           p.src_slot.data_ptr() if p is not None else None, Kk, row_bytes,
+                                           (ctypes.c_void_p * R)(*px.peer[0]), flags0, epoch, done, st),
+              "rf_moe_ep_devplan_push")
+        self._mark("dispatch push")
+        px.wait(DISPATCH)
+        self._mark("dispatch wait")
+        y = None
+        if S > 0:
+            xl = torch.empty(stt["rows_cap"], H, dtype=x2.dtype, device=dev)
+            check(lib().rf_moe_ep_devplan_regroup(ws.data_ptr(), R, E, S, nslots, px.recv_ptr(), xl.data_ptr(),
+                                                  row_bytes, st), "rf_moe_ep_devplan_regroup")
+            self._mark("regroup gather")
+            y = self._expert_gemms(xl, None, stt["seg_off"], stt["seg_cnt"])
+        check(lib().rf_moe_ep_devplan_push(ws.data_ptr(), R, E, S, nslots, 1, y.data_ptr() if y is not None else None,
+                                           None, 1, row_bytes, (ctypes.c_void_p * R)(*px.peer[1]), flags1, epoch,
+                                           done, st), "rf_moe_ep_devplan_push")
+        self._mark("return push")
+        px.wait(RETURN)
+        self._mark("return wait")
+        out = torch.empty(T, H, dtype=x2.dtype, device=dev)
+        if T == 0:
+            return out
+        # the return push left every result at its permuted row: the combine
+        # reads them through the permute's own row_of_slot (expert order)
+        shared_y = None
+        if self._shared is not None:
+            shared_y = K.dense_gated_mlp(x2, self._shared[0], self._shared[1], self.activation)
+        wf = w.contiguous()
+        mode = _lib_mod.COMBINE_FP32 if self.precise_combine else _lib_mod.COMBINE_REFERENCE
+        check(lib().rf_moe_combine(px.back_ptr(), p.row_of_slot.data_ptr(), wf.data_ptr(), T, Kk, H,
+                                   dtype_code(x2.dtype), None if shared_y is None else shared_y.data_ptr(),
+                                   None if sscale is None else sscale.data_ptr(),
+                                   None if res2 is None else res2.data_ptr(), 0, mode, out.data_ptr(), st),
+              "rf_moe_combine")
+        self._mark("shared+combine")
+        return out
 
     def _exchange_p2p(self, x2, res2, p, plan, views, w, sscale, cnt) -> torch.Tensor:
         """Steps 3-5 over peer memory: push token rows into the experts' ranks,

@@ -247,9 +247,12 @@ def run_gpu(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    from reframework_b200.parallel.dist import bind_to_device_cpus
+    # host threads and (first-touch) pinned buffers on the GPU's own NUMA node
+    host_cpus = bind_to_device_cpus(dev)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     cfg = CONFIGS[args.config]
     T = cfg.tokens
     d = generate(cfg, device=str(dev), with_x=False)
@@ -351,7 +354,8 @@ def run_gpu(args):
                 "h2d_bytes_per_step": x.numel() * x.element_size(),
                 "d2h_bytes_per_step": x.numel() * x.element_size(),
                 "ms_per_step": ms_e2e, "api": "FusedMoE.forward" if world == 1 else "EPFusedMoE.forward",
-                "pipeline": "H2D of step i+1 and D2H of step i on two copy streams overlap step i's forward"},
+                "pipeline": "H2D of step i+1 and D2H of step i on two copy streams overlap step i's forward",
+                "host_cpus": (f"{len(host_cpus)} CPUs local to the GPU" if host_cpus else "unbound")},
         "gpu_launches": args.steps * (LAUNCHES_PER_FORWARD if world == 1 else ep_launches(layer)),
         "clocks": clk,
     }

@@ -8,8 +8,11 @@ ep_size``); ``current()`` raises RuntimeError when no group is live; ``run``
 raises RuntimeError when a child exits non-zero.  The backend is NCCL on GPUs
 (one process per GPU over NVLink/NVSwitch) and gloo for CPU tests.
 
-Added for expert parallelism: ``all_to_all_v`` (variable split sizes) and a
-``timeout`` on ``init`` so ranks waiting on a dead peer end with an error.
+Added for expert parallelism: ``all_to_all_v`` (variable split sizes), a
+``timeout`` on ``init`` so ranks waiting on a dead peer end with an error, and
+``bind_to_device_cpus`` (host threads and first-touch pinned buffers on the
+CPUs next to this rank's GPU, so eight ranks' host copies do not cross the
+socket link).
 """
 
 from __future__ import annotations
@@ -24,7 +27,7 @@ import torch.distributed as dist
 
 __all__ = ["ParallelContext", "init", "run", "is_initialized", "current", "get_rank", "get_world_size",
            "all_reduce_sum", "all_gather", "all_to_all", "all_to_all_v", "send", "recv", "barrier",
-           "destroy"]
+           "destroy", "device_local_cpus", "bind_to_device_cpus"]
 
 
 @dataclass(frozen=True)
@@ -174,3 +177,47 @@ def destroy() -> None:
     if dist.is_initialized():
         dist.destroy_process_group()
     _current = None
+
+
+# ------------------------------------------------------------- host placement
+def _parse_cpulist(text: str) -> List[int]:
+    """``"0-3,8,10-11"`` -> [0, 1, 2, 3, 8, 10, 11]."""
+    cpus: List[int] = []
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        if "-" in part:
+            a, b = part.split("-")
+            cpus.extend(range(int(a), int(b) + 1))
+        else:
+            cpus.append(int(part))
+    return cpus
+
+
+def device_local_cpus(domain: int, bus: int, device: int, sysfs: str = "/sys") -> Optional[List[int]]:
+    """CPUs on the same NUMA node as the PCI device ``domain:bus:device.0``
+    (its ``local_cpulist`` in sysfs), or None when sysfs does not say."""
+    path = os.path.join(sysfs, "bus", "pci", "devices", f"{domain:04x}:{bus:02x}:{device:02x}.0", "local_cpulist")
+    try:
+        with open(path) as f:
+            cpus = _parse_cpulist(f.read())
+    except (OSError, ValueError):
+        return None
+    return cpus or None
+
+
+def bind_to_device_cpus(device: torch.device, sysfs: str = "/sys") -> Optional[List[int]]:
+    """Restrict this process to the CPUs next to ``device`` (intersected with
+    the CPUs it may use) and return them; None (nothing changed) when the
+    topology is unknown or the intersection is empty.  Call it before pinned
+    host buffers are allocated: their pages are placed on first touch."""
+    props = torch.cuda.get_device_properties(device)
+    cpus = device_local_cpus(props.pci_domain_id, props.pci_bus_id, props.pci_device_id, sysfs)
+    if not cpus or not hasattr(os, "sched_setaffinity"):
+        return None
+    allowed = os.sched_getaffinity(0)
+    mine = sorted(set(cpus) & allowed)
+    if not mine or set(mine) == allowed:
+        return mine or None
+    os.sched_setaffinity(0, mine)
+    return mine

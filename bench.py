@@ -226,9 +226,10 @@ def e2e_run(fwd, xh, steps, dev):
 # router x2 (tensor-core logits, top-k), permute x3 (histogram, scatter, gather), gated GEMM, down GEMM, combine
 LAUNCHES_PER_FORWARD = 8
 # EP, exchange planned on the device and carried over peer memory: router x2, permute x2 (histogram,
-# scatter), planner, dispatch push + wait, regroup gather, gated GEMM, down GEMM, return push + wait,
-# combine; NCCL's own kernels (the counts all-gather) are not counted
-EP_LAUNCHES_PER_FORWARD = 13
+# scatter), planner, dispatch push + wait, regroup gather, gated GEMM, down GEMM storing its rows into
+# the token ranks' return buffers + return wait, combine; NCCL's own kernels (the counts all-gather)
+# are not counted
+EP_LAUNCHES_PER_FORWARD = 12
 
 
 def ep_launches(layer) -> int:
@@ -236,8 +237,8 @@ def ep_launches(layer) -> int:
     one more gather when replicas reorder the sent rows)."""
     if layer.p2p and layer.device_plan:
         return EP_LAUNCHES_PER_FORWARD
-    plan = layer.last_plan
-    return EP_LAUNCHES_PER_FORWARD - 1 + (1 if plan is not None and plan.send_index is not None else 0)
+    plan = layer.last_plan  # + return push, - planner
+    return EP_LAUNCHES_PER_FORWARD + (1 if plan is not None and plan.send_index is not None else 0)
 
 
 def run_gpu(args):

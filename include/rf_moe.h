@@ -73,6 +73,7 @@ typedef enum {
 #define RF_DEV_OK 0
 #define RF_DEV_BAD_EXPERT_ID 1   /* a routed id was outside [0, E) */
 #define RF_DEV_WAIT_TIMEOUT 2    /* a pipeline wait ran out of time and gave up */
+#define RF_DEV_PLAN_OVERFLOW 3   /* an expert-parallel plan needed more rows than its buffers hold */
 
 /* Message of the calling thread's last failed call ("" if none). */
 const char *rf_moe_last_error(void);
@@ -326,9 +327,10 @@ int rf_moe_ep_wait(const int32_t *flags, int32_t R, int32_t epoch, rf_stream_t s
  * slot_offsets, device copies of the host arrays; S = this rank's slot count,
  * n_slots = all slots) into `workspace` (rf_moe_ep_devplan_workspace_size
  * bytes): small tables — send pieces, per-peer offsets, the receive table and
- * the slot-major GEMM segments.  recv_capacity / rows_capacity bound what the
- * row kernels may write; a plan exceeding them is flagged (device error word)
- * and moves no rows.
+ * the slot-major GEMM segments.  recv_capacity / back_capacity are the rows of
+ * every rank's receive / return buffer and rows_capacity those of this rank's
+ * GEMM rows; a plan exceeding them is flagged (device error word) and moves
+ * no rows (the buffer check is global, so every rank's plan fails with it).
  *   rf_moe_ep_devplan_push     dir 0: this rank's routed token rows (src = x,
  *                              src_slot from rf_moe_permute, div = K; both may
  *                              be NULL when this rank has no tokens) into the
@@ -340,6 +342,13 @@ int rf_moe_ep_wait(const int32_t *flags, int32_t R, int32_t epoch, rf_stream_t s
  *                              that permute's row_of_slot; then flags as
  *                              rf_moe_ep_push_rows
  *   rf_moe_ep_devplan_regroup  receive buffer -> slot-major GEMM rows
+ *   rf_moe_ep_devplan_down_return  dir 1 fused into the down GEMM: the
+ *                              tensor-core epilogue stores every row of
+ *                              h[rows_capacity, I] . w2[j][H, I]^T straight
+ *                              into its token rank's return buffer (same rows
+ *                              as the GEMM + dir-1 push), then flags as
+ *                              rf_moe_ep_push_rows; RF_ERR_UNSUPPORTED when the
+ *                              tensor-core path does not take the dtype/shape
  * rf_moe_ep_devplan_layout: byte offsets inside the workspace of
  *   [0] int32 segment offsets [S+1], [1] int32 segment counts [S] (grouped
  *   GEMM arguments), [2] int32 overflow, [3] int64 recv_total, [4] int64 n_send,
@@ -351,14 +360,18 @@ size_t rf_moe_ep_devplan_workspace_size(int32_t R, int32_t E, int32_t S, int32_t
 int rf_moe_ep_devplan_layout(int32_t R, int32_t E, int32_t S, int32_t n_slots, int64_t *out);
 int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_experts, const int32_t *slot_offsets,
                       int32_t R, int32_t E, int32_t me, int32_t S, int32_t n_slots, int32_t align,
-                      int32_t rounds, int64_t recv_capacity, int64_t rows_capacity, void *workspace,
-                      size_t ws_bytes, rf_stream_t stream);
+                      int32_t rounds, int64_t recv_capacity, int64_t back_capacity, int64_t rows_capacity,
+                      void *workspace, size_t ws_bytes, rf_stream_t stream);
 int rf_moe_ep_devplan_push(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
                            int32_t dir, const void *src, const int32_t *src_slot, int64_t div,
                            int64_t row_bytes, void *const *dst, int32_t *const *flag, int32_t epoch,
                            uint32_t *done, rf_stream_t stream);
 int rf_moe_ep_devplan_regroup(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
                               const void *recv, void *xl, int64_t row_bytes, rf_stream_t stream);
+int rf_moe_ep_devplan_down_return(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
+                                  const void *h, const void *w2, int64_t rows_capacity, int64_t H, int64_t I,
+                                  int32_t dtype, void *const *dst, int32_t *const *flag, int32_t epoch,
+                                  uint32_t *done, rf_stream_t stream);
 
 /* Summation modes of rf_moe_combine. */
 #define RF_COMBINE_REFERENCE 0  /* the reference's rounding points and order */

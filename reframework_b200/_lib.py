@@ -21,7 +21,8 @@ LIB_PATH = os.path.join(_HERE, "_rf_moe.so")
 RF_F32, RF_F16, RF_BF16 = 0, 1, 2
 ACTIVATIONS = {"silu": 0, "gelu": 1, "gelu_tanh": 2}
 COMBINE_REFERENCE, COMBINE_FP32 = 0, 1
-DEV_ERRORS = {0: "ok", 1: "routed expert id out of range", 2: "pipeline wait timed out"}
+DEV_ERRORS = {0: "ok", 1: "routed expert id out of range", 2: "pipeline wait timed out",
+              3: "expert-parallel plan exceeds its buffers"}
 
 _c_void_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -72,12 +73,16 @@ _SIGNATURES = {
     "rf_moe_ep_wait": (_int, [_c_void_p, ctypes.c_int32, ctypes.c_int32, _c_void_p]),
     "rf_moe_ep_devplan_workspace_size": (ctypes.c_size_t, [ctypes.c_int32] * 4),
     "rf_moe_ep_devplan_layout": (_int, [ctypes.c_int32] * 4 + [_c_void_p]),
-    "rf_moe_ep_devplan": (_int, [_c_void_p, _c_void_p, _c_void_p] + [ctypes.c_int32] * 7 + [_i64, _i64, _c_void_p,
+    "rf_moe_ep_devplan": (_int, [_c_void_p, _c_void_p, _c_void_p] + [ctypes.c_int32] * 7 + [_i64, _i64, _i64, _c_void_p,
                                                                                            ctypes.c_size_t, _c_void_p]),
     "rf_moe_ep_devplan_push": (_int, [_c_void_p] + [ctypes.c_int32] * 5 + [_c_void_p, _c_void_p, _i64, _i64,
                                                                             _c_void_p, _c_void_p, ctypes.c_int32,
                                                                             _c_void_p, _c_void_p]),
     "rf_moe_ep_devplan_regroup": (_int, [_c_void_p] + [ctypes.c_int32] * 4 + [_c_void_p, _c_void_p, _i64, _c_void_p]),
+    "rf_moe_ep_devplan_down_return": (_int, [_c_void_p] + [ctypes.c_int32] * 4 + [_c_void_p, _c_void_p, _i64, _i64,
+                                                                               _i64, ctypes.c_int32, _c_void_p,
+                                                                               _c_void_p, ctypes.c_int32, _c_void_p,
+                                                                               _c_void_p]),
     "rf_moe_ep_plan": (_int, [_c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_void_p, _c_void_p,
                               ctypes.c_int32, ctypes.c_int32, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
 }

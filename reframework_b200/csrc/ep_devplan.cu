@@ -24,6 +24,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "gemm.cuh"
 
 RF_DEVICE_ERROR_WORD();
 
@@ -100,8 +101,9 @@ struct PlannerArgs {
   const int32_t *counts;        // [R][E]
   const int32_t *slot_experts;  // [total slots]
   const int32_t *slot_offsets;  // [R+1]
-  int R, E, me, align, rounds;
-  int64_t recv_capacity, rows_capacity;  // buffers the row kernels may fill
+  int R, E, me, S, align, rounds;  // S: this rank's slot count as the host laid out the workspace
+  int64_t recv_capacity, back_capacity;  // every rank's receive / return buffer rows
+  int64_t rows_capacity;                 // this rank's slot-major GEMM rows
   RfEpDevPlan *plan;
   int64_t *cs_prefix;           // [R][S+1]
   int64_t *cj_prefix;           // [S][R+1]
@@ -121,12 +123,27 @@ __device__ int64_t piece_dev(const PlannerArgs &a, int e, int src, int h, int64_
   return hi - lo > 0 ? hi - lo : 0;
 }
 
+// A failed plan moves no row and gives the GEMMs empty segments.
+__device__ void clear_plan(RfEpDevPlan *P, int S) {
+  for (int j = 0; j <= S; ++j) {
+    P->loff[j] = 0;
+    P->loff32[j] = 0;
+  }
+  for (int j = 0; j < S; ++j) {
+    P->lcount[j] = 0;
+    P->lcount32[j] = 0;
+  }
+  P->n_send = P->recv_total = P->rows_used = 0;
+  P->n_pieces = 0;
+  P->overflow = 1;
+}
+
 __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
   const int R = a.R, E = a.E, me = a.me;
   RfEpDevPlan *P = a.plan;
   __shared__ int s_bad;
   if (threadIdx.x == 0) {
-    s_bad = 0;
+    s_bad = a.slot_offsets[me + 1] - a.slot_offsets[me] != a.S ? 1 : 0;
     int64_t *quota = a.sc.quota, *lo = a.sc.lo, *sbase = a.sc.sbase, *total = a.sc.total, *load = a.sc.load;
     // holders of every expert, in rank order (CSR)
     for (int e = 0; e <= E; ++e) a.hoff[e] = 0;
@@ -211,7 +228,7 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
   __syncthreads();
   if (s_bad) {
     if (threadIdx.x == 0) {
-      P->overflow = 1;
+      clear_plan(P, a.S);
       rf_report(RF_DEV_BAD_EXPERT_ID);
     }
     return;
@@ -230,6 +247,22 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
     for (int e = 0; e < E; ++e) c[e + 1] = c[e] + a.counts[(int64_t)s * E + e];
   }
   __syncthreads();
+  // every rank's buffers (the same check on every rank: all plans fail together)
+  if (threadIdx.x == 0) {
+    for (int d = 0; d < R; ++d) {
+      int64_t in = 0;
+      for (int s = 0; s < R; ++s) in += a.M[(int64_t)s * R + d];
+      if (in > a.recv_capacity || a.cpre[(int64_t)d * (E + 1) + E] > a.back_capacity) s_bad = 1;
+    }
+  }
+  __syncthreads();
+  if (s_bad) {
+    if (threadIdx.x == 0) {
+      clear_plan(P, a.S);
+      rf_report(RF_DEV_PLAN_OVERFLOW);
+    }
+    return;
+  }
   if (threadIdx.x != 0) return;
   // ---- this rank's tables
   int bad = 0;
@@ -302,7 +335,10 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
   P->rows_used = P->loff[S];
   if (P->recv_total > a.recv_capacity || P->rows_used > a.rows_capacity) bad = 1;
   P->overflow = bad;
-  if (bad) rf_report(RF_DEV_BAD_EXPERT_ID);
+  if (bad) {
+    clear_plan(P, S);
+    rf_report(RF_DEV_PLAN_OVERFLOW);
+  }
 }
 
 }  // namespace
@@ -471,8 +507,8 @@ extern "C" int rf_moe_ep_devplan_layout(int32_t R, int32_t E, int32_t S, int32_t
 
 extern "C" int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_experts, const int32_t *slot_offsets,
                                  int32_t R, int32_t E, int32_t me, int32_t S, int32_t n_slots, int32_t align,
-                                 int32_t rounds, int64_t recv_capacity, int64_t rows_capacity, void *workspace,
-                                 size_t ws_bytes, rf_stream_t stream) {
+                                 int32_t rounds, int64_t recv_capacity, int64_t back_capacity, int64_t rows_capacity,
+                                 void *workspace, size_t ws_bytes, rf_stream_t stream) {
   RF_CHECK_ARG(counts && slot_experts && slot_offsets && workspace, "rf_moe_ep_devplan: null pointer");
   RF_CHECK_ARG(R >= 1 && R <= MAXR && E >= 1 && me >= 0 && me < R && S >= 0 && S <= MAXS && align >= 1 &&
                    rounds >= 0,
@@ -487,9 +523,11 @@ extern "C" int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_expe
   a.R = R;
   a.E = E;
   a.me = me;
+  a.S = S;
   a.align = align;
   a.rounds = rounds;
   a.recv_capacity = recv_capacity;
+  a.back_capacity = back_capacity;
   a.rows_capacity = rows_capacity;
   a.plan = reinterpret_cast<RfEpDevPlan *>(w + L.plan);
   a.cs_prefix = reinterpret_cast<int64_t *>(w + L.cs);
@@ -556,4 +594,57 @@ extern "C" int rf_moe_ep_devplan_regroup(const void *workspace, int32_t R, int32
       reinterpret_cast<const int64_t *>(w + L.cj), reinterpret_cast<const uint8_t *>(recv),
       reinterpret_cast<uint8_t *>(xl), row_bytes, R, S);
   return rf::check_launch("rf_moe_ep_devplan_regroup");
+}
+
+// dir 1 fused into the down GEMM: y = h . w2[j]^T per local slot, each row
+// stored by the GEMM epilogue into its token rank's return buffer.
+extern "C" int rf_moe_ep_devplan_down_return(const void *workspace, int32_t R, int32_t E, int32_t S,
+                                             int32_t n_slots, const void *h, const void *w2, int64_t rows_capacity,
+                                             int64_t H, int64_t I, int32_t dtype, void *const *dst,
+                                             int32_t *const *flag, int32_t epoch, uint32_t *done,
+                                             rf_stream_t stream) {
+  RF_CHECK_ARG(workspace && h && w2 && dst && flag && done, "rf_moe_ep_devplan_down_return: null pointer");
+  RF_CHECK_ARG(R >= 1 && R <= MAXR && R <= rf::REMOTE_MAX_RANKS && S >= 1 && S <= MAXS && E >= 1 && H >= 1 &&
+                   I >= 1 && rows_capacity >= 1 && rows_capacity < ((int64_t)1 << 31) && H < (1 << 30) &&
+                   I < (1 << 30),
+               "rf_moe_ep_devplan_down_return: bad sizes");
+  RF_CHECK_ARG(rf::valid_dtype(dtype), "rf_moe_ep_devplan_down_return: unknown dtype");
+  const Layout L = layout_of(R, E, S, n_slots);
+  const uint8_t *w = reinterpret_cast<const uint8_t *>(workspace);
+  const RfEpDevPlan *P = reinterpret_cast<const RfEpDevPlan *>(w + L.plan);
+  rf::RemoteOut ro;
+  ro.cj = reinterpret_cast<const int64_t *>(w + L.cj);
+  ro.ps = reinterpret_cast<const int64_t *>(w + L.ps);
+  ro.R = R;
+  ro.S = S;
+  ro.epoch = epoch;
+  ro.done = done;
+  for (int d = 0; d < R; ++d) {
+    RF_CHECK_ARG(dst[d] && flag[d] && (uintptr_t)dst[d] % 16 == 0,
+                 "rf_moe_ep_devplan_down_return: missing or unaligned peer buffer");
+    ro.dst[d] = dst[d];
+    ro.flag[d] = flag[d];
+  }
+  rf::GroupedGemmArgs g;
+  g.a = h;
+  g.w = w2;
+  g.out = dst[0];  // rows go through ro; kept for the operand checks
+  g.offsets = P->loff32;
+  g.counts = P->lcount32;
+  g.slot = nullptr;
+  g.groups = nullptr;
+  g.n_groups = S;
+  g.E = S;
+  g.num_slots = S;
+  g.rows_capacity = rows_capacity;
+  g.Kdim = (int)I;
+  g.N = (int)H;
+  g.dtype = dtype;
+  g.act = 0;
+  g.remote = &ro;
+  const int rc = rf::tc_down_remote(g, (cudaStream_t)stream);
+  if (rc < 0)
+    return rf::fail(RF_ERR_UNSUPPORTED,
+                    "rf_moe_ep_devplan_down_return: needs the tensor-core path (bf16/fp16, sizes multiple of 8)");
+  return rc;
 }

@@ -6,6 +6,24 @@
 
 namespace rf {
 
+constexpr int REMOTE_MAX_RANKS = 64;
+
+// Down GEMM with the expert-parallel return exchange in its epilogue: output
+// row k of local slot j came from source rank s = the last s with
+// cj[j][s] <= k, and is stored at row ps[s][j] + (k - cj[j][s]) of rank s's
+// return buffer dst[s] (a peer pointer) instead of locally.  When every CTA
+// is done, the last one fences at system scope and raises flag[d] = epoch in
+// every rank d (done: a zeroed block counter of this rank).
+struct RemoteOut {
+  const int64_t *cj;  // [S][R+1]
+  const int64_t *ps;  // [R][S]
+  int R, S;
+  int32_t epoch;
+  uint32_t *done;
+  void *dst[REMOTE_MAX_RANKS];
+  int32_t *flag[REMOTE_MAX_RANKS];
+};
+
 struct GroupedGemmArgs {
   const void *a;                 // [rows_capacity, Kdim]
   const void *w;                 // gated: [S, 2*N, Kdim]; down: [S, N, Kdim]
@@ -27,6 +45,9 @@ struct GroupedGemmArgs {
   const int32_t *gather_src = nullptr;
   int gather_div = 1;
   int64_t a_rows = 0;
+  // down GEMM only: store rows into the peers' return buffers (slot / groups
+  // must be NULL, so group j is local slot j)
+  const RemoteOut *remote = nullptr;
 };
 
 int launch_simt_grouped_gemm(const GroupedGemmArgs &g, bool gated, cudaStream_t st);
@@ -35,5 +56,10 @@ int launch_simt_grouped_gemm(const GroupedGemmArgs &g, bool gated, cudaStream_t 
 // (gemm_tc.cu); -1 when the shape or dtype is not handled there.
 int tc_dense_f32(const void *a, const void *w, float *out, int64_t M, int64_t N, int64_t Kdim,
                  int64_t ld_out, int dtype, cudaStream_t st);
+
+// The down GEMM of `g` (g.remote set) on the tensor cores, launched even when
+// no row is routed (the flags must rise); -1 when the shape or dtype is not
+// handled there, else a status.
+int tc_down_remote(const GroupedGemmArgs &g, cudaStream_t st);
 
 }  // namespace rf

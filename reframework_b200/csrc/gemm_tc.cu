@@ -27,6 +27,10 @@
 // Every mbarrier wait is bounded (2 s): on expiry the CTA sets the device
 // error word, stops issuing, waits for its own in-flight MMAs and copies and
 // releases TMEM before returning.
+// REMOTE (down GEMM of the expert-parallel layer): the epilogue stores each
+// output row straight into the return buffer of the rank that sent the token
+// (NVLink peer stores, overlapping the next tile's MMAs), and the last CTA
+// raises that exchange's completion flags; see rf::RemoteOut.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -239,13 +243,23 @@ __host__ __device__ constexpr uint32_t instr_desc() {
          ((uint32_t)(BM >> 4) << 24);
 }
 
+struct NoRemote {};
+
+__device__ __forceinline__ void st_release_sys_u32(int32_t *p, int32_t v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // OUTF32 (down kernel only): the accumulator is stored as fp32, unrounded.
 // GATHER: A rows are fetched from the token rows with TMA gather4 (no
 // expert-ordered activation copy in HBM).
-template <typename T, bool GATED, int ACT, int BN_, bool OUTF32 = false, bool GATHER = false>
+// REMOTE (down kernel only): rows go to the peers' return buffers (ro).
+template <typename T, bool GATED, int ACT, int BN_, bool OUTF32 = false, bool GATHER = false,
+          bool REMOTE = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA32,
-                    const __grid_constant__ CUtensorMap tmB, const TcArgs p) {
+                    const __grid_constant__ CUtensorMap tmB, const TcArgs p,
+                    const __grid_constant__ std::conditional_t<REMOTE, rf::RemoteOut, NoRemote> ro) {
+  static_assert(!REMOTE || (!GATED && !OUTF32 && !GATHER), "remote stores: plain down GEMM only");
   using C = Cfg<BN_>;
   constexpr int BN = C::BN, STAGES = C::STAGES, B_BYTES = C::B_BYTES, STAGE_BYTES = C::STAGE_BYTES;
   constexpr int NUM_BARS = C::NUM_BARS;
@@ -482,6 +496,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const uint32_t tb = tmem_base + ((uint32_t)(wq * 32) << 16) + (uint32_t)(acc * BN);
       const bool row_ok = r < rows;
       T *orow = out + (int64_t)(row0 + r) * p.out_ld;
+      if constexpr (REMOTE) {
+        if (row_ok) {  // source rank of local row k of slot s, and its row there
+          const int64_t k = (int64_t)(row0 + r) - g_row0[s];
+          const int64_t *cj = ro.cj + (int64_t)s * (ro.R + 1);
+          int lo = 0, hi = ro.R - 1;
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (cj[mid] <= k) lo = mid;
+            else hi = mid - 1;
+          }
+          orow = reinterpret_cast<T *>(ro.dst[lo]) + (ro.ps[(int64_t)lo * ro.S + s] + (k - cj[lo])) * p.out_ld;
+        }
+      }
       if (GATED) {
         const int n0 = nb * (BN / 2);
 #pragma unroll 1
@@ -558,6 +585,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
+  if constexpr (REMOTE) {
+    if (threadIdx.x == 0) {
+      __threadfence_system();  // this CTA's peer stores, visible to every GPU, before the count
+      const uint32_t prev = atomicAdd(ro.done, 1u);
+      if (prev == gridDim.x - 1) {  // last CTA: every row of the launch has landed
+        __threadfence_system();
+        for (int d = 0; d < ro.R; ++d) st_release_sys_u32(ro.flag[d], ro.epoch);
+        *ro.done = 0u;
+      }
+    }
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -599,11 +637,11 @@ bool encode(CUtensorMap *m, int dtype, int rank, const void *base, const cuuint6
   return r == CUDA_SUCCESS;
 }
 
-template <typename T, bool GATED, int ACT, int BN, bool GATHER = false>
+template <typename T, bool GATED, int ACT, int BN, bool GATHER = false, bool REMOTE = false>
 int launch_tc_t(const rf::GroupedGemmArgs &g, const CUtensorMap &ma, const CUtensorMap &ma32,
                 const CUtensorMap &mb, cudaStream_t st) {
   using C = Cfg<BN>;
-  auto kern = tc_grouped_gemm<T, GATED, ACT, BN, false, GATHER>;
+  auto kern = tc_grouped_gemm<T, GATED, ACT, BN, false, GATHER, REMOTE>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -628,14 +666,22 @@ int launch_tc_t(const rf::GroupedGemmArgs &g, const CUtensorMap &ma, const CUten
   p.act = g.act;
   p.gather_src = g.gather_src;
   p.gather_div = g.gather_div;
-  kern<<<rf::num_sms(), NTHREADS, C::SMEM_BYTES, st>>>(ma, ma32, mb, p);
-  return rf::check_launch(GATED ? "tensor-core gated GEMM" : "tensor-core down GEMM");
+  if constexpr (REMOTE) {
+    kern<<<rf::num_sms(), NTHREADS, C::SMEM_BYTES, st>>>(ma, ma32, mb, p, *g.remote);
+    return rf::check_launch("tensor-core down GEMM with peer stores");
+  } else {
+    kern<<<rf::num_sms(), NTHREADS, C::SMEM_BYTES, st>>>(ma, ma32, mb, p, NoRemote{});
+    return rf::check_launch(GATED ? "tensor-core gated GEMM" : "tensor-core down GEMM");
+  }
 }
 
 template <typename T, int BN>
 int launch_tc_bn(const rf::GroupedGemmArgs &g, bool gated, const CUtensorMap &ma, const CUtensorMap &ma32,
                  const CUtensorMap &mb, cudaStream_t st) {
-  if (!gated) return launch_tc_t<T, false, 0, BN>(g, ma, ma32, mb, st);
+  if (!gated) {
+    if (g.remote) return launch_tc_t<T, false, 0, BN, false, true>(g, ma, ma32, mb, st);
+    return launch_tc_t<T, false, 0, BN>(g, ma, ma32, mb, st);
+  }
   if (g.gather_src) {
     if (g.act == RF_ACT_SILU) return launch_tc_t<T, true, RF_ACT_SILU, BN, true>(g, ma, ma32, mb, st);
     if (g.act == RF_ACT_GELU) return launch_tc_t<T, true, RF_ACT_GELU, BN, true>(g, ma, ma32, mb, st);
@@ -736,7 +782,7 @@ int launch_dense(const CUtensorMap &ma, const CUtensorMap &ma32, const CUtensorM
     return rf::fail(RF_ERR_CUDA, std::string("tensor-core GEMM: ") + cudaGetErrorString(attr_err));
   const int64_t tiles = (M + BM - 1) / BM * p.n_tiles_n;
   const int grid = (int)std::min<int64_t>(tiles, rf::num_sms());
-  kern<<<grid, NTHREADS, C::SMEM_BYTES, st>>>(ma, ma32, mb, p);
+  kern<<<grid, NTHREADS, C::SMEM_BYTES, st>>>(ma, ma32, mb, p, NoRemote{});
   return rf::check_launch("tensor-core dense GEMM (fp32 out)");
 }
 
@@ -789,6 +835,14 @@ int tc_dense_f32(const void *a, const void *w, float *out, int64_t M, int64_t N,
   if (bn == 64) return launch_dense<__half, 64>(ma, ma32, mb, p, M, st);
   if (bn == 128) return launch_dense<__half, 128>(ma, ma32, mb, p, M, st);
   return launch_dense<__half, 256>(ma, ma32, mb, p, M, st);
+}
+
+int tc_down_remote(const GroupedGemmArgs &g, cudaStream_t st) {
+  if (!g.remote || g.slot || g.groups || g.gather_src) return -1;
+  if (g.rows_capacity <= 0 || g.n_groups < 1 || g.remote->R < 1 || g.remote->R > REMOTE_MAX_RANKS) return -1;
+  int rc = RF_OK;
+  if (!try_tc(g, false, st, &rc)) return -1;
+  return rc;
 }
 }  // namespace rf
 

@@ -608,6 +608,7 @@ class EPFusedMoE(nn.Module):
             }
         recv_cap = R * self.max_tokens_per_rank * Kk
         st["recv_cap"] = recv_cap
+        st["back_cap"] = self.max_tokens_per_rank * Kk
         st["rows_cap"] = recv_cap + st["S"] * (K.ALIGN - 1)
         px = self._exchange()
         px.ensure(recv_cap, self.max_tokens_per_rank * Kk, row_bytes)
@@ -632,7 +633,8 @@ class EPFusedMoE(nn.Module):
         st = stream_of(dev)
         check(lib().rf_moe_ep_devplan(cnt.data_ptr(), stt["flat"].data_ptr(), stt["offs"].data_ptr(), R, E,
                                       self.ep_rank, S, nslots, K.ALIGN, self.split_rounds, stt["recv_cap"],
-                                      stt["rows_cap"], ws.data_ptr(), ws.numel(), st), "rf_moe_ep_devplan")
+                                      stt["back_cap"], stt["rows_cap"], ws.data_ptr(), ws.numel(), st),
+              "rf_moe_ep_devplan")
         self._mark("device plan")
         epoch = px.next_epoch()
         ctrl = px.peer[2]
@@ -647,16 +649,35 @@ class EPFusedMoE(nn.Module):
         px.wait(DISPATCH)
         self._mark("dispatch wait")
         y = None
+        back = (ctypes.c_void_p * R)(*px.peer[1])
+        returned = False
         if S > 0:
-            xl = torch.empty(stt["rows_cap"], H, dtype=x2.dtype, device=dev)
+            rows = stt["rows_cap"]
+            xl = torch.empty(rows, H, dtype=x2.dtype, device=dev)
             check(lib().rf_moe_ep_devplan_regroup(ws.data_ptr(), R, E, S, nslots, px.recv_ptr(), xl.data_ptr(),
                                                   row_bytes, st), "rf_moe_ep_devplan_regroup")
             self._mark("regroup gather")
-            y = self._expert_gemms(xl, None, stt["seg_off"], stt["seg_cnt"])
-        check(lib().rf_moe_ep_devplan_push(ws.data_ptr(), R, E, S, nslots, 1, y.data_ptr() if y is not None else None,
-                                           None, 1, row_bytes, (ctypes.c_void_p * R)(*px.peer[1]), flags1, epoch,
-                                           done, st), "rf_moe_ep_devplan_push")
-        self._mark("return push")
+            w1b, w2b = self._gemm_banks()
+            I = self.intermediate_size
+            h = torch.empty(rows, I, dtype=x2.dtype, device=dev)
+            K.grouped_gemm_gated(xl, w1b, stt["seg_off"], stt["seg_cnt"], h, activation=self.activation)
+            self._mark("gated GEMM")
+            # the down GEMM's epilogue stores every row into its token rank's
+            # return buffer (the exchange overlaps the GEMM tile by tile)
+            rc = lib().rf_moe_ep_devplan_down_return(ws.data_ptr(), R, E, S, nslots, h.data_ptr(), w2b.data_ptr(),
+                                                     rows, H, I, dtype_code(x2.dtype), back, flags1, epoch, done, st)
+            if rc == _lib_mod.RF_ERR_UNSUPPORTED:  # no tensor-core path: down GEMM, then the push
+                y = torch.empty(rows, H, dtype=x2.dtype, device=dev)
+                K.grouped_gemm_down(h, w2b, stt["seg_off"], stt["seg_cnt"], y)
+            else:
+                check(rc, "rf_moe_ep_devplan_down_return")
+                returned = True
+            self._mark("down GEMM + return")
+        if not returned:
+            check(lib().rf_moe_ep_devplan_push(ws.data_ptr(), R, E, S, nslots, 1,
+                                               y.data_ptr() if y is not None else None, None, 1, row_bytes, back,
+                                               flags1, epoch, done, st), "rf_moe_ep_devplan_push")
+            self._mark("return push")
         px.wait(RETURN)
         self._mark("return wait")
         out = torch.empty(T, H, dtype=x2.dtype, device=dev)

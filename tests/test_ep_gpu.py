@@ -199,7 +199,7 @@ def test_device_plan_matches_host_plan_and_round_trips(cuda_ok, seed):
         assert L.rf_moe_ep_devplan_layout(R, E, S, nslots, lo.ctypes.data) == 0
         rows_cap = cap_recv + S * 128
         assert L.rf_moe_ep_devplan(cnt.data_ptr(), flat_d.data_ptr(), offs_d.data_ptr(), R, E, me, S, nslots, 128, 4,
-                                   cap_recv, rows_cap, w.data_ptr(), nb, st) == 0
+                                   cap_recv, max(Ts) * topk, rows_cap, w.data_ptr(), nb, st) == 0
         ws.append(w)
         lay.append(lo)
     torch.cuda.synchronize()
@@ -254,4 +254,80 @@ def test_device_plan_matches_host_plan_and_round_trips(cuda_ok, seed):
         assert torch.equal(got, want), f"rank {me}: rows did not come back"
     torch.cuda.synchronize()
     assert all(bool((c[:2 * R] == 7).all()) for c in ctrl), "every rank raised its flags in every peer"
+
+    # the down GEMM with the return exchange in its epilogue stores exactly the
+    # rows of "down GEMM, then the return push"
+    w2s = [(torch.randn(len(pl.slots[me]), H, H, generator=g) * 0.1).bfloat16().to(dev) for me in range(R)]
+    fused = [torch.zeros_like(b) for b in back]
+    plain = [torch.zeros_like(b) for b in back]
+    for me in range(R):
+        S = len(pl.slots[me])
+        lo = lay[me]
+        seg_off = ws[me][lo[0]:lo[0] + 4 * (S + 1)].view(torch.int32)
+        seg_cnt = ws[me][lo[1]:lo[1] + 4 * S].view(torch.int32)
+        rows = ys[me].shape[0]
+        y = torch.zeros(rows, H, dtype=torch.bfloat16, device=dev)
+        K.grouped_gemm_down(ys[me], w2s[me], seg_off, seg_cnt, y)
+        flags = (ctypes.c_void_p * R)(*[ctrl[d].data_ptr() + 4 * (R + me) for d in range(R)])
+        assert L.rf_moe_ep_devplan_push(ws[me].data_ptr(), R, E, S, nslots, 1, y.data_ptr(), None, 1, row_bytes,
+                                        ptrs(plain), flags, 8, done.data_ptr() + 4 * me, st) == 0
+        assert L.rf_moe_ep_devplan_down_return(ws[me].data_ptr(), R, E, S, nslots, ys[me].data_ptr(),
+                                               w2s[me].data_ptr(), rows, H, H, _lib.dtype_code(torch.bfloat16),
+                                               ptrs(fused), flags, 9, done.data_ptr() + 4 * me, st) == 0
+    torch.cuda.synchronize()
+    for me in range(R):
+        n = Ts[me] * topk
+        assert torch.equal(fused[me][:n], plain[me][:n]), f"rank {me}: fused return differs"
+    assert all(bool((c[R:2 * R] == 9).all()) for c in ctrl), "the fused GEMM raised its flags in every peer"
+    assert _lib.device_status() == 0
+
+
+def test_device_plan_too_small_buffers_move_nothing(cuda_ok):
+    """A plan that needs more rows than the receive buffers hold fails on every
+    rank at once (the capacity check is global): the error word reads
+    RF_DEV_PLAN_OVERFLOW, the GEMM segments are empty, the pushes write no row
+    and still raise their flags (so no peer waits out its limit)."""
+    import ctypes
+    import numpy as np
+    from reframework_b200 import _lib
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    R, E, topk, H = 2, 4, 2, 64
+    slots = [[0, 1], [2, 3]]
+    flat = torch.tensor([e for s in slots for e in s], dtype=torch.int32, device=dev)
+    offs = torch.tensor([0, 2, 4], dtype=torch.int32, device=dev)
+    Ts = [40, 24]
+    cnt = torch.tensor([[20, 20, 20, 20], [12, 12, 12, 12]], dtype=torch.int32, device=dev)  # T*K per rank
+    recv_cap = 50  # rank 0 receives 40 + 24 = 64 rows
+    st = torch.cuda.current_stream(dev).cuda_stream
+    assert _lib.device_status() == 0
+    ws, lay = [], []
+    for me in range(R):
+        nb = L.rf_moe_ep_devplan_workspace_size(R, E, 2, 4)
+        w = torch.full((nb,), 0x55, dtype=torch.uint8, device=dev)  # stale bytes everywhere
+        lo = np.zeros(12, np.int64)
+        assert L.rf_moe_ep_devplan_layout(R, E, 2, 4, lo.ctypes.data) == 0
+        assert L.rf_moe_ep_devplan(cnt.data_ptr(), flat.data_ptr(), offs.data_ptr(), R, E, me, 2, 4, 128, 4,
+                                   recv_cap, max(Ts) * topk, recv_cap + 2 * 127, w.data_ptr(), nb, st) == 0
+        ws.append(w)
+        lay.append(lo)
+    assert _lib.device_status() == 3  # RF_DEV_PLAN_OVERFLOW (read and cleared)
+    for me in range(R):
+        wb, lo = ws[me].cpu().numpy(), lay[me]
+        assert wb[lo[2]:lo[2] + 4].view(np.int32)[0] == 1, f"rank {me}: plan not flagged"
+        assert not wb[lo[0]:lo[0] + 12].view(np.int32).any() and not wb[lo[1]:lo[1] + 8].view(np.int32).any()
+        assert wb[lo[4]:lo[4] + 8].view(np.int64)[0] == 0 and wb[lo[3]:lo[3] + 8].view(np.int64)[0] == 0
+    recv = [torch.zeros(recv_cap, H, dtype=torch.bfloat16, device=dev) for _ in range(R)]
+    ctrl = [torch.zeros(2 * R, dtype=torch.int32, device=dev) for _ in range(R)]
+    done = torch.zeros(R, dtype=torch.int32, device=dev)
+    x = torch.randn(max(Ts), H, device=dev).bfloat16()
+    src_slot = torch.arange(max(Ts) * topk, dtype=torch.int32, device=dev)
+    for me in range(R):
+        flags = (ctypes.c_void_p * R)(*[ctrl[d].data_ptr() + 4 * me for d in range(R)])
+        assert L.rf_moe_ep_devplan_push(ws[me].data_ptr(), R, E, 2, 4, 0, x.data_ptr(), src_slot.data_ptr(), topk,
+                                        H * 2, (ctypes.c_void_p * R)(*[t.data_ptr() for t in recv]), flags, 5,
+                                        done.data_ptr() + 4 * me, st) == 0
+    torch.cuda.synchronize()
+    assert all(not bool(t.any()) for t in recv), "a failed plan moved rows"
+    assert all(bool((c[:R] == 5).all()) for c in ctrl), "flags must rise even when nothing moves"
     assert _lib.device_status() == 0

@@ -354,14 +354,28 @@ int rf_moe_ep_wait(const int32_t *flags, int32_t R, int32_t epoch, rf_stream_t s
  *   GEMM arguments), [2] int32 overflow, [3] int64 recv_total, [4] int64 n_send,
  *   [5] workspace bytes, [6] int64 send_off [R+1], [7] int64 dst_row0 [R],
  *   [8] int64 recv_off [R+1], [9] int64 back_row0 [R], [10] int32 identity,
- *   [11] int64 rows used.
+ *   [11] int64 rows used, [12] int64 cs [R][S+1] (rows from source s for the
+ *   slots below j), [13] int64 cj [S][R+1] (rows of slot j from the sources
+ *   below s), [14] int64 pstart [R][S] (source s's permuted row of its first
+ *   row for slot j), [15] int64 piece_pos [n_pieces+1], [16] int64 piece_src
+ *   [n_pieces] (send positions [piece_pos[k], piece_pos[k+1]) carry permuted
+ *   rows from piece_src[k]), [17] int32 n_pieces.  `out` holds
+ *   RF_EP_DEVPLAN_LAYOUT_N entries.
  */
+#define RF_EP_DEVPLAN_LAYOUT_N 18
 size_t rf_moe_ep_devplan_workspace_size(int32_t R, int32_t E, int32_t S, int32_t n_slots);
 int rf_moe_ep_devplan_layout(int32_t R, int32_t E, int32_t S, int32_t n_slots, int64_t *out);
 int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_experts, const int32_t *slot_offsets,
                       int32_t R, int32_t E, int32_t me, int32_t S, int32_t n_slots, int32_t align,
                       int32_t rounds, int64_t recv_capacity, int64_t back_capacity, int64_t rows_capacity,
                       void *workspace, size_t ws_bytes, rf_stream_t stream);
+/* The planner of rf_moe_ep_devplan (the same source) run on the host over host
+ * buffers, for checks on the CPU: *status gets the RF_DEV_* code the kernel
+ * would have reported (0 = a valid plan). */
+int rf_moe_ep_devplan_host(const int32_t *counts, const int32_t *slot_experts, const int32_t *slot_offsets,
+                           int32_t R, int32_t E, int32_t me, int32_t S, int32_t n_slots, int32_t align,
+                           int32_t rounds, int64_t recv_capacity, int64_t back_capacity, int64_t rows_capacity,
+                           void *workspace, size_t ws_bytes, int32_t *status);
 int rf_moe_ep_devplan_push(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
                            int32_t dir, const void *src, const int32_t *src_slot, int64_t div,
                            int64_t row_bytes, void *const *dst, int32_t *const *flag, int32_t epoch,

@@ -75,6 +75,10 @@ _SIGNATURES = {
     "rf_moe_ep_devplan_layout": (_int, [ctypes.c_int32] * 4 + [_c_void_p]),
     "rf_moe_ep_devplan": (_int, [_c_void_p, _c_void_p, _c_void_p] + [ctypes.c_int32] * 7 + [_i64, _i64, _i64, _c_void_p,
                                                                                            ctypes.c_size_t, _c_void_p]),
+    "rf_moe_ep_devplan_host": (_int, [_c_void_p, _c_void_p, _c_void_p] + [ctypes.c_int32] * 7 + [_i64, _i64, _i64,
+                                                                                                _c_void_p,
+                                                                                                ctypes.c_size_t,
+                                                                                                _c_void_p]),
     "rf_moe_ep_devplan_push": (_int, [_c_void_p] + [ctypes.c_int32] * 5 + [_c_void_p, _c_void_p, _i64, _i64,
                                                                             _c_void_p, _c_void_p, ctypes.c_int32,
                                                                             _c_void_p, _c_void_p]),
@@ -152,6 +156,7 @@ def device_status() -> int:
 
 _gemm_impl = 0
 RF_ERR_UNSUPPORTED = 2
+EP_DEVPLAN_LAYOUT_N = 18  # entries of rf_moe_ep_devplan_layout's output (RF_EP_DEVPLAN_LAYOUT_N)
 
 
 def set_gemm_impl(impl: int) -> None:

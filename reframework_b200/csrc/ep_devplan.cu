@@ -56,7 +56,7 @@ struct RfEpDevPlan {
 
 namespace {
 
-__device__ void waterfill_dev(int64_t n, const int64_t *base, int m, int64_t *out, int *order, int64_t *loads,
+__host__ __device__ void waterfill_dev(int64_t n, const int64_t *base, int m, int64_t *out, int *order, int64_t *loads,
                               int64_t *give) {
   for (int i = 0; i < m; ++i) order[i] = i;
   for (int i = 1; i < m; ++i) {  // stable insertion sort by base
@@ -101,7 +101,7 @@ struct PlannerArgs {
   const int32_t *counts;        // [R][E]
   const int32_t *slot_experts;  // [total slots]
   const int32_t *slot_offsets;  // [R+1]
-  int R, E, me, S, align, rounds;  // S: this rank's slot count as the host laid out the workspace
+  int R, E, me, S, n_slots, align, rounds;  // S: this rank's slot count as the host laid out the workspace
   int64_t recv_capacity, back_capacity;  // every rank's receive / return buffer rows
   int64_t rows_capacity;                 // this rank's slot-major GEMM rows
   RfEpDevPlan *plan;
@@ -114,7 +114,7 @@ struct PlannerArgs {
   int32_t *hoff, *hlist;        // holders CSR: [E+1], [total slots]
 };
 
-__device__ int64_t piece_dev(const PlannerArgs &a, int e, int src, int h, int64_t *offset) {
+__host__ __device__ int64_t piece_dev(const PlannerArgs &a, int e, int src, int h, int64_t *offset) {
   const int R = a.R;
   const int64_t qlo = a.sc.lo[(int64_t)e * R + h], qhi = qlo + a.sc.quota[(int64_t)e * R + h];
   const int64_t slo = a.sc.sbase[(int64_t)e * R + src], shi = slo + a.counts[(int64_t)src * a.E + e];
@@ -124,7 +124,7 @@ __device__ int64_t piece_dev(const PlannerArgs &a, int e, int src, int h, int64_
 }
 
 // A failed plan moves no row and gives the GEMMs empty segments.
-__device__ void clear_plan(RfEpDevPlan *P, int S) {
+__host__ __device__ void clear_plan(RfEpDevPlan *P, int S) {
   for (int j = 0; j <= S; ++j) {
     P->loff[j] = 0;
     P->loff32[j] = 0;
@@ -138,16 +138,55 @@ __device__ void clear_plan(RfEpDevPlan *P, int S) {
   P->overflow = 1;
 }
 
-__global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
+// Runs the planner body: one block on the device (threads meet at barriers and
+// share `bad` in shared memory), one thread on the host (the same code, for
+// checks on the CPU; errors are recorded instead of setting the error word).
+struct PlanExec {
+  int *bad;
+  int code = 0;
+  __host__ __device__ int tid() const {
+#ifdef __CUDA_ARCH__
+    return (int)threadIdx.x;
+#else
+    return 0;
+#endif
+  }
+  __host__ __device__ int nthreads() const {
+#ifdef __CUDA_ARCH__
+    return (int)blockDim.x;
+#else
+    return 1;
+#endif
+  }
+  __host__ __device__ void sync() const {
+#ifdef __CUDA_ARCH__
+    __syncthreads();
+#endif
+  }
+  __host__ __device__ void report(int c) {
+#ifdef __CUDA_ARCH__
+    rf_report(c);
+#else
+    if (!code) code = c;
+#endif
+  }
+};
+
+__host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
   const int R = a.R, E = a.E, me = a.me;
   RfEpDevPlan *P = a.plan;
-  __shared__ int s_bad;
-  if (threadIdx.x == 0) {
-    s_bad = a.slot_offsets[me + 1] - a.slot_offsets[me] != a.S ? 1 : 0;
+  int &s_bad = *x.bad;
+  if (x.tid() == 0) {
+    s_bad = 0;
+    // the placement: offsets from 0 to n_slots, ascending, this rank's count as laid out
+    if (a.slot_offsets[0] != 0 || a.slot_offsets[R] != a.n_slots) s_bad = 1;
+    for (int r = 0; r < R; ++r)
+      if (a.slot_offsets[r + 1] < a.slot_offsets[r]) s_bad = 1;
+    if (!s_bad && a.slot_offsets[me + 1] - a.slot_offsets[me] != a.S) s_bad = 1;
     int64_t *quota = a.sc.quota, *lo = a.sc.lo, *sbase = a.sc.sbase, *total = a.sc.total, *load = a.sc.load;
     // holders of every expert, in rank order (CSR)
     for (int e = 0; e <= E; ++e) a.hoff[e] = 0;
-    for (int r = 0; r < R; ++r)
+    for (int r = 0; r < R && !s_bad; ++r)
       for (int s = a.slot_offsets[r]; s < a.slot_offsets[r + 1]; ++s) {
         const int e = a.slot_experts[s];
         if (e < 0 || e >= E) s_bad = 1;
@@ -158,6 +197,9 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
     for (int e = 0; e < E; ++e) a.sc.repl[e] = a.hoff[e];  // fill cursors
     for (int r = 0; r < R && !s_bad; ++r)
       for (int s = a.slot_offsets[r]; s < a.slot_offsets[r + 1]; ++s) a.hlist[a.sc.repl[a.slot_experts[s]]++] = r;
+    for (int e = 0; e < E && !s_bad; ++e)  // no rank holds an expert twice
+      for (int h = a.hoff[e] + 1; h < a.hoff[e + 1]; ++h)
+        if (a.hlist[h] == a.hlist[h - 1]) s_bad = 1;
     for (int r = 0; r < R; ++r)
       for (int e = 0; e < E; ++e) {
         const int32_t c = a.counts[(int64_t)r * E + e];
@@ -225,45 +267,45 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
       }
     }
   }
-  __syncthreads();
+  x.sync();
   if (s_bad) {
-    if (threadIdx.x == 0) {
+    if (x.tid() == 0) {
       clear_plan(P, a.S);
-      rf_report(RF_DEV_BAD_EXPERT_ID);
+      x.report(RF_DEV_BAD_EXPERT_ID);
     }
     return;
   }
   // the all-to-all matrix M[s][d], one (s, d) pair per thread, and every
   // source's expert-major row starts (its permuted layout, align 1)
-  for (int t = threadIdx.x; t < R * R; t += blockDim.x) {
+  for (int t = x.tid(); t < R * R; t += x.nthreads()) {
     const int s = t / R, d = t % R;
     int64_t n = 0;
     for (int sl = a.slot_offsets[d]; sl < a.slot_offsets[d + 1]; ++sl) n += piece_dev(a, a.slot_experts[sl], s, d, nullptr);
     a.M[t] = n;
   }
-  for (int s = threadIdx.x; s < R; s += blockDim.x) {
+  for (int s = x.tid(); s < R; s += x.nthreads()) {
     int64_t *c = a.cpre + (int64_t)s * (E + 1);
     c[0] = 0;
     for (int e = 0; e < E; ++e) c[e + 1] = c[e] + a.counts[(int64_t)s * E + e];
   }
-  __syncthreads();
+  x.sync();
   // every rank's buffers (the same check on every rank: all plans fail together)
-  if (threadIdx.x == 0) {
+  if (x.tid() == 0) {
     for (int d = 0; d < R; ++d) {
       int64_t in = 0;
       for (int s = 0; s < R; ++s) in += a.M[(int64_t)s * R + d];
       if (in > a.recv_capacity || a.cpre[(int64_t)d * (E + 1) + E] > a.back_capacity) s_bad = 1;
     }
   }
-  __syncthreads();
+  x.sync();
   if (s_bad) {
-    if (threadIdx.x == 0) {
+    if (x.tid() == 0) {
       clear_plan(P, a.S);
-      rf_report(RF_DEV_PLAN_OVERFLOW);
+      x.report(RF_DEV_PLAN_OVERFLOW);
     }
     return;
   }
-  if (threadIdx.x != 0) return;
+  if (x.tid() != 0) return;
   // ---- this rank's tables
   int bad = 0;
   P->R = R;
@@ -337,8 +379,14 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
   P->overflow = bad;
   if (bad) {
     clear_plan(P, S);
-    rf_report(RF_DEV_PLAN_OVERFLOW);
+    x.report(RF_DEV_PLAN_OVERFLOW);
   }
+}
+
+__global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
+  __shared__ int s_bad;
+  PlanExec x{&s_bad};
+  planner_body(a, x);
 }
 
 }  // namespace
@@ -502,21 +550,30 @@ extern "C" int rf_moe_ep_devplan_layout(int32_t R, int32_t E, int32_t S, int32_t
   out[9] = (int64_t)(L.plan + offsetof(RfEpDevPlan, back_row0));  // int64 [R]
   out[10] = (int64_t)(L.plan + offsetof(RfEpDevPlan, identity));  // int32
   out[11] = (int64_t)(L.plan + offsetof(RfEpDevPlan, rows_used)); // int64
+  out[12] = (int64_t)L.cs;                                         // int64 [R][S+1] receive prefix per source
+  out[13] = (int64_t)L.cj;                                         // int64 [S][R+1] receive prefix per slot
+  out[14] = (int64_t)L.ps;                                         // int64 [R][S]   permuted row starts
+  out[15] = (int64_t)(L.plan + offsetof(RfEpDevPlan, piece_pos));  // int64 [n_pieces+1] send pieces
+  out[16] = (int64_t)(L.plan + offsetof(RfEpDevPlan, piece_src));  // int64 [n_pieces]
+  out[17] = (int64_t)(L.plan + offsetof(RfEpDevPlan, n_pieces));   // int32
   return RF_OK;
 }
 
-extern "C" int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_experts, const int32_t *slot_offsets,
-                                 int32_t R, int32_t E, int32_t me, int32_t S, int32_t n_slots, int32_t align,
-                                 int32_t rounds, int64_t recv_capacity, int64_t back_capacity, int64_t rows_capacity,
-                                 void *workspace, size_t ws_bytes, rf_stream_t stream) {
-  RF_CHECK_ARG(counts && slot_experts && slot_offsets && workspace, "rf_moe_ep_devplan: null pointer");
-  RF_CHECK_ARG(R >= 1 && R <= MAXR && E >= 1 && me >= 0 && me < R && S >= 0 && S <= MAXS && align >= 1 &&
-                   rounds >= 0,
-               "rf_moe_ep_devplan: bad sizes (R <= 64, slots per rank <= 1024)");
+namespace {
+
+// Checks the sizes and lays the planner's arguments out in `workspace`.
+int planner_args(PlannerArgs &a, const int32_t *counts, const int32_t *slot_experts, const int32_t *slot_offsets,
+                 int32_t R, int32_t E, int32_t me, int32_t S, int32_t n_slots, int32_t align, int32_t rounds,
+                 int64_t recv_capacity, int64_t back_capacity, int64_t rows_capacity, void *workspace,
+                 size_t ws_bytes, const char *name) {
+  const std::string nm(name);
+  RF_CHECK_ARG(counts && slot_experts && slot_offsets && workspace, nm + ": null pointer");
+  RF_CHECK_ARG(R >= 1 && R <= MAXR && E >= 1 && me >= 0 && me < R && S >= 0 && S <= MAXS && n_slots >= S &&
+                   align >= 1 && rounds >= 0,
+               nm + ": bad sizes (R <= 64, slots per rank <= 1024)");
   const Layout L = layout_of(R, E, S, n_slots);
-  RF_CHECK_ARG(ws_bytes >= L.bytes && (uintptr_t)workspace % 16 == 0, "rf_moe_ep_devplan: workspace too small");
+  RF_CHECK_ARG(ws_bytes >= L.bytes && (uintptr_t)workspace % 16 == 0, nm + ": workspace too small");
   uint8_t *w = reinterpret_cast<uint8_t *>(workspace);
-  PlannerArgs a;
   a.counts = counts;
   a.slot_experts = slot_experts;
   a.slot_offsets = slot_offsets;
@@ -524,6 +581,7 @@ extern "C" int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_expe
   a.E = E;
   a.me = me;
   a.S = S;
+  a.n_slots = n_slots;
   a.align = align;
   a.rounds = rounds;
   a.recv_capacity = recv_capacity;
@@ -543,8 +601,39 @@ extern "C" int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_expe
   a.M = reinterpret_cast<int64_t *>(w + L.M);
   a.hoff = reinterpret_cast<int32_t *>(w + L.hoff);
   a.hlist = reinterpret_cast<int32_t *>(w + L.hlist);
+  return RF_OK;
+}
+
+}  // namespace
+
+extern "C" int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_experts, const int32_t *slot_offsets,
+                                 int32_t R, int32_t E, int32_t me, int32_t S, int32_t n_slots, int32_t align,
+                                 int32_t rounds, int64_t recv_capacity, int64_t back_capacity, int64_t rows_capacity,
+                                 void *workspace, size_t ws_bytes, rf_stream_t stream) {
+  PlannerArgs a;
+  const int rc = planner_args(a, counts, slot_experts, slot_offsets, R, E, me, S, n_slots, align, rounds,
+                              recv_capacity, back_capacity, rows_capacity, workspace, ws_bytes, "rf_moe_ep_devplan");
+  if (rc != RF_OK) return rc;
   ep_planner_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(a);
   return rf::check_launch("rf_moe_ep_devplan");
+}
+
+extern "C" int rf_moe_ep_devplan_host(const int32_t *counts, const int32_t *slot_experts,
+                                      const int32_t *slot_offsets, int32_t R, int32_t E, int32_t me, int32_t S,
+                                      int32_t n_slots, int32_t align, int32_t rounds, int64_t recv_capacity,
+                                      int64_t back_capacity, int64_t rows_capacity, void *workspace, size_t ws_bytes,
+                                      int32_t *status) {
+  RF_CHECK_ARG(status, "rf_moe_ep_devplan_host: null status");
+  PlannerArgs a;
+  const int rc = planner_args(a, counts, slot_experts, slot_offsets, R, E, me, S, n_slots, align, rounds,
+                              recv_capacity, back_capacity, rows_capacity, workspace, ws_bytes,
+                              "rf_moe_ep_devplan_host");
+  if (rc != RF_OK) return rc;
+  int bad = 0;
+  PlanExec x{&bad};
+  planner_body(a, x);
+  *status = x.code;
+  return RF_OK;
 }
 
 // dir 0: dispatch (src = token rows x, src_slot/div map send positions to them);

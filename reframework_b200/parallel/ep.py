@@ -597,7 +597,7 @@ class EPFusedMoE(nn.Module):
             offs = np.ascontiguousarray(np.cumsum([0] + [len(s_) for s_ in self.placement.slots]), dtype=np.int32)
             S, nslots = len(self.placement.slots[self.ep_rank]), int(flat.size)
             nb = int(lib().rf_moe_ep_devplan_workspace_size(R, E, S, nslots))
-            lay = np.zeros(12, dtype=np.int64)
+            lay = np.zeros(_lib_mod.EP_DEVPLAN_LAYOUT_N, dtype=np.int64)
             check(lib().rf_moe_ep_devplan_layout(R, E, S, nslots, lay.ctypes.data), "rf_moe_ep_devplan_layout")
             ws = torch.zeros(nb, dtype=torch.uint8, device=dev)
             st = self._dp = {

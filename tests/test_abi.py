@@ -58,6 +58,13 @@ def test_version_and_sizes():
     assert lib.rf_moe_router_workspace_size(64, 2048, 60, 1) >= 8 * 64 * 61 * 4
 
 
+def test_header_constants_match_bindings():
+    src = open(HEADER).read()
+    assert int(re.search(r"#define RF_EP_DEVPLAN_LAYOUT_N (\d+)", src).group(1)) == _lib.EP_DEVPLAN_LAYOUT_N
+    codes = {int(v): k for k, v in re.findall(r"#define (RF_DEV_[A-Z_]+) (\d+)", src)}
+    assert set(codes) == set(_lib.DEV_ERRORS), "every device error code has a message"
+
+
 def test_fused_gather_gemm_reports_unsupported_dtype():
     """fp32 has no tensor-core path: the fused-gather GEMM declines (status 2)
     without touching a GPU, and the caller gathers explicitly."""

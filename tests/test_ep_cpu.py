@@ -244,3 +244,166 @@ def test_current_without_group_raises():
     D.destroy()
     with pytest.raises(RuntimeError, match="No process group"):
         D.current()
+
+
+# ------------------------------------------------ device planner, run on the host
+def _aligned_bytes(n):
+    buf = np.zeros(n + 16, np.uint8)
+    off = (-buf.ctypes.data) % 16
+    return buf[off:off + n]
+
+
+def _devplan_host(cnt, flat, offs, R, E, me, align, recv_cap, back_cap, rows_cap, S=None):
+    """rf_moe_ep_devplan's planner (same source) on the host: (status, ws, layout)."""
+    import ctypes
+    from reframework_b200 import _lib
+    L = _lib.lib()
+    S = int(offs[me + 1] - offs[me]) if S is None else S
+    nslots = int(flat.size)
+    nb = L.rf_moe_ep_devplan_workspace_size(R, E, S, nslots)
+    ws = _aligned_bytes(nb)
+    ws[:] = 0x55  # stale bytes: every table the row kernels read must be written
+    lay = np.zeros(_lib.EP_DEVPLAN_LAYOUT_N, np.int64)
+    assert L.rf_moe_ep_devplan_layout(R, E, S, nslots, lay.ctypes.data) == 0
+    st = ctypes.c_int32(-1)
+    assert L.rf_moe_ep_devplan_host(cnt.ctypes.data, flat.ctypes.data, offs.ctypes.data, R, E, me, S, nslots, align,
+                                    4, recv_cap, back_cap, rows_cap, ws.ctypes.data, nb, ctypes.byref(st)) == 0
+    return st.value, ws, lay
+
+
+def _find_le(a, v):
+    """Largest index k with a[k] <= v (a ascending, a[0] <= v) — the row kernels' lookup."""
+    return np.searchsorted(a, v, side="right") - 1
+
+
+def _random_case(rng, max_r):
+    R = int(rng.integers(1, max_r + 1))
+    E = int(rng.integers(R, 3 * R + 4))
+    K = int(rng.integers(1, min(E, 4) + 1))
+    shards = [shard_range(E, R, r) for r in range(R)]
+    Ts = [int(rng.integers(0, 120)) if rng.random() > 0.1 else 0 for _ in range(R)]
+    cnt = np.zeros((R, E), np.int32)
+    for r in range(R):  # each token routes to K distinct experts, skewed
+        p = rng.dirichlet(np.full(E, 0.4))
+        for _ in range(Ts[r]):
+            cnt[r, rng.choice(E, size=K, replace=False, p=p)] += 1
+    pl = place_experts(cnt.sum(0) + 1, shards, int(rng.integers(0, 4)))
+    flat = np.ascontiguousarray([e for s in pl.slots for e in s], dtype=np.int32)
+    offs = np.ascontiguousarray(np.cumsum([0] + [len(s) for s in pl.slots]), dtype=np.int32)
+    return R, E, K, Ts, cnt, pl, flat, offs
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_device_planner_on_host_matches_host_plan_and_round_trips(seed):
+    """The device planner's own code (compiled for the host) against the host
+    planner for every rank, then the dispatch / regroup / return index math of
+    the row kernels replayed over its tables: every (token, slot) row comes back
+    to its own permuted row on its own rank, each exactly once, and every GEMM
+    segment holds only rows of its slot's expert."""
+    from reframework_b200 import _lib
+    L = _lib.lib()
+    rng = np.random.default_rng(1000 + seed)
+    R, E, K, Ts, cnt, pl, flat, offs = _random_case(rng, 64 if seed % 10 == 9 else 12)
+    align = 128 if seed % 2 else 1
+    recv_cap = max(int(cnt.sum()), 1)
+    back_cap = max(max(Ts) * K, 1)
+    M = np.zeros(R * R, np.int64)
+    assert L.rf_moe_ep_pair_rows(cnt.ctypes.data, R, E, flat.ctypes.data, offs.ctypes.data, 4, M.ctypes.data) == 0
+    M = M.reshape(R, R)
+    cpre = np.concatenate([np.zeros((R, 1), np.int64), np.cumsum(cnt, axis=1)], axis=1)
+    plans = []
+    for me in range(R):
+        S = int(offs[me + 1] - offs[me])
+        st, wb, lo = _devplan_host(cnt, flat, offs, R, E, me, align, recv_cap, back_cap, recv_cap + S * align)
+        assert st == 0, f"rank {me}: status {st}"
+        i64 = lambda off, n: wb[off:off + 8 * n].view(np.int64)
+        i32 = lambda off, n: wb[off:off + 4 * n].view(np.int32)
+        send = np.zeros(R, np.int64)
+        recvs = np.zeros(R, np.int64)
+        hl = np.zeros(15, np.int64)
+        buf = np.zeros(4 * int(cnt.sum()) + 4096, np.int32)
+        assert L.rf_moe_ep_plan(cnt.ctypes.data, R, E, me, flat.ctypes.data, offs.ctypes.data, align, 4,
+                                send.ctypes.data, recvs.ctypes.data, buf.ctypes.data, buf.size, hl.ctypes.data) == 0
+        assert i32(lo[2], 1)[0] == 0
+        send_off, recv_off = i64(lo[6], R + 1), i64(lo[8], R + 1)
+        assert np.array_equal(send_off, np.concatenate([[0], np.cumsum(send)]))
+        assert np.array_equal(recv_off, np.concatenate([[0], np.cumsum(recvs)]))
+        assert np.array_equal(i64(lo[7], R), M[:me].sum(0) if me else np.zeros(R))
+        assert np.array_equal(i64(lo[9], R), M[:, :me].sum(1) if me else np.zeros(R))
+        seg = lambda i: buf[hl[2 * i]:hl[2 * i] + hl[2 * i + 1]]
+        assert np.array_equal(i32(lo[0], S + 1), seg(2)) and np.array_equal(i32(lo[1], S), seg(3))
+        assert i32(lo[10], 1)[0] == hl[13] and i64(lo[11], 1)[0] == hl[12]
+        npc = int(i32(lo[17], 1)[0])
+        plans.append(dict(S=S, send_off=send_off, recv_off=recv_off, dst_row0=i64(lo[7], R),
+                          loff=i32(lo[0], S + 1).astype(np.int64), lcount=i32(lo[1], S).astype(np.int64),
+                          cs=i64(lo[12], R * (S + 1)).reshape(R, S + 1), cj=i64(lo[13], S * (R + 1)).reshape(S, R + 1),
+                          ps=i64(lo[14], R * S).reshape(R, S), piece_pos=i64(lo[15], npc + 1),
+                          piece_src=i64(lo[16], npc), n_send=int(i64(lo[4], 1)[0])))
+    # dispatch: tag = source * 2^20 + its permuted row
+    recv = [np.full(max(int(recv_off_d[-1]), 1), -1, np.int64) for recv_off_d in (p["recv_off"] for p in plans)]
+    for s, p in enumerate(plans):
+        assert p["n_send"] == Ts[s] * K
+        i = np.arange(p["n_send"])
+        if not i.size:
+            continue
+        k = _find_le(p["piece_pos"][:-1], i)
+        src_row = p["piece_src"][k] + i - p["piece_pos"][k]
+        d = _find_le(p["send_off"][:R], i)
+        drow = p["dst_row0"][d] + i - p["send_off"][d]
+        assert np.array_equal(np.sort(src_row), np.arange(Ts[s] * K)), "every routed row is sent once"
+        for dd in np.unique(d):
+            recv[dd][drow[d == dd]] = (s << 20) + src_row[d == dd]
+    back = [np.full(max(T * K, 1), -1, np.int64) for T in Ts]
+    for me, p in enumerate(plans):
+        assert (recv[me][:p["recv_off"][-1]] >= 0).all(), f"rank {me}: receive rows left unwritten"
+        for j in range(p["S"]):
+            e = int(flat[offs[me] + j])
+            k = np.arange(p["lcount"][j])
+            if not k.size:
+                continue
+            s = _find_le(p["cj"][j, :R], k)
+            q = p["recv_off"][s] + p["cs"][s, j] + k - p["cj"][j, s]
+            rows = recv[me][q]  # regroup: GEMM rows of slot j
+            src, prow = rows >> 20, rows & ((1 << 20) - 1)
+            assert np.array_equal(src, s)
+            assert ((cpre[src, e] <= prow) & (prow < cpre[src, e + 1])).all(), f"slot {j} holds another expert's rows"
+            drow = p["ps"][s, j] + k - p["cj"][j, s]  # fused return: the source's permuted row
+            for ss in np.unique(s):
+                assert (back[ss][drow[s == ss]] == -1).all(), "a return row written twice"
+                back[ss][drow[s == ss]] = rows[s == ss]
+    for s in range(R):
+        assert np.array_equal(back[s][:Ts[s] * K], (s << 20) + np.arange(Ts[s] * K)), f"rank {s}: round trip"
+
+
+def test_device_planner_on_host_rejects_bad_placements_and_small_buffers():
+    """Status codes of the planner's own checks (host build of the same source):
+    a plan that needs more rows than the buffers hold fails on every rank with
+    RF_DEV_PLAN_OVERFLOW and empty segments; a broken placement fails with
+    RF_DEV_BAD_EXPERT_ID."""
+    R, E = 2, 4
+    cnt = np.array([[20, 20, 20, 20], [12, 12, 12, 12]], np.int32)
+    flat = np.array([0, 1, 2, 3], np.int32)
+    offs = np.array([0, 2, 4], np.int32)
+    for me in range(R):  # rank 0 receives 64 rows, capacity 50: both ranks' plans fail
+        st, wb, lo = _devplan_host(cnt, flat, offs, R, E, me, 1, 50, 80, 400)
+        assert st == 3
+        assert wb[lo[2]:lo[2] + 4].view(np.int32)[0] == 1
+        assert not wb[lo[0]:lo[0] + 12].view(np.int32).any() and not wb[lo[1]:lo[1] + 8].view(np.int32).any()
+        assert wb[lo[4]:lo[4] + 8].view(np.int64)[0] == 0
+    st, *_ = _devplan_host(cnt, flat, offs, R, E, 0, 1, 64, 79, 400)  # rank 0's 80 return rows, capacity 79
+    assert st == 3
+    st, *_ = _devplan_host(cnt, flat, offs, R, E, 0, 128, 64, 80, 64 + 127)  # GEMM rows: 2 x 128 > 191
+    assert st == 3
+    st, *_ = _devplan_host(cnt, flat, offs, R, E, 0, 1, 64, 80, 400)
+    assert st == 0
+    bad = [
+        (np.array([0, 1, 2, 7], np.int32), offs, None),          # expert id out of range
+        (np.array([0, 0, 2, 3], np.int32), offs, None),          # expert 0 twice on rank 0, expert 1 nowhere
+        (np.array([0, 1, 2, 2, 3], np.int32), np.array([0, 2, 5], np.int32), None),  # rank 1 holds expert 2 twice
+        (flat, np.array([0, 2, 3], np.int32), None),             # offsets end before n_slots
+        (flat, offs, 3),                                         # S differs from the placement
+    ]
+    for fl, of, S in bad:
+        st, wb, lo = _devplan_host(cnt, fl, of, R, E, 0, 1, 64, 80, 400, S=S)
+        assert st == 1, (fl, of, S)
+        assert wb[lo[2]:lo[2] + 4].view(np.int32)[0] == 1

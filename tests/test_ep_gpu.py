@@ -195,7 +195,7 @@ def test_device_plan_matches_host_plan_and_round_trips(cuda_ok, seed):
         S = len(pl.slots[me])
         nb = L.rf_moe_ep_devplan_workspace_size(R, E, S, nslots)
         w = torch.zeros(nb, dtype=torch.uint8, device=dev)
-        lo = np.zeros(12, np.int64)
+        lo = np.zeros(_lib.EP_DEVPLAN_LAYOUT_N, np.int64)
         assert L.rf_moe_ep_devplan_layout(R, E, S, nslots, lo.ctypes.data) == 0
         rows_cap = cap_recv + S * 128
         assert L.rf_moe_ep_devplan(cnt.data_ptr(), flat_d.data_ptr(), offs_d.data_ptr(), R, E, me, S, nslots, 128, 4,
@@ -305,7 +305,7 @@ def test_device_plan_too_small_buffers_move_nothing(cuda_ok):
     for me in range(R):
         nb = L.rf_moe_ep_devplan_workspace_size(R, E, 2, 4)
         w = torch.full((nb,), 0x55, dtype=torch.uint8, device=dev)  # stale bytes everywhere
-        lo = np.zeros(12, np.int64)
+        lo = np.zeros(_lib.EP_DEVPLAN_LAYOUT_N, np.int64)
         assert L.rf_moe_ep_devplan_layout(R, E, 2, 4, lo.ctypes.data) == 0
         assert L.rf_moe_ep_devplan(cnt.data_ptr(), flat.data_ptr(), offs.data_ptr(), R, E, me, 2, 4, 128, 4,
                                    recv_cap, max(Ts) * topk, recv_cap + 2 * 127, w.data_ptr(), nb, st) == 0

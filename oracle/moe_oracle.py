@@ -27,7 +27,7 @@ Harness adaptations (not in the reference; both are opt-in):
 from __future__ import annotations
 
 import math
-from typing import Dict, List, Optional, Sequence, Tuple
+from typing import Dict, Optional, Tuple
 
 import numpy as np
 import torch

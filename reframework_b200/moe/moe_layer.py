@@ -32,7 +32,6 @@ Opt-in extensions (default off, reference behaviour unchanged):
 from __future__ import annotations
 
 import logging
-import math
 import time
 from collections import deque
 from typing import Deque, Dict, List, Optional, Sequence, Tuple

@@ -25,9 +25,8 @@ expert weights, x [T,H], then the bias.  Changing it changes every fixture.
 
 from __future__ import annotations
 
-import math
-from dataclasses import dataclass, field, replace
-from typing import Dict, List, Optional
+from dataclasses import dataclass, replace
+from typing import Dict, Optional
 
 import numpy as np
 import torch

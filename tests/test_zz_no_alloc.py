@@ -9,8 +9,6 @@ This file is collected last so that, in a run that stops at the first failure,
 every other test has already run; it also passes on its own in a fresh process
 (the first call performs the per-device set-up)."""
 
-import ctypes
-
 import pytest
 import torch
 

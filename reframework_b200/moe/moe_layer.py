@@ -118,6 +118,17 @@ def adjacent_router_weights(owner, gate: torch.Tensor,
     return cat[:-1], cat[-1]
 
 
+def reference_output(out: torch.Tensor, x: torch.Tensor, hidden: int) -> torch.Tensor:
+    """The layer output in the input's dtype and the reference's shape
+    (moe_layer.py:519, ep.py:150): ``[x.shape[0], hidden]`` for an input of two
+    or more dimensions (``[B, 1, H]`` gives ``[B, H]``; like the reference's
+    reshape, ``[B, S > 1, H]`` is rejected), ``[1, hidden]`` for one ``[H]``
+    token."""
+    if out.dtype != x.dtype:
+        out = out.to(x.dtype)
+    return out.reshape(x.shape[:1] + (hidden,)) if x.dim() > 1 else out
+
+
 class FusedMoE(nn.Module):
     """A routed MoE block: ``gate`` -> top-k -> grouped expert GEMMs -> combine."""
 
@@ -327,11 +338,7 @@ class FusedMoE(nn.Module):
         return self._shape_like(normed, x), self._shape_like(res, x)
 
     def _shape_like(self, out: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
-        if out.dtype != x.dtype:
-            out = out.to(x.dtype)
-        if x.dim() <= 2:
-            return out
-        return out.reshape(x.shape)
+        return reference_output(out, x, self.hidden_size)
 
     def _forward_impl(self, x: torch.Tensor, residual: Optional[torch.Tensor], norm):
         x2 = self._prep(x)

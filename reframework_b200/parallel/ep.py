@@ -44,7 +44,7 @@ from .. import kernels as K
 from .. import _lib as _lib_mod
 from .._lib import ACTIVATIONS, RfMoeError, check, dtype_code, lib, stream_of
 from ..moe.keys import expert_tensor
-from ..moe.moe_layer import FusedMoE, _bank_view, adjacent_router_weights
+from ..moe.moe_layer import FusedMoE, _bank_view, adjacent_router_weights, reference_output
 from . import dist as _dist
 from .eplb import Placement, place_experts, split_rows
 
@@ -360,9 +360,7 @@ class EPFusedMoE(nn.Module):
             hi = T * (self.ep_rank + 1) // self.ep_size
             part = self._forward_shard(x2[lo:hi], None if res2 is None else res2[lo:hi])
             out = self._all_gather_rows(part, T)
-        if out.dtype != x.dtype:
-            out = out.to(x.dtype)
-        return out if x.dim() <= 2 else out.reshape(x.shape)
+        return reference_output(out, x, self.hidden_size)
 
     def _all_gather_rows(self, part: torch.Tensor, T: int) -> torch.Tensor:
         R = self.ep_size

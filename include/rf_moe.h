@@ -36,6 +36,16 @@
  *   rf_moe_combine_rmsnorm  the same + the next RMSNorm (norm.py:27-53)
  *   rf_moe_ep_push_rows / rf_moe_ep_wait  reframework/parallel/dist.py:194-206
  *                           (EP dispatch / return all-to-all) as NVLink stores
+ *   rf_moe_ep_plan / rf_moe_ep_pair_rows  the split of that exchange, replacing
+ *                           the replicate-and-all-reduce forward of
+ *                           reframework/parallel/ep.py:119-150
+ *   rf_moe_ep_devplan, rf_moe_ep_devplan_host, _push, _regroup  the same plan
+ *                           and exchange driven from the GPU (no host sync)
+ *   rf_moe_ep_devplan_down_return  reframework/moe/fused.py:83 on the expert's
+ *                           rank + the return all-to-all (dist.py:194-206) in
+ *                           one kernel
+ *   rf_moe_peer_alloc / _open / _close / _free  buffers mapped by every peer
+ *                           (no reference counterpart)
  */
 #ifndef RF_MOE_H
 #define RF_MOE_H

@@ -44,6 +44,10 @@ __all__ = [
     "dense_mlp",
     "moe_forward",
     "forward_streaming",
+    "sym_int8_quantize",
+    "masked_experts",
+    "int8_experts",
+    "split_forward",
     "shard_range",
 ]
 
@@ -242,6 +246,123 @@ def forward_streaming(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
                              loc_ids[valid].unsqueeze(-1), activation)
         out.index_add_(0, t_idx[valid], part.to(torch.float32))
     return out.to(x.dtype)
+
+
+def sym_int8_quantize(w: torch.Tensor) -> Tuple[torch.Tensor, float]:
+    """Symmetric per-tensor int8 — reframework/moe/offload_cache.py:58-72:
+    scale = max|w| / 127 (fp32), codes = round(w / scale) clamped to +-127;
+    an all-zero tensor gets scale 1.0 and zero codes."""
+    amax = w.abs().max().float()
+    if amax <= 0:
+        return torch.zeros_like(w, dtype=torch.int8), 1.0
+    scale = amax / 127.0
+    wq = (w.float() / scale).round().clamp(-127, 127).to(torch.int8).contiguous()
+    return wq, float(scale)
+
+
+def masked_experts(hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                   topk_weights: torch.Tensor, topk_ids: torch.Tensor, active: torch.Tensor,
+                   activation: str = "silu") -> torch.Tensor:
+    """The GPU half of the CPU/GPU split — reframework/moe/fused.py:89-137:
+    ``fused_experts`` over the slots with ``active`` set only (``topk_ids``
+    local rows of ``w1``/``w2``).  Slot (t, k) belongs to token t; the
+    reference's ``arange(M).repeat(K)`` (fused.py:118) maps it to token
+    (t*K + k) % M instead, which differs for K > 1, so this restatement uses
+    ``repeat_interleave`` (the two agree for K = 1)."""
+    M, H = hidden_states.shape
+    K = topk_ids.shape[1]
+    E = w1.shape[0]
+    out = torch.zeros((M, H), dtype=hidden_states.dtype)
+    flat_expert = topk_ids.reshape(-1)
+    flat_weight = topk_weights.reshape(-1)
+    flat_active = active.reshape(-1)
+    flat_token = torch.arange(M).repeat_interleave(K)
+    active_ids = torch.where(flat_active, flat_expert, torch.full_like(flat_expert, -1))
+    counts = torch.bincount(active_ids[flat_active], minlength=E)
+    for e in torch.nonzero(counts, as_tuple=False).flatten().tolist():
+        sel = (flat_expert == e) & flat_active
+        tok = flat_token[sel]
+        w = flat_weight[sel].to(hidden_states.dtype)
+        x = hidden_states[tok]
+        gu = x.to(w1.dtype) @ w1[e].t()
+        inter = gated_act_and_mul(activation, gu)
+        y = inter @ w2[e].t()
+        y = y * w.unsqueeze(-1)
+        out.index_add_(0, tok, y)
+    return out
+
+
+def int8_experts(hidden_states: torch.Tensor, w1q: torch.Tensor, w2q: torch.Tensor, scales1: torch.Tensor,
+                 scales2: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                 active: torch.Tensor, activation: str = "silu") -> torch.Tensor:
+    """The int8 half of the CPU/GPU split — reframework/moe/fused.py:140-197
+    (same token mapping fix as ``masked_experts``).  Per active expert e
+    (ascending): its rows in fp32 quantized to int8 with one scale for the
+    whole block, ``int8 x int8 -> int32`` GEMM against ``w1q[e]``, dequantized
+    by ``block scale * scales1[e]``, gated activation in fp32, the result
+    quantized again per block, a second int8 GEMM against ``w2q[e]``,
+    dequantized, scaled by the fp32 routing weight and ``index_add_``-ed into an
+    fp32 output."""
+    M, H = hidden_states.shape
+    K = topk_ids.shape[1]
+    E = w1q.shape[0]
+    x2 = hidden_states.float()
+    out = torch.zeros((M, H), dtype=torch.float32)
+    flat_expert = topk_ids.reshape(-1)
+    flat_weight = topk_weights.float().reshape(-1)
+    flat_active = active.reshape(-1)
+    flat_token = torch.arange(M).repeat_interleave(K)
+    active_ids = torch.where(flat_active, flat_expert, torch.full_like(flat_expert, -1))
+    counts = torch.bincount(active_ids[flat_active], minlength=E)
+    for e in torch.nonzero(counts, as_tuple=False).flatten().tolist():
+        sel = (flat_expert == e) & flat_active
+        tok = flat_token[sel]
+        w = flat_weight[sel]
+        x = x2[tok]
+        xq, xs = sym_int8_quantize(x)
+        gu = torch._int_mm(xq, w1q[e].t().contiguous()).float() * (xs * float(scales1[e]))
+        inter = gated_act_and_mul(activation, gu)
+        iq, iscale = sym_int8_quantize(inter)
+        y = torch._int_mm(iq, w2q[e].t().contiguous()).float() * (iscale * float(scales2[e]))
+        y = y * w.unsqueeze(-1)
+        out.index_add_(0, tok, y)
+    return out
+
+
+def split_forward(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_weights: torch.Tensor,
+                  topk_ids: torch.Tensor, resident, activation: str = "silu") -> Dict[str, torch.Tensor]:
+    """One step of the CPU/GPU split forward — reframework/moe/moe_layer.py:523-627
+    with the host int8 bank of offload_cache.py:386-434.  The routed experts
+    resident before the step ("hits", ascending) run in the layer dtype
+    (``masked_experts``); the others ("misses", ascending) run on their int8
+    copies (``int8_experts``); out = (hits.float() + misses).to(x.dtype).
+    Every miss is computed (the reference packs at most RE_MAX_PACK of them,
+    offload_cache.py:417-421)."""
+    E = w1.shape[0]
+    routed = sorted(set(int(i) for i in topk_ids.reshape(-1).tolist()))
+    hits = [e for e in routed if e in resident]
+    misses = [e for e in routed if e not in resident]
+    out = torch.zeros(x.shape, dtype=x.dtype)
+    if hits:
+        remap = torch.full((E,), -1, dtype=torch.long)
+        for k, e in enumerate(hits):
+            remap[e] = k
+        loc = remap[topk_ids]
+        out = masked_experts(x, w1[hits], w2[hits], topk_weights, loc.clamp_min(0), loc >= 0, activation)
+    half = torch.zeros(x.shape, dtype=torch.float32)
+    if misses:
+        remap = torch.full((E,), -1, dtype=torch.long)
+        for k, e in enumerate(misses):
+            remap[e] = k
+        loc = remap[topk_ids]
+        q = [sym_int8_quantize(w1[e]) for e in misses], [sym_int8_quantize(w2[e]) for e in misses]
+        w1q = torch.stack([a for a, _ in q[0]])
+        w2q = torch.stack([a for a, _ in q[1]])
+        s1 = torch.tensor([b for _, b in q[0]], dtype=torch.float32)
+        s2 = torch.tensor([b for _, b in q[1]], dtype=torch.float32)
+        half = int8_experts(x, w1q, w2q, s1, s2, topk_weights, loc.clamp_min(0), loc >= 0, activation)
+    return {"out": (out.float() + half).to(x.dtype), "hits": hits, "misses": misses, "gpu_half": out,
+            "int8_half": half}
 
 
 def shard_range(num_experts: int, ep_size: int, ep_rank: int) -> Tuple[int, int]:

@@ -20,6 +20,10 @@ Reference code paths used (paths relative to the reference root):
   * ``MLP`` (shared experts)             reframework/layers/mlp.py:19-65
   * ``EPFusedMoE`` over 2 gloo ranks     reframework/parallel/ep.py:58-150,
                                          reframework/parallel/dist.py:135-176
+  * ``FusedMoE._forward_split``          reframework/moe/moe_layer.py:523-627 with the
+    int8 host bank (offload_cache.py:386-434, fused.py:89-197), at top-1 routing
+    (where the reference's slot-to-token mapping is right) and RE_MAX_PACK=8 (so
+    every miss is packed)
 Where the benchmark configuration asks for an fp32 router with a bias (which
 the reference's ``route`` cannot express), the case routes with
 ``softmax(x.float() @ gate.float().T + bias)`` through the reference's own
@@ -63,6 +67,8 @@ def golden_cases():
                                      router_fp32=False, seed=6), "entropy"),
         ("ep2_mini_bf16", MoEConfig("ep2_mini_bf16", 256, 8, 2, 256, 64, torch.bfloat16,
                                     router_fp32=False, seed=7), "ep2"),
+        ("int8_split_k1", mini(c["c5_mixtral22b_offload"], hidden=256, inter=256, tokens=96, steps=4,
+                               top_k=1, seed=9, name="int8_split_k1"), "split"),
     ]
 
 
@@ -176,6 +182,28 @@ def run_case(name: str, cfg: MoEConfig, mode: str):
         finally:
             del os.environ["RE_CHUNK_SIZE"]
         rec.update(ids=torch.stack(idss), weights=torch.stack(wss), out=torch.stack(outs),
+                   cache_stats=moe._cache.stats.as_dict())
+        spy = None
+    elif mode == "split":
+        moe = _build_layer(FusedMoE, cfg, d)
+        moe.build_offload_cache(torch.device("cpu"), lru_capacity=4)
+        moe.enable_cpu_split()
+        os.environ["RE_MAX_PACK"] = "8"
+        outs, idss, wss, res = [], [], [], []
+        try:
+            for s in range(cfg.steps):
+                logits = x.float() @ d["gate"].float().t() + d["bias"][s]
+                w, ids = torch_fused_topk(logits, cfg.top_k, cfg.renormalize)
+                res.append(torch.tensor(sorted(moe._cache._lru.keys()), dtype=torch.long))
+                with torch.no_grad():
+                    o = moe._forward_split(x, x, w, ids)
+                outs.append(o)
+                idss.append(ids)
+                wss.append(w)
+        finally:
+            del os.environ["RE_MAX_PACK"]
+        rec.update(ids=torch.stack(idss), weights=torch.stack(wss), out=torch.stack(outs), resident_before=res,
+                   resident_after=torch.tensor(sorted(moe._cache._lru.keys()), dtype=torch.long),
                    cache_stats=moe._cache.stats.as_dict())
         spy = None
     elif mode == "ep2":

@@ -68,6 +68,36 @@ def test_oracle_streaming_matches_reference():
         assert torch.equal(out, rec["out"][s]), max_rel(out, rec["out"][s])
 
 
+def test_oracle_split_matches_reference():
+    """The CPU/GPU split (hits in bf16, misses on int8 copies) step by step
+    against the reference's own _forward_split, given the experts resident
+    before each step; bit for bit."""
+    rec = load_golden("int8_split_k1")
+    cfg = golden_config(rec)
+    d = generate(cfg)
+    for s in range(cfg.steps):
+        w, ids = O.route(d["x"], d["gate"], cfg.top_k, cfg.renormalize, bias=d["bias"][s])
+        assert torch.equal(ids, rec["ids"][s])
+        res = O.split_forward(d["x"], d["w1"], d["w2"], w, ids, set(rec["resident_before"][s].tolist()))
+        assert torch.equal(res["out"], rec["out"][s]), (s, max_rel(res["out"], rec["out"][s]))
+    assert any(rec["resident_before"][s].numel() for s in range(cfg.steps)), "some step has hits"
+
+
+def test_oracle_int8_quantizer_and_gemm_are_exact():
+    """sym_int8_quantize round-trips within half a step, and the int8 GEMM is
+    exact integer arithmetic (the part of the int8 half a GPU reproduces bit
+    for bit)."""
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(64, 96, generator=g)
+    q, sc = O.sym_int8_quantize(w)
+    assert q.dtype == torch.int8 and int(q.abs().max()) == 127
+    assert float((q.float() * sc - w).abs().max()) <= sc / 2 + 1e-7
+    z, sz = O.sym_int8_quantize(torch.zeros(3, 4))
+    assert sz == 1.0 and not z.any()
+    a = torch.randint(-127, 128, (17, 96), generator=g, dtype=torch.int8)
+    assert torch.equal(torch._int_mm(a, q.t().contiguous()), a.int() @ q.int().t())
+
+
 def test_oracle_ep_sum_matches_reference_ep():
     """The reference EP (replicate tokens, mask, all-reduce over 2 gloo ranks)
     equals the single-process layer up to fp summation order; the oracle's

@@ -130,6 +130,18 @@ class Prediction:
         return out
 
 
+def sym_int8_quantize(w: torch.Tensor) -> Tuple[torch.Tensor, float]:
+    """Symmetric per-tensor int8 (offload_cache.py:58-72): scale = max|w| / 127
+    in fp32, codes = round(w / scale) clamped to +-127; an all-zero tensor gets
+    scale 1.0.  Runs once per expert when the split is armed (host setup)."""
+    amax = w.detach().abs().max().float()
+    if amax <= 0:
+        return torch.zeros_like(w, dtype=torch.int8), 1.0
+    scale = amax / 127.0
+    wq = (w.detach().float() / scale).round().clamp(-127, 127).to(torch.int8).contiguous()
+    return wq, float(scale)
+
+
 def _pin(t: torch.Tensor) -> Tuple[torch.Tensor, bool]:
     if not torch.cuda.is_available():
         return t, False
@@ -166,6 +178,19 @@ class ExpertOffloadCache:
     _slot_free_evt: List[Optional[object]] = field(default_factory=list, repr=False, compare=False)
     _copy_stream: Optional[object] = field(default=None, repr=False, compare=False)
     h2d_seconds: float = field(default=0.0, repr=False, compare=False)
+    # expert split: int8 copies of the host pool (one pinned buffer), their
+    # scales [E, 2] (host and device) and a device pool the step's misses are
+    # staged in
+    _cpu_split: bool = field(default=False, repr=False, compare=False)
+    _int8_host: List[Tuple[torch.Tensor, torch.Tensor, float, float]] = field(default_factory=list, repr=False,
+                                                                               compare=False)
+    _int8_buf: Optional[torch.Tensor] = field(default=None, repr=False, compare=False)
+    _int8_scales: Optional[torch.Tensor] = field(default=None, repr=False, compare=False)
+    _int8_scales_dev: Optional[torch.Tensor] = field(default=None, repr=False, compare=False)
+    pool_q1: Optional[torch.Tensor] = field(default=None, repr=False, compare=False)
+    pool_q2: Optional[torch.Tensor] = field(default=None, repr=False, compare=False)
+    _int8_free_evt: Optional[object] = field(default=None, repr=False, compare=False)
+    int8_transfer_bytes: int = field(default=0, repr=False, compare=False)  # outside OffloadStats (reference keys)
 
     def __post_init__(self) -> None:
         self.device = torch.device(self.device)
@@ -244,7 +269,8 @@ class ExpertOffloadCache:
 
     @property
     def cpu_split(self) -> bool:
-        return False
+        """True once the int8 copies are built and the split is armed."""
+        return self._cpu_split
 
     def copy_stream(self):
         if self._copy_stream is None and self._cuda:
@@ -460,6 +486,127 @@ class ExpertOffloadCache:
     def _pack(self, uniq: Sequence[int]) -> Tuple[torch.Tensor, torch.Tensor, Dict[int, int]]:
         self.wait_ready(uniq)
         return self.pool_w1, self.pool_w2, {i: self._lru[i] for i in uniq}
+
+    # ------------------------------------------------------------ expert split
+    def quantize_int8_host(self) -> None:
+        """Per-expert symmetric int8 copies of the host pool for the expert
+        split (offload_cache.py:386-408), in one pinned buffer (half the bytes
+        of a 16-bit pool): a step's non-resident experts cross PCIe as int8."""
+        if not self._host:
+            return
+        n = sum(w1.numel() + w2.numel() for w1, w2 in self._host)
+        buf = None
+        if self._cuda and torch.cuda.is_available():
+            try:
+                buf = torch.empty(n, dtype=torch.int8, pin_memory=True)
+            except RuntimeError:
+                buf = None
+        if buf is None:
+            buf = torch.empty(n, dtype=torch.int8)
+        scales = torch.empty(len(self._host), 2, dtype=torch.float32)
+        self._int8_host = []
+        off = 0
+        for i, (w1, w2) in enumerate(self._host):
+            q1, s1 = sym_int8_quantize(w1)
+            q2, s2 = sym_int8_quantize(w2)
+            v1 = buf[off:off + q1.numel()].view(tuple(q1.shape))
+            v1.copy_(q1)
+            off += q1.numel()
+            v2 = buf[off:off + q2.numel()].view(tuple(q2.shape))
+            v2.copy_(q2)
+            off += q2.numel()
+            self._int8_host.append((v1, v2, s1, s2))
+            scales[i, 0], scales[i, 1] = s1, s2
+        self._int8_buf = buf
+        self._int8_scales = scales
+        self._int8_scales_dev = scales.to(self.device)
+        self._cpu_split = True
+        logger.info("expert split: int8 copies of %d experts (symmetric per-tensor)", len(self._int8_host))
+
+    def split_prefetch(self, indices: Sequence[int]) -> Tuple[Tuple[torch.Tensor, torch.Tensor, Dict[int, int]],
+                                                               List[int]]:
+        """Dispatch the routed set by residency (offload_cache.py:509-552):
+        ``((pool_w1, pool_w2, {hit: slot}), misses)``, both ascending; hits
+        count as hits and move to the LRU's recent end; misses are not loaded
+        here (``reactive_load`` brings them resident after the step)."""
+        uniq = sorted(set(int(i) for i in indices if int(i) >= 0))
+        hits = [i for i in uniq if i in self._lru]
+        misses = [i for i in uniq if i not in self._lru]
+        for i in hits:
+            self._lru.move_to_end(i)
+            self.stats.hits += 1
+        return self._pack(hits), misses
+
+    def cpu_banks(self, indices: Sequence[int]) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                                          Dict[int, int]]:
+        """The int8 copies of ``indices`` (ascending) on the host:
+        ``(w1q [N,2I,H], w2q [N,H,I], scales1 [N], scales2 [N], {id: row})``
+        (offload_cache.py:410-434; every index is packed)."""
+        uniq = sorted(set(int(i) for i in indices))
+        local = {e: k for k, e in enumerate(uniq)}
+        if not uniq:
+            w1, w2 = self._host[0]
+            return (torch.empty((0,) + tuple(w1.shape), dtype=torch.int8),
+                    torch.empty((0,) + tuple(w2.shape), dtype=torch.int8),
+                    torch.empty(0), torch.empty(0), local)
+        return (torch.stack([self._int8_host[e][0] for e in uniq]), torch.stack([self._int8_host[e][1] for e in uniq]),
+                self._int8_scales[uniq, 0].clone(), self._int8_scales[uniq, 1].clone(), local)
+
+    def int8_banks(self, indices: Sequence[int]) -> Tuple[torch.Tensor, torch.Tensor, Dict[int, int]]:
+        """Stage the int8 copies of ``indices`` in the device int8 pool (one
+        H2D copy per matrix on the copy stream, after the previous step's int8
+        GEMMs released the pool; the current stream waits for the copies).
+        Returns ``(pool_q1, pool_q2, {id: pool row})``; the scales of every
+        expert are ``_int8_scales_dev`` [E, 2]."""
+        uniq = sorted(set(int(i) for i in indices))
+        if not uniq:
+            return self.pool_q1, self.pool_q2, {}
+        w1, w2 = self._int8_host[0][0], self._int8_host[0][1]
+        if self.pool_q1 is None or self.pool_q1.shape[0] < len(uniq):
+            if self._cuda and self._int8_free_evt is not None:
+                torch.cuda.current_stream(self.device).wait_event(self._int8_free_evt)
+            self.pool_q1 = torch.empty((len(uniq),) + tuple(w1.shape), dtype=torch.int8, device=self.device)
+            self.pool_q2 = torch.empty((len(uniq),) + tuple(w2.shape), dtype=torch.int8, device=self.device)
+            self._int8_free_evt = None
+        pinned = self._int8_buf is not None and self._int8_buf.is_pinned()
+        if self._cuda:
+            cs = self.copy_stream()
+            with torch.cuda.stream(cs):
+                if self._int8_free_evt is not None:
+                    cs.wait_event(self._int8_free_evt)
+                for k, e in enumerate(uniq):
+                    self.pool_q1[k].copy_(self._int8_host[e][0], non_blocking=pinned)
+                    self.pool_q2[k].copy_(self._int8_host[e][1], non_blocking=pinned)
+                ready = torch.cuda.Event()
+                ready.record(cs)
+            torch.cuda.current_stream(self.device).wait_event(ready)
+        else:
+            for k, e in enumerate(uniq):
+                self.pool_q1[k].copy_(self._int8_host[e][0])
+                self.pool_q2[k].copy_(self._int8_host[e][1])
+        self.int8_transfer_bytes += sum(self._int8_host[e][0].numel() + self._int8_host[e][1].numel()
+                                        for e in uniq)
+        return self.pool_q1, self.pool_q2, {e: k for k, e in enumerate(uniq)}
+
+    def int8_release(self) -> None:
+        """The int8 pool may be overwritten once the work queued so far has run."""
+        if self._cuda:
+            evt = torch.cuda.Event()
+            evt.record(torch.cuda.current_stream(self.device))
+            self._int8_free_evt = evt
+
+    def reactive_load(self, indices: Sequence[int]) -> None:
+        """Bring this step's misses resident for the next step
+        (offload_cache.py:554-567): every miss is loaded (no substitution) with
+        all of them protected, then the LRU is trimmed with the next-step
+        reserve as the soft tier."""
+        uniq = sorted(set(int(i) for i in indices))
+        hard = set(uniq)
+        soft = set(self._next_reserve) - hard
+        for i in uniq:
+            if i not in self._lru:
+                self._fill(i, hard, soft)
+        self._evict(uniq, soft)
 
     def slot_table(self) -> torch.Tensor:
         """int32 [E] expert -> slot (-1 when not resident), on the device."""

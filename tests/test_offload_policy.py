@@ -287,3 +287,52 @@ def test_stats_as_dict_keys():
     d = cache.stats.as_dict()
     assert set(d) == {"hits", "misses", "evictions", "subs", "predicts", "inflight_bytes", "transfer_mb"}
     assert "hit=" in cache.report()
+
+
+# ------------------------------------------------------------- expert split
+def test_split_residency_and_stats_follow_the_reference():
+    """split_prefetch + reactive_load over the steps of the reference's own
+    split run (golden fixture): the experts resident before every step, the
+    final residency and the hit / miss / eviction / transfer counters agree."""
+    from conftest import golden_config, load_golden
+    from reframework_b200.workloads import generate
+    rec = load_golden("int8_split_k1")
+    cfg = golden_config(rec)
+    d = generate(cfg)
+    cache = ExpertOffloadCache(device=torch.device("cpu"), lru_capacity=4, dtype=cfg.dtype)
+    cache.load([{"w1": d["w1"][e], "w2": d["w2"][e]} for e in range(cfg.experts)])
+    cache.quantize_int8_host()
+    assert cache.cpu_split
+    for s in range(cfg.steps):
+        assert sorted(cache._lru) == rec["resident_before"][s].tolist(), f"step {s}"
+        (_, _, hit_slots), misses = cache.split_prefetch(rec["ids"][s].reshape(-1).tolist())
+        routed = sorted(set(rec["ids"][s].reshape(-1).tolist()))
+        assert sorted(hit_slots) == [e for e in routed if e in rec["resident_before"][s].tolist()]
+        assert misses == [e for e in routed if e not in hit_slots]
+        cache.reactive_load(misses)
+    assert sorted(cache._lru) == rec["resident_after"].tolist()
+    st, ref = cache.stats.as_dict(), rec["cache_stats"]
+    for k in ("hits", "misses", "evictions", "subs", "transfer_mb"):
+        assert st[k] == ref[k], (k, st[k], ref[k])
+
+
+def test_int8_copies_match_the_reference_quantizer():
+    """quantize_int8_host / cpu_banks give the codes and scales of the
+    reference's symmetric per-tensor quantizer (restated in the oracle)."""
+    from oracle import moe_oracle as O
+    g = torch.Generator().manual_seed(3)
+    cache = ExpertOffloadCache(device=torch.device("cpu"), lru_capacity=2, dtype=torch.bfloat16)
+    ex = [{"w1": (torch.randn(12, 8, generator=g) * 0.02).bfloat16(), "w2": (torch.randn(8, 6, generator=g) * 0.02).bfloat16()}
+          for _ in range(3)]
+    ex[1]["w2"].zero_()
+    cache.load(ex)
+    cache.quantize_int8_host()
+    w1q, w2q, s1, s2, local = cache.cpu_banks([2, 0, 1])
+    assert local == {0: 0, 1: 1, 2: 2}
+    for k, e in enumerate([0, 1, 2]):
+        q1, r1 = O.sym_int8_quantize(ex[e]["w1"])
+        q2, r2 = O.sym_int8_quantize(ex[e]["w2"])
+        assert torch.equal(w1q[k], q1) and torch.equal(w2q[k], q2)
+        assert float(s1[k]) == torch.tensor(r1, dtype=torch.float32).item()
+        assert float(s2[k]) == torch.tensor(r2, dtype=torch.float32).item()
+    assert float(s2[1]) == 1.0 and not w2q[1].any()  # an all-zero matrix: scale 1, zero codes

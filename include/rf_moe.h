@@ -46,6 +46,10 @@
  *                           one kernel
  *   rf_moe_peer_alloc / _open / _close / _free  buffers mapped by every peer
  *                           (no reference counterpart)
+ *   rf_moe_int8_quantize, rf_moe_int8_grouped_gemm, rf_moe_split_combine
+ *                           the int8 half of the CPU/GPU expert split
+ *                           (reframework/moe/fused.py:89-197,
+ *                           moe_layer.py:523-627, offload_cache.py:58-72)
  */
 #ifndef RF_MOE_H
 #define RF_MOE_H
@@ -396,6 +400,39 @@ int rf_moe_ep_devplan_down_return(const void *workspace, int32_t R, int32_t E, i
                                   const void *h, const void *w2, int64_t rows_capacity, int64_t H, int64_t I,
                                   int32_t dtype, void *const *dst, int32_t *const *flag, int32_t epoch,
                                   uint32_t *done, rf_stream_t stream);
+
+/*
+ * Expert split, int8 half (fused.py:140-197 with slot (t, k) -> token t;
+ * offload_cache.py:58-72 for the quantizer).  The listed experts (groups[n],
+ * expert ids) own rows [offsets[e], offsets[e] + counts[e]) of the permuted
+ * layout.
+ *   rf_moe_int8_quantize  per listed expert: scale = max|src| / 127 over its
+ *       rows (fp32; 1 when that max is <= 0), q = round-half-even(src / scale)
+ *       clamped to +-127; scales[n] receive the scales.  compute_amax = 0
+ *       takes amax[n] as given (the gated GEMM's max|inter|).
+ *   rf_moe_int8_grouped_gemm  exact int32 sums of a[rows] . w[slot[e]]^T
+ *       (w int8 [num_slots, gated ? 2N : N, Kdim], Kdim % 16 == 0), scaled by
+ *       a_scales[i] * w_scales[e * w_scale_stride] in fp32.  gated: out[r, n] =
+ *       act(g) * u in fp32 with g / u the first / second N rows' sums, and
+ *       amax_out[i] = max|out| over the expert's rows.  down: out[r, n] =
+ *       scaled sum * row_weights[src_slot[r]].
+ *   rf_moe_split_combine  out[t] = round(float(sum over the token's resident
+ *       experts of round(y_hit * round(w)), accumulated in the layer dtype) +
+ *       sum over its int8 experts of y_int8 (fp32)), both in ascending expert
+ *       order; is_miss[E] marks the int8 experts, ids [T*K] the slot experts.
+ */
+int rf_moe_int8_quantize(const void *src, int32_t src_dtype, const int32_t *offsets, const int32_t *counts,
+                         const int32_t *groups, int32_t n_groups, int32_t E, int64_t rows_capacity, int64_t cols,
+                         float *amax, int32_t compute_amax, float *scales, int8_t *q, rf_stream_t stream);
+int rf_moe_int8_grouped_gemm(const int8_t *a, const int8_t *w, const int32_t *offsets, const int32_t *counts,
+                             const int32_t *groups, const int32_t *slot, int32_t n_groups, int32_t E,
+                             int32_t num_slots, int64_t rows_capacity, int64_t Kdim, int64_t N,
+                             const float *a_scales, const float *w_scales, int64_t w_scale_stride, int32_t gated,
+                             int32_t act, float *out, float *amax_out, const float *row_weights,
+                             const int32_t *src_slot, rf_stream_t stream);
+int rf_moe_split_combine(const void *y_hit, const float *y_int8, const int32_t *row_of_slot, const int32_t *ids,
+                         const uint8_t *is_miss, const float *topk_weights, int64_t T, int32_t K, int64_t H,
+                         int32_t E, int32_t dtype, void *out, rf_stream_t stream);
 
 /* Summation modes of rf_moe_combine. */
 #define RF_COMBINE_REFERENCE 0  /* the reference's rounding points and order */

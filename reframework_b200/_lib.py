@@ -87,6 +87,14 @@ _SIGNATURES = {
                                                                                _i64, ctypes.c_int32, _c_void_p,
                                                                                _c_void_p, ctypes.c_int32, _c_void_p,
                                                                                _c_void_p]),
+    "rf_moe_int8_quantize": (_int, [_c_void_p, ctypes.c_int32, _c_void_p, _c_void_p, _c_void_p, ctypes.c_int32,
+                                     ctypes.c_int32, _i64, _i64, _c_void_p, ctypes.c_int32, _c_void_p, _c_void_p,
+                                     _c_void_p]),
+    "rf_moe_int8_grouped_gemm": (_int, [_c_void_p] * 6 + [ctypes.c_int32] * 3 + [_i64, _i64, _i64, _c_void_p,
+                                                                                 _c_void_p, _i64, ctypes.c_int32,
+                                                                                 ctypes.c_int32] + [_c_void_p] * 5),
+    "rf_moe_split_combine": (_int, [_c_void_p] * 6 + [_i64, ctypes.c_int32, _i64, ctypes.c_int32, ctypes.c_int32,
+                                                       _c_void_p, _c_void_p]),
     "rf_moe_ep_plan": (_int, [_c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_void_p, _c_void_p,
                               ctypes.c_int32, ctypes.c_int32, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
 }

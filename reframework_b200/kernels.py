@@ -279,3 +279,50 @@ def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, weights: to
         torch.cuda.current_stream(x.device).wait_event(before_combine)
     return combine(y, p.row_of_slot, weights, out, shared_y=shared_y, shared_scale=shared_scale,
                    residual=residual, precise=precise, norm=norm, norm_out=norm_out)
+
+
+# ------------------------------------------------------- expert split, int8 half
+def int8_quantize(src: torch.Tensor, offsets: torch.Tensor, counts: torch.Tensor, groups: torch.Tensor,
+                  q: torch.Tensor, scales: torch.Tensor, amax: torch.Tensor, *, compute_amax: bool = True) -> None:
+    """Per listed expert (``groups``), its rows of ``src`` [rows_cap, cols] to
+    int8 ``q`` with one symmetric scale (``scales``); ``amax`` [n] fp32 holds
+    (or, with ``compute_amax``, receives) each block's max|src|."""
+    dev = _require_cuda(src, offsets, counts, groups, q, scales, amax)
+    rc = lib().rf_moe_int8_quantize(ptr(src), dtype_code(src.dtype), ptr(offsets), ptr(counts), ptr(groups),
+                                    groups.numel(), counts.shape[0], src.shape[0], src.shape[1], ptr(amax),
+                                    1 if compute_amax else 0, ptr(scales), ptr(q), stream_of(dev))
+    check(rc, "rf_moe_int8_quantize")
+
+
+def int8_grouped_gemm(a: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor, counts: torch.Tensor,
+                      groups: torch.Tensor, slot: torch.Tensor, a_scales: torch.Tensor, w_scales: torch.Tensor,
+                      w_scale_stride: int, out: torch.Tensor, *, gated: bool, activation: str = "silu",
+                      amax_out: Optional[torch.Tensor] = None, row_weights: Optional[torch.Tensor] = None,
+                      src_slot: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Exact int8 grouped GEMM with the split's dequantizing epilogues
+    (gated: fp32 ``act(g) * u`` and max|.| per expert; down: fp32 rows times
+    the routing weight).  ``w_scales`` points at expert 0's scale, stride
+    ``w_scale_stride`` elements."""
+    dev = _require_cuda(a, w, offsets, counts, groups, slot, a_scales, w_scales, out, amax_out, row_weights, src_slot)
+    if activation not in _lib.ACTIVATIONS:
+        raise ValueError(f"unknown gated activation {activation!r}; known: {tuple(_lib.ACTIVATIONS)}")
+    rc = lib().rf_moe_int8_grouped_gemm(ptr(a), ptr(w), ptr(offsets), ptr(counts), ptr(groups), ptr(slot),
+                                        groups.numel(), counts.shape[0], w.shape[0], a.shape[0], a.shape[1],
+                                        out.shape[1], ptr(a_scales), ptr(w_scales), int(w_scale_stride),
+                                        1 if gated else 0, _lib.ACTIVATIONS[activation], ptr(out), ptr(amax_out),
+                                        ptr(row_weights), ptr(src_slot), stream_of(dev))
+    check(rc, "rf_moe_int8_grouped_gemm")
+    return out
+
+
+def split_combine(y_hit: torch.Tensor, y_int8: torch.Tensor, row_of_slot: torch.Tensor, ids32: torch.Tensor,
+                  is_miss: torch.Tensor, weights: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """Merge of the split's halves per token (rf_moe_split_combine)."""
+    dev = _require_cuda(y_hit, y_int8, row_of_slot, ids32, is_miss, weights, out)
+    T, K = weights.shape
+    wf = weights.float().contiguous()
+    rc = lib().rf_moe_split_combine(ptr(y_hit), ptr(y_int8), ptr(row_of_slot), ptr(ids32), ptr(is_miss), ptr(wf),
+                                    T, K, out.shape[1], is_miss.numel(), dtype_code(out.dtype), ptr(out),
+                                    stream_of(dev))
+    check(rc, "rf_moe_split_combine")
+    return out

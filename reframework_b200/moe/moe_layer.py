@@ -257,17 +257,21 @@ class FusedMoE(nn.Module):
         self._predictor = self._cache._predictor
 
     def enable_cpu_split(self) -> None:
-        """The reference's int8 CPU/GPU split (moe_layer.py:263-282) is not provided:
-        its token mapping is incorrect for K>1 (fused.py:118,175) and on B200 the
-        exact slot-streaming path replaces it.  Logged and ignored."""
-        logger.warning("FusedMoE.enable_cpu_split: not supported; the exact offload path is used")
+        """Arm the expert split (moe_layer.py:263-282): build the int8 copies of
+        the offloaded experts and, from the next forward on, compute every step's
+        non-resident experts on them (``_forward_split``).  No-op without an
+        offload cache."""
+        if self._cache is None:
+            return
+        self._cache.quantize_int8_host()
+        self._cpu_split_enabled = True
 
     def set_shuttle(self, shuttle: Optional[CpuShuttle]) -> None:
         self._shuttle = shuttle
 
     @property
     def cpu_split(self) -> bool:
-        return False
+        return self._cpu_split_enabled and self.uses_offload and self._cache.cpu_split
 
     @property
     def uses_offload(self) -> bool:
@@ -366,7 +370,12 @@ class FusedMoE(nn.Module):
         w, ids32, _, _, sscale = self._router(x2, ids32=True, ids64=False)
         if sb is not None and self.uses_offload:
             shared_y = K.dense_gated_mlp(x2, sb[0], sb[1], self.activation)
-        if self.uses_offload:
+        if self.cpu_split:
+            if shared_y is not None or res2 is not None or norm is not None:
+                raise RfMoeError("the expert split computes the routed experts only (no shared experts, "
+                                 "residual or fused norm)")
+            out = self._forward_split(x2, w, ids32)
+        elif self.uses_offload:
             out = self._forward_offload(x2, w, ids32, shared_y, sscale, res2, norm, normed)
         else:
             w1b, w2b = self._resident_banks()
@@ -436,6 +445,75 @@ class FusedMoE(nn.Module):
                   precise=self.precise_combine, norm=norm, norm_out=normed)
         if self._predictor is not None:
             self._predictor.record_step(active, is_prefill=(T > 1), forward_ms=self._since_last_step_ms(),
+                                        inflight_bytes=(self._shuttle.inflight_bytes()
+                                                        if self._shuttle is not None else 0.0))
+        return out
+
+    def _forward_split(self, x2, w, ids32):
+        """The CPU/GPU expert split (moe_layer.py:523-627), B200 form.
+
+        The routed experts resident in the device slots ("hits") run in the
+        layer dtype on the grouped tensor-core GEMMs; the others ("misses") run
+        on their int8 copies (fused.py:140-197), which cross PCIe at half the
+        bytes of the 16-bit weights and are computed on the GPU with exact int8
+        GEMMs; the halves meet in fp32 per token (rf_moe_split_combine).  The
+        misses are then loaded resident for the next step (``reactive_load``).
+        Every miss is computed (no RE_MAX_PACK cap) and slot (t, k) belongs to
+        token t (the reference's ``repeat(K)`` mapping, fused.py:118,175, is
+        wrong for K > 1).
+        """
+        cache = self._cache
+        dev = x2.device
+        T, H = x2.shape
+        E, I = self.num_experts, self.intermediate_size
+        p = K.permute(ids32, E, x=x2)
+        counts = p.counts.to("cpu").tolist()  # host sync: which experts this step routes to
+        routed = [e for e in range(E) if counts[e] > 0]
+        (pool_w1, pool_w2, hit_slots), misses = cache.split_prefetch(routed)
+        hits = sorted(hit_slots)
+        if self._shuttle is not None:
+            self._shuttle.send(x2)
+        y = torch.empty(p.rows_cap, H, dtype=x2.dtype, device=dev)
+        if hits:
+            slots = torch.full((E,), -1, dtype=torch.int32)
+            for e in hits:
+                slots[e] = hit_slots[e]
+            slot_t = slots.pin_memory().to(dev, non_blocking=True)
+            grp = torch.tensor(hits, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+            h = torch.empty(p.rows_cap, I, dtype=x2.dtype, device=dev)
+            K.grouped_gemm_gated(p.x_perm, pool_w1, p.offsets, p.counts, h, slot=slot_t, groups=grp,
+                                 activation=self.activation)
+            K.grouped_gemm_down(h, pool_w2, p.offsets, p.counts, y, slot=slot_t, groups=grp)
+        y8 = torch.empty(p.rows_cap, H, dtype=torch.float32, device=dev)
+        miss_mask = torch.zeros(E, dtype=torch.uint8)
+        if misses:
+            miss_mask[misses] = 1
+            q1, q2, rows8 = cache.int8_banks(misses)
+            n = len(misses)
+            slot8 = torch.full((E,), -1, dtype=torch.int32)
+            for e, k in rows8.items():
+                slot8[e] = k
+            slot8 = slot8.pin_memory().to(dev, non_blocking=True)
+            grp8 = torch.tensor(misses, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+            f32 = dict(dtype=torch.float32, device=dev)
+            xq = torch.empty(p.rows_cap, H, dtype=torch.int8, device=dev)
+            amax, xs = torch.empty(n, **f32), torch.empty(n, **f32)
+            K.int8_quantize(p.x_perm, p.offsets, p.counts, grp8, xq, xs, amax)
+            scales = cache._int8_scales_dev  # [E, 2]: w1, w2
+            inter = torch.empty(p.rows_cap, I, **f32)
+            amax2, iscale = torch.empty(n, **f32), torch.empty(n, **f32)
+            K.int8_grouped_gemm(xq, q1, p.offsets, p.counts, grp8, slot8, xs, scales[:, 0], 2, inter, gated=True,
+                                activation=self.activation, amax_out=amax2)
+            iq = torch.empty(p.rows_cap, I, dtype=torch.int8, device=dev)
+            K.int8_quantize(inter, p.offsets, p.counts, grp8, iq, iscale, amax2, compute_amax=False)
+            K.int8_grouped_gemm(iq, q2, p.offsets, p.counts, grp8, slot8, iscale, scales[:, 1], 2, y8, gated=False,
+                                row_weights=w.float().contiguous().reshape(-1), src_slot=p.src_slot)
+            cache.int8_release()
+        out = torch.empty(T, H, dtype=x2.dtype, device=dev)
+        K.split_combine(y, y8, p.row_of_slot, ids32, miss_mask.pin_memory().to(dev, non_blocking=True), w, out)
+        cache.reactive_load(misses)
+        if self._predictor is not None:
+            self._predictor.record_step(routed, is_prefill=(T > 1), forward_ms=self._since_last_step_ms(),
                                         inflight_bytes=(self._shuttle.inflight_bytes()
                                                         if self._shuttle is not None else 0.0))
         return out

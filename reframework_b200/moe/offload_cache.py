@@ -563,14 +563,15 @@ class ExpertOffloadCache:
             return self.pool_q1, self.pool_q2, {}
         w1, w2 = self._int8_host[0][0], self._int8_host[0][1]
         if self.pool_q1 is None or self.pool_q1.shape[0] < len(uniq):
-            if self._cuda and self._int8_free_evt is not None:
-                torch.cuda.current_stream(self.device).wait_event(self._int8_free_evt)
+            # a larger pool; its memory may be the old pool's, so the copies
+            # below still wait for the last release of the old one
             self.pool_q1 = torch.empty((len(uniq),) + tuple(w1.shape), dtype=torch.int8, device=self.device)
             self.pool_q2 = torch.empty((len(uniq),) + tuple(w2.shape), dtype=torch.int8, device=self.device)
-            self._int8_free_evt = None
         pinned = self._int8_buf is not None and self._int8_buf.is_pinned()
         if self._cuda:
             cs = self.copy_stream()
+            self.pool_q1.record_stream(cs)
+            self.pool_q2.record_stream(cs)
             with torch.cuda.stream(cs):
                 if self._int8_free_evt is not None:
                     cs.wait_event(self._int8_free_evt)

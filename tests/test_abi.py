@@ -90,6 +90,12 @@ def test_fused_gather_gemm_reports_unsupported_dtype():
     (lambda L: L.rf_moe_set_gemm_impl(5), "0 to 4"),
     (lambda L: L.rf_moe_combine_rmsnorm(None, None, None, 4, 2, 64, 2, None, None, None, 0, None, None, -1.0,
                                         None, None, None), "eps"),
+    (lambda L: L.rf_moe_int8_quantize(None, 9, None, None, None, 1, 4, 8, 64, None, 1, None, None, None), "dtype"),
+    (lambda L: L.rf_moe_int8_grouped_gemm(None, None, None, None, None, None, 1, 4, 4, 128, 8, 64, None, None, 1,
+                                          1, 0, None, None, None, None, None), "multiple of 16"),
+    (lambda L: L.rf_moe_int8_grouped_gemm(None, None, None, None, None, None, 1, 4, 4, 128, 64, 64, None, None, 1,
+                                          1, 7, None, None, None, None, None), "activation"),
+    (lambda L: L.rf_moe_split_combine(None, None, None, None, None, None, 4, 17, 64, 8, 2, None, None), "K <= 16"),
 ])
 def test_argument_validation(call, needle):
     lib = _lib.lib()

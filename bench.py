@@ -13,7 +13,8 @@ time = max over ranks.
 
 ``--impl reference`` times the CPU restatement of the reference's torch path
 (oracle/moe_oracle.py, the reference's per-call expert restack included) on
-the host cores over a bounded token sample per step.
+the host cores, one full 4096-token forward per step (the same workload as
+the GPU arm).
 """
 
 from __future__ import annotations
@@ -57,8 +58,11 @@ def sustained_bf16_peak():
     return 1400.0, "fallback"
 
 
+TRAFFIC_FILE = os.path.join("profiles", "traffic.json")
+
+
 def committed_traffic():
-    p = os.path.join(ROOT, "profiles", "traffic.json")
+    p = os.path.join(ROOT, TRAFFIC_FILE)
     if os.path.exists(p):
         try:
             return json.load(open(p))
@@ -295,8 +299,7 @@ def run_gpu(args):
                 stage_fn(layer, x, [torch.cuda.Event(enable_timing=True) for _ in range(nev)])
             else:
                 fwd(x)
-        clocks = Clocks(range(world), os.path.join(ROOT, "gpurun_out", "clocks_bench.csv")
-                        if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else None)
+        clocks = Clocks(range(world), args.clocks_out)
         if rank == 0:
             clocks.start()  # before the barrier: no rank may start timing while rank 0 sets up sampling
         barrier()
@@ -369,14 +372,22 @@ def run_gpu(args):
         flop_g = 2.0 * rows * cfg.hidden * 2 * cfg.inter
         flop_d = 2.0 * rows * cfg.inter * cfg.hidden
         ach = flop_g / (per["gemm_gated"] / 1e3) / 1e12
-        tr = committed_traffic().get("gemm_gated_bytes_per_launch")
+        trd = committed_traffic()
         sus, sus_src = sustained_bf16_peak()
-        res["roofline"] = {"kernel": "tc_grouped_gemm<bf16, gated> (K3)", "bound": "tensor",
-                           "achieved": ach, "peak": sus, "unit": "TFLOP/s", "frac": ach / sus,
-                           "peak_source": f"{sus_src} bf16 (sustained): K3 is timed inside back-to-back "
-                                          "layer steps, where the power cap sets the clock (see clocks.reasons)",
-                           "peak_burst": bf16_peak, "frac_burst": ach / bf16_peak, "traffic": tr,
-                           "algorithmic_flop_per_launch": flop_g}
+        sm_mhz = clk["sm_mhz"] if clk else None
+        res["roofline"] = {"kernel": trd.get("gemm_gated_kernel", "grouped gated GEMM (K3)"), "bound": "tensor",
+                           "achieved": ach, "peak": bf16_peak, "unit": "TFLOP/s", "frac": ach / bf16_peak,
+                           "peak_source": f"{src} bf16 burst (cuBLAS 8192^3, best of 10): K3 is a 1-2 ms "
+                                          "launch inside a sub-second timed region",
+                           "peak_sustained": sus, "frac_sustained": ach / sus,
+                           "traffic": trd.get("gemm_gated_bytes_per_launch"),
+                           "traffic_source": (f"{TRAFFIC_FILE}: dram__bytes_read.sum + dram__bytes_write.sum of "
+                                              "one K3 launch of this workload from a committed ncu capture, "
+                                              "not measured in this run") if trd else None,
+                           "algorithmic_flop_per_launch": flop_g,
+                           "k3_ms_x_sm_mhz": (per["gemm_gated"] * sm_mhz) if sm_mhz else None,
+                           "clock_note": "sm_mhz is NVML's reported clock sampled every 2 ms; ncu's "
+                                         "sm__cycles_elapsed.avg.per_second for K3 is in the profile summary"}
         tot_ms = per["gemm_gated"] + per["gemm_down"]
         res["gemms_tflops"] = (flop_g + flop_d) / (tot_ms / 1e3) / 1e12
         res["layer_tflops"] = cfg.flops / (ms / 1e3) / 1e12
@@ -419,8 +430,10 @@ def _cpu_layer_forward(x, gate, w1_list, w2_list, bias, top_k):
     return O.fused_experts(x, w1, w2, w, ids)
 
 
-def cpu_baseline(cfg, layer, budget_s=25.0, sample_tokens=1024):
-    """Time the oracle port of the reference layer on the host cores (rank 0, N=1)."""
+def cpu_baseline(cfg, layer, budget_s=25.0, sample_tokens=None):
+    """Time the oracle port of the reference layer on the host cores (rank 0, N=1):
+    full forwards of all the workload's tokens, as many as fit in the budget."""
+    sample_tokens = sample_tokens or cfg.tokens
     torch.set_num_threads(os.cpu_count())
     w1b, w2b = layer._resident_banks()
     w1 = [w.cpu() for w in w1b]
@@ -429,7 +442,7 @@ def cpu_baseline(cfg, layer, budget_s=25.0, sample_tokens=1024):
     bias = layer.router_bias.cpu() if layer.router_bias is not None else None
     g = torch.Generator().manual_seed(5)
     x = torch.randn(sample_tokens, cfg.hidden, generator=g).to(cfg.dtype)
-    _cpu_layer_forward(x[:64], gate, w1, w2, bias, cfg.top_k)  # warm-up (thread pool, allocator)
+    _cpu_layer_forward(x, gate, w1, w2, bias, cfg.top_k)  # warm-up (thread pool, allocator)
     times = []
     t_end = time.perf_counter() + budget_s
     while not times or (time.perf_counter() < t_end and len(times) < 5):
@@ -440,7 +453,8 @@ def cpu_baseline(cfg, layer, budget_s=25.0, sample_tokens=1024):
     info = _cpu_info()
     return {"value": sample_tokens / s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{sample_tokens} of the {cfg.tokens} tokens per call, {len(times)} timed calls "
-                      f"(median {s:.2f} s); restack + fp32 router + torch bf16 experts on the CPU",
+                      f"(median {s:.2f} s) after one warm-up call; restack + fp32 router + torch bf16 "
+                      "experts on the CPU",
             "cpu": info.get("cpu"), "amx": info.get("amx")}
 
 
@@ -457,7 +471,7 @@ def run_reference(args):
     w1 = list(d["w1"])
     w2 = list(d["w2"])
     bias = d["bias"][0] if d["bias"] is not None else None
-    sample = args.ref_tokens
+    sample = args.ref_tokens or cfg.tokens
     g = torch.Generator().manual_seed(6)
     x = torch.randn(sample, cfg.hidden, generator=g).to(cfg.dtype)
     for _ in range(args.warmup):
@@ -476,10 +490,11 @@ def run_reference(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
         "config": {"workload": cfg.name, "hidden": cfg.hidden, "experts": cfg.experts, "top_k": cfg.top_k,
                    "inter": cfg.inter, "tokens_per_gpu": cfg.tokens, "sample_tokens_per_step": sample,
-                   "parallelism": "cpu"},
+                   "same_config": sample == cfg.tokens, "parallelism": "cpu"},
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": f"{sample} tokens per step (of {cfg.tokens}), reference restack + "
-                                   "fp32 router + per-expert torch bf16 GEMMs",
+                         "sample": f"{sample} tokens per step (of {cfg.tokens}), {args.steps} timed steps after "
+                                   f"{args.warmup} warm-up; reference restack + fp32 router + per-expert "
+                                   "torch bf16 GEMMs",
                          "cpu": info.get("cpu"), "amx": info.get("amx")},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -566,10 +581,10 @@ def run_generic(args):
         "roofline": ({"bound": "hbm", "achieved": hbm_ach, "peak": hbm_peak, "unit": "GB/s",
                       "frac": hbm_ach / hbm_peak, "peak_source": src,
                       "algorithmic_bytes": weight_bytes + act_bytes} if hbm_bound else
-                     {"bound": "tensor", "achieved": tf_ach, "peak": sustained_bf16_peak()[0], "unit": "TFLOP/s",
-                      "frac": tf_ach / sustained_bf16_peak()[0],
-                      "peak_source": f"{sustained_bf16_peak()[1]} bf16 (sustained): whole layer steps back to back",
-                      "peak_burst": bf16_peak, "frac_burst": tf_ach / bf16_peak}),
+                     {"bound": "tensor", "achieved": tf_ach, "peak": bf16_peak, "unit": "TFLOP/s",
+                      "frac": tf_ach / bf16_peak, "peak_source": f"{src} bf16 burst (cuBLAS 8192^3, best of 10)",
+                      "peak_sustained": sustained_bf16_peak()[0],
+                      "frac_sustained": tf_ach / sustained_bf16_peak()[0]}),
         "clocks": clk,
     }
     print(json.dumps(res))
@@ -654,7 +669,10 @@ def main():
     ap.add_argument("--config", default="c2_mixtral_bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=25.0)
-    ap.add_argument("--ref-tokens", type=int, default=512)
+    ap.add_argument("--ref-tokens", type=int, default=0,
+                    help="reference arm: tokens per step (0 = the workload's full token count)")
+    ap.add_argument("--clocks-out", default=None,
+                    help="CSV of the NVML clock samples (default: a temporary file)")
     ap.add_argument("--redundant", type=int, default=2,
                     help="EP: replica expert slots per rank for load balancing (0 = contiguous shards only)")
     ap.add_argument("--slots", type=int, default=4, help="offload workload: device expert slots")

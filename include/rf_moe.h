@@ -31,6 +31,8 @@
  *   rf_moe_grouped_gemm_gated_gather  the same with fused.py:80 (hidden_states[tok])
  *                           folded into the operand load
  *   rf_moe_grouped_gemm_down   reframework/moe/fused.py:83 (inter @ w2[e].t())
+ *   rf_moe_grouped_gemm_down_add  the same plus a rounded add: the shared
+ *                           experts' sum (reframework/layers/mlp.py:35-39 each)
  *   rf_moe_combine          reframework/moe/fused.py:84-86 (y * w, index_add_)
  *                           + reframework/layers/norm.py:43-53 (residual add, opt-in)
  *   rf_moe_combine_rmsnorm  the same + the next RMSNorm (norm.py:27-53)
@@ -183,7 +185,10 @@ int rf_moe_permute(const int32_t *topk_ids, int64_t T, int64_t K, int64_t E, int
  *
  * The first call on a device looks up the array's device address for that
  * device (cudaGetSymbolAddress, with that device current); make that first
- * call before any stream capture.  All calls share the one array, which keeps
+ * call before any stream capture.  The address is kept per device ordinal
+ * for the life of the process: it does not survive cudaDeviceReset (or any
+ * other teardown of the device's primary context), after which this entry
+ * point must not be called again in that process.  All calls share the one array, which keeps
  * the last call's contents (nothing in it needs to start at zero: each call
  * overwrites the words it reads), so calls that overlap on the same GPU —
  * from two streams at once, for instance — race; order them on one stream or
@@ -250,8 +255,9 @@ int rf_moe_grouped_gemm_gated_gather(const void *x, int64_t x_rows, const int32_
  * Selects the grouped-GEMM implementation for subsequent calls of this
  * process: 0 = automatic (tensor cores whenever the shape allows, tile width
  * chosen per launch), 1 = CUDA cores only (used by tests to cross-check the
- * two implementations), 2 / 3 / 4 = tensor cores with tile width N = 256 /
- * 128 / 64 (tests and tuning; the results are the same bits for every width).
+ * two implementations), 2 / 3 / 4 = single-CTA tensor-core kernel with tile
+ * width N = 256 / 128 / 64, 5 = the CTA-pair tensor-core kernel (weights on
+ * the MMA's M side; the automatic choice for 16-bit layers).
  * No reference counterpart (the reference has a single torch matmul path).
  */
 int rf_moe_set_gemm_impl(int impl);
@@ -267,6 +273,19 @@ int rf_moe_grouped_gemm_down(const void *h, const void *w2, void *y,
                              const int32_t *expert_slot, const int32_t *groups, int64_t n_groups,
                              int64_t E, int64_t num_slots, int64_t rows_capacity,
                              int64_t H, int64_t I, int dtype, rf_stream_t stream);
+
+/*
+ * K4 with an addend: y[r, n] = round(addend[r, n] + round(sum_j h[r,j] *
+ * w2[s,n,j])) in the layer dtype (addend has y's layout and may be y).  The
+ * layer sums its shared experts with it in the reference harness's order:
+ * each expert's output rounded, then added in the layer dtype
+ * (sum_s MLP_s(x), reframework/layers/mlp.py:35-39 per shared expert).
+ */
+int rf_moe_grouped_gemm_down_add(const void *h, const void *w2, void *y, const void *addend,
+                                 const int32_t *expert_offsets, const int32_t *expert_counts,
+                                 const int32_t *expert_slot, const int32_t *groups, int64_t n_groups,
+                                 int64_t E, int64_t num_slots, int64_t rows_capacity,
+                                 int64_t H, int64_t I, int dtype, rf_stream_t stream);
 
 /*
  * Expert-parallel exchange plan for one rank (host function, no GPU work).

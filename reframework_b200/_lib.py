@@ -56,6 +56,9 @@ _SIGNATURES = {
     "rf_moe_grouped_gemm_down": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                         _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64,
                                         _int, _c_void_p]),
+    "rf_moe_grouped_gemm_down_add": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                            _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64,
+                                            _int, _c_void_p]),
     "rf_moe_combine": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p,
                               _c_void_p, _c_void_p, _int, _int, _c_void_p, _c_void_p]),
     "rf_moe_combine_rmsnorm": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _int, _c_void_p,

@@ -2,6 +2,8 @@
 // the CUDA-core implementation (gemm_simt.cu).
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace rf {
@@ -48,9 +50,23 @@ struct GroupedGemmArgs {
   // down GEMM only: store rows into the peers' return buffers (slot / groups
   // must be NULL, so group j is local slot j)
   const RemoteOut *remote = nullptr;
+  // down GEMM only: out[r, n] = round(addend[r, n] + round(acc)) in the layer
+  // dtype (addend has out's layout; it may be out itself)
+  const void *addend = nullptr;
 };
 
 int launch_simt_grouped_gemm(const GroupedGemmArgs &g, bool gated, cudaStream_t st);
+
+// A 16-bit tiled tensor map with the 128-byte swizzle (gemm_tc.cu).
+bool tma_encode(CUtensorMap *m, int dtype, int rank, const void *base, const cuuint64_t *dims,
+                const cuuint64_t *strides, const cuuint32_t *box);
+// The GEMM implementation chosen by rf_moe_set_gemm_impl (0 = automatic).
+int gemm_impl();
+
+// The grouped GEMM of `g` on CTA pairs (gemm_pair.cu): weight rows on the
+// MMA's M side (256 per pair), token rows on N in steps of 16.  -1 when the
+// shape, dtype or device does not suit it, else a status.
+int launch_pair_grouped_gemm(const GroupedGemmArgs &g, bool gated, cudaStream_t st);
 
 // Dense out[M, ld_out] (fp32) = a[M, K] . w[N, K]^T on the tensor cores
 // (gemm_tc.cu); -1 when the shape or dtype is not handled there.

@@ -145,7 +145,9 @@ __global__ void __launch_bounds__(NT) simt_grouped_gemm(rf::GroupedGemmArgs p) {
     for (int j = 0; j < 4; ++j) {
       const int c = n0 + tx * 4 + j;
       if (c >= p.N) continue;
-      const float v = GATED ? rf::gated_elem<T>(p.act, accg[i][j], accu[i][j]) : accg[i][j];
+      float v = GATED ? rf::gated_elem<T>(p.act, accg[i][j], accu[i][j]) : accg[i][j];
+      if (!GATED && p.addend)  // a second shared expert adds onto the first: both rounded, summed
+        v = rf::Cvt<T>::to_f(reinterpret_cast<const T *>(p.addend)[(row0 + r) * p.N + c]) + rf::round_to<T>(v);
       out[(row0 + r) * p.N + c] = rf::Cvt<T>::from_f(v);
     }
   }
@@ -273,7 +275,10 @@ __global__ void __launch_bounds__(SNT) simt_skinny_gemm(rf::GroupedGemmArgs p) {
 #pragma unroll
       for (int r = 0; r < RPT; ++r) {
         if (rg * RPT + r >= rows) break;
-        const float v = GATED ? rf::gated_elem<T>(p.act, accg[r], accu[GATED ? r : 0]) : accg[r];
+        float v = GATED ? rf::gated_elem<T>(p.act, accg[r], accu[GATED ? r : 0]) : accg[r];
+        if (!GATED && p.addend)
+          v = rf::Cvt<T>::to_f(reinterpret_cast<const T *>(p.addend)[(orow - out) + (int64_t)r * p.N]) +
+              rf::round_to<T>(v);
         orow[(int64_t)r * p.N] = rf::Cvt<T>::from_f(v);
       }
     }

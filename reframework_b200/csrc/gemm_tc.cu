@@ -11,7 +11,7 @@
 //   warp 0      TMA producer: per 64-deep k-block loads the 128-row A tile
 //               and the 256-row B tile (gated: 128 gate rows + the matching
 //               128 up rows, so one accumulator holds both halves) into a
-//               4-stage shared-memory ring (128-byte swizzle, no multicast).
+//               4-stage shared-memory ring (128-byte swizzle, this CTA only).
 //   warp 1      allocates 512 TMEM columns and issues tcgen05.mma (M=128,
 //               N=256, K=16, bf16/fp16 in, fp32 accumulate) from one thread;
 //               two accumulators (2 x 256 columns) let the epilogue of tile i
@@ -41,6 +41,7 @@
 #include "gemm.cuh"
 
 RF_DEVICE_ERROR_WORD();
+#include "tc_ptx.cuh"
 
 namespace {
 
@@ -58,7 +59,6 @@ constexpr int NTHREADS = 32 * (2 + EPI_WARPS);
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int BM_SMALL = 32;          // A rows loaded for a tile with at most 32 valid rows
 constexpr int MAX_GROUPS = 1024;
-constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
 // Per tile width BN (the MMA's N: 256, 128 or 64).  Narrower tiles give more
 // tiles (better balance over 148 SMs when there are few rows, as in decode)
@@ -92,147 +92,8 @@ struct TcArgs {
   // of the tensor behind the A map (the token's activation row); -1 = pad row
   const int32_t *gather_src;
   int gather_div;
+  const void *addend;  // down only: out = round(addend + round(acc)); may be NULL or out
 };
-
-// ------------------------------------------------------------------ PTX
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Wait for the phase of `parity` to complete.  Gives up (false) when another
-// role of this CTA aborted, or after WAIT_LIMIT_NS (then flags the abort).
-__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                          unsigned sleep_ns = 0) {
-  if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = rf::globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (sleep_ns) __nanosleep(sleep_ns);
-    if (mbar_try(bar, parity)) return true;
-    if ((it & 63) == 0) {
-      if (*abort_flag) return false;
-      if (rf::globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
-        *abort_flag = 1;
-        rf_report(RF_DEV_WAIT_TIMEOUT);
-        return false;
-      }
-    }
-  }
-}
-// Wait used on the teardown path only: bounded, ignores the abort flag.
-__device__ void mbar_wait_teardown(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = rf::globaltimer_ns();
-  while (!mbar_try(bar, parity)) {
-    if (rf::globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
-      rf_report(RF_DEV_WAIT_TIMEOUT);
-      return;
-    }
-  }
-}
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
-                                            int c0, int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-      "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1)
-      : "memory");
-}
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
-                                            int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-      "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-// Four rows of a 2-D tensor (row indices r0..r3, one 64-column box each) into
-// four consecutive 128-byte smem rows (Blackwell tile::gather4; the tensor
-// map's box is 64 x 1).
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0,
-                                            int r0, int r1, int r2, int r3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
-      "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_alloc(uint32_t holder, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(holder),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
-}
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// 32 TMEM lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld_wait() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
-// 128 bytes grouped by 8 (1024 B between groups), sm_100 descriptor version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu)   // start address (16-byte units)
-         | ((uint64_t)1 << 16)                // leading byte offset (unused for SW128 K-major)
-         | ((uint64_t)(1024 >> 4) << 32)      // stride byte offset: 8-row group pitch
-         | ((uint64_t)1 << 46)                // descriptor version (sm_100)
-         | ((uint64_t)2 << 61);               // layout: 128-byte swizzle
-}
 
 // Instruction descriptor of kind::f16: fp32 accumulator, A/B K-major,
 // M = 128, N = BN; operand format 0 = f16, 1 = bf16 (A and B always equal).
@@ -567,6 +428,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j)
               pk[j] = rf::pack2<T>(__uint_as_float(v32[2 * j]), __uint_as_float(v32[2 * j + 1]));
+            if (!REMOTE && p.addend) {  // a second shared expert adds onto the first
+              const T *arow = reinterpret_cast<const T *>(p.addend) + (int64_t)(row0 + r) * p.out_ld;
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                const int col = n0 + c + 8 * v;
+                if (col >= p.N) continue;
+                float yf[8], af[8];
+                rf::unpack16<T>(make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]), yf);
+                rf::unpack16<T>(*reinterpret_cast<const uint4 *>(arow + col), af);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) pk[4 * v + i] = rf::pack2<T>(af[2 * i] + yf[2 * i], af[2 * i + 1] + yf[2 * i + 1]);
+              }
+            }
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               const int col = n0 + c + 8 * v;
@@ -622,7 +496,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-int g_gemm_impl = 0;  // 0 = auto, 1 = CUDA cores only, 2/3/4 = tensor cores with BN 256/128/64
+// 0 = auto (CTA-pair tensor-core kernel where it applies), 1 = CUDA cores only,
+// 2/3/4 = single-CTA tensor-core kernel with BN 256/128/64, 5 = CTA pairs
+int g_gemm_impl = 0;
 
 bool encode(CUtensorMap *m, int dtype, int rank, const void *base, const cuuint64_t *dims,
             const cuuint64_t *strides, const cuuint32_t *box) {
@@ -666,6 +542,7 @@ int launch_tc_t(const rf::GroupedGemmArgs &g, const CUtensorMap &ma, const CUten
   p.act = g.act;
   p.gather_src = g.gather_src;
   p.gather_div = g.gather_div;
+  p.addend = GATED ? nullptr : g.addend;
   if constexpr (REMOTE) {
     kern<<<rf::num_sms(), NTHREADS, C::SMEM_BYTES, st>>>(ma, ma32, mb, p, *g.remote);
     return rf::check_launch("tensor-core down GEMM with peer stores");
@@ -709,7 +586,7 @@ int launch_tc_dt(const rf::GroupedGemmArgs &g, bool gated, int bn, const CUtenso
 // the SMs, so N = 128.
 int pick_bn(const rf::GroupedGemmArgs &g, bool gated) {
   (void)gated;
-  if (g_gemm_impl >= 2) return g_gemm_impl == 2 ? 256 : g_gemm_impl == 3 ? 128 : 64;
+  if (g_gemm_impl >= 2 && g_gemm_impl <= 4) return g_gemm_impl == 2 ? 256 : g_gemm_impl == 3 ? 128 : 64;
   const int64_t groups = std::max(1, g.n_groups);
   int64_t pairs = g.rows_capacity - groups * (BM - 1);
   if (pairs < 1) pairs = std::min<int64_t>(g.rows_capacity, groups);
@@ -720,6 +597,13 @@ int pick_bn(const rf::GroupedGemmArgs &g, bool gated) {
 // shape or dtype is outside what it handles (the CUDA-core kernel runs then).
 int try_tc(const rf::GroupedGemmArgs &g, bool gated, cudaStream_t st, int *rc) {
   if (g_gemm_impl == 1) return 0;
+  if (g_gemm_impl == 0 || g_gemm_impl == 5) {
+    const int prc = rf::launch_pair_grouped_gemm(g, gated, st);
+    if (prc >= 0) {
+      *rc = prc;
+      return 1;
+    }
+  }
   if (g.dtype != RF_BF16 && g.dtype != RF_F16) return 0;
   if (g.Kdim % 8 || g.N % 8 || g.n_groups > MAX_GROUPS) return 0;
   if ((uintptr_t)g.a % 16 || (uintptr_t)g.w % 16 || (uintptr_t)g.out % 16) return 0;
@@ -789,6 +673,12 @@ int launch_dense(const CUtensorMap &ma, const CUtensorMap &ma32, const CUtensorM
 }  // namespace
 
 namespace rf {
+bool tma_encode(CUtensorMap *m, int dtype, int rank, const void *base, const cuuint64_t *dims,
+                const cuuint64_t *strides, const cuuint32_t *box) {
+  return encode(m, dtype, rank, base, dims, strides, box);
+}
+int gemm_impl() { return g_gemm_impl; }
+
 // out[m, n] = sum_k a[m, k] * w[n, k] for m < M, n < N, fp32 accumulation
 // on the tensor cores, stored unrounded as fp32 rows of ld_out (a multiple of
 // 4, >= N) columns.  a [M, K] and w [N, K] are 16-bit of the same dtype.
@@ -852,7 +742,7 @@ int grouped_gemm(const void *a, const void *w, void *out, const int32_t *offsets
                  const int32_t *counts, const int32_t *slot, const int32_t *groups,
                  int64_t n_groups, int64_t E, int64_t num_slots, int64_t rows_capacity,
                  int64_t Kdim, int64_t N, int dtype, int act, bool gated, rf_stream_t stream,
-                 const char *name) {
+                 const char *name, const void *addend = nullptr) {
   const std::string nm(name);
   RF_CHECK_ARG(rf::valid_dtype(dtype), nm + ": unknown dtype");
   RF_CHECK_ARG(act == RF_ACT_SILU || act == RF_ACT_GELU || act == RF_ACT_GELU_TANH,
@@ -881,6 +771,7 @@ int grouped_gemm(const void *a, const void *w, void *out, const int32_t *offsets
   g.N = (int)N;
   g.dtype = dtype;
   g.act = act;
+  g.addend = addend;
   cudaStream_t st = (cudaStream_t)stream;
   int rc = RF_OK;
   if (try_tc(g, gated, st, &rc)) return rc;
@@ -890,7 +781,7 @@ int grouped_gemm(const void *a, const void *w, void *out, const int32_t *offsets
 }  // namespace
 
 extern "C" int rf_moe_set_gemm_impl(int impl) {
-  if (impl < 0 || impl > 4) return rf::fail(RF_ERR_ARG, "rf_moe_set_gemm_impl: 0 to 4");
+  if (impl < 0 || impl > 5) return rf::fail(RF_ERR_ARG, "rf_moe_set_gemm_impl: 0 to 5");
   g_gemm_impl = impl;
   return RF_OK;
 }
@@ -960,4 +851,16 @@ extern "C" int rf_moe_grouped_gemm_down(const void *h, const void *w2, void *y,
   return grouped_gemm(h, w2, y, expert_offsets, expert_counts, expert_slot, groups, n_groups, E,
                       num_slots, rows_capacity, I, H, dtype, RF_ACT_SILU, false, stream,
                       "rf_moe_grouped_gemm_down");
+}
+
+extern "C" int rf_moe_grouped_gemm_down_add(const void *h, const void *w2, void *y, const void *addend,
+                                            const int32_t *expert_offsets, const int32_t *expert_counts,
+                                            const int32_t *expert_slot, const int32_t *groups,
+                                            int64_t n_groups, int64_t E, int64_t num_slots,
+                                            int64_t rows_capacity, int64_t H, int64_t I, int dtype,
+                                            rf_stream_t stream) {
+  RF_CHECK_ARG(addend, "rf_moe_grouped_gemm_down_add: null addend");
+  return grouped_gemm(h, w2, y, expert_offsets, expert_counts, expert_slot, groups, n_groups, E,
+                      num_slots, rows_capacity, I, H, dtype, RF_ACT_SILU, false, stream,
+                      "rf_moe_grouped_gemm_down_add", addend);
 }

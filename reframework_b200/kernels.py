@@ -172,16 +172,26 @@ def grouped_gemm_gated_gather(x: torch.Tensor, src_slot: torch.Tensor, topk: int
 
 def grouped_gemm_down(h: torch.Tensor, w2: torch.Tensor, offsets: torch.Tensor, counts: torch.Tensor,
                       out: torch.Tensor, *, slot: Optional[torch.Tensor] = None,
-                      groups: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``out[r] = h[r] . w2[s]^T`` per expert segment."""
-    dev = _require_cuda(h, w2, offsets, counts, out, slot, groups)
+                      groups: Optional[torch.Tensor] = None, addend: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out[r] = h[r] . w2[s]^T`` per expert segment; with ``addend`` (out's
+    shape and dtype, may be ``out``): ``out[r] = addend[r] + round(h[r] . w2[s]^T)``
+    rounded in the layer dtype."""
+    dev = _require_cuda(h, w2, offsets, counts, out, slot, groups, addend)
     S, H, I = w2.shape
     E = counts.shape[0]
-    rc = lib().rf_moe_grouped_gemm_down(
-        ptr(h), ptr(w2), ptr(out), ptr(offsets), ptr(counts), ptr(slot), ptr(groups),
-        0 if groups is None else groups.numel(), E, S, h.shape[0], H, I, dtype_code(h.dtype),
-        stream_of(dev))
-    check(rc, "rf_moe_grouped_gemm_down")
+    ng = 0 if groups is None else groups.numel()
+    if addend is None:
+        rc = lib().rf_moe_grouped_gemm_down(
+            ptr(h), ptr(w2), ptr(out), ptr(offsets), ptr(counts), ptr(slot), ptr(groups),
+            ng, E, S, h.shape[0], H, I, dtype_code(h.dtype), stream_of(dev))
+        check(rc, "rf_moe_grouped_gemm_down")
+        return out
+    if addend.shape != out.shape or addend.dtype != out.dtype or not addend.is_contiguous():
+        raise _lib.RfMoeError("grouped_gemm_down: addend must be contiguous with out's shape and dtype")
+    rc = lib().rf_moe_grouped_gemm_down_add(
+        ptr(h), ptr(w2), ptr(out), ptr(addend), ptr(offsets), ptr(counts), ptr(slot), ptr(groups),
+        ng, E, S, h.shape[0], H, I, dtype_code(h.dtype), stream_of(dev))
+    check(rc, "rf_moe_grouped_gemm_down_add")
     return out
 
 
@@ -237,16 +247,30 @@ def dense_segment(device: torch.device, rows: int) -> Tuple[torch.Tensor, torch.
     return seg
 
 
-def dense_gated_mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, activation: str = "silu") -> torch.Tensor:
-    """A dense gated MLP over all rows of ``x`` (the shared expert), on the grouped kernels
-    with a single segment.  w1 [2I,H], w2 [H,I]."""
+def dense_gated_mlp(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, activation: str = "silu", *,
+                    addend: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """A dense gated MLP over all rows of ``x`` (a shared expert), on the grouped kernels
+    with a single segment.  w1 [2I,H], w2 [H,I].  With ``addend`` [T,H] the result
+    is ``addend + MLP(x)`` with both terms rounded to the layer dtype (written
+    into ``addend``)."""
     T, H = x.shape
     off, cnt = dense_segment(x.device, T)
     I = w2.shape[1]
     h = torch.empty(T, I, dtype=x.dtype, device=x.device)
     grouped_gemm_gated(x, w1.unsqueeze(0), off, cnt, h, activation=activation)
-    y = torch.empty(T, H, dtype=x.dtype, device=x.device)
-    grouped_gemm_down(h, w2.unsqueeze(0), off, cnt, y)
+    y = addend if addend is not None else torch.empty(T, H, dtype=x.dtype, device=x.device)
+    grouped_gemm_down(h, w2.unsqueeze(0), off, cnt, y, addend=addend)
+    return y
+
+
+def shared_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, activation: str = "silu") -> torch.Tensor:
+    """``sum_s MLP_s(x)`` over the shared experts w1 [S,2I,H], w2 [S,H,I] in the
+    reference harness's arithmetic: each expert's output rounded to the layer
+    dtype, then added in order in the layer dtype (the second and later
+    experts' down GEMMs add onto the running sum in their epilogue)."""
+    y = None
+    for s in range(w1.shape[0]):
+        y = dense_gated_mlp(x, w1[s], w2[s], activation, addend=y)
     return y
 
 

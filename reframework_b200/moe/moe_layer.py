@@ -166,7 +166,6 @@ class FusedMoE(nn.Module):
         else:
             self.shared_w1 = self.shared_w2 = self.shared_gate = None
         self._bank_cache: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
-        self._shared_cache: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
         self._router_cat: Optional[Tuple[tuple, torch.Tensor]] = None
         self._cache: Optional[ExpertOffloadCache] = None
         self._cpu_split_enabled = False
@@ -199,14 +198,12 @@ class FusedMoE(nn.Module):
     # ------------------------------------------------------------ weight banks
     def _apply(self, fn, recurse=True):
         self._bank_cache = None
-        self._shared_cache = None
         self._router_cat = None
         return super()._apply(fn, recurse)
 
     def invalidate_banks(self) -> None:
         """Call after replacing an expert parameter's ``.data`` directly."""
         self._bank_cache = None
-        self._shared_cache = None
         self._router_cat = None
 
     def _resident_banks(self) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -226,17 +223,12 @@ class FusedMoE(nn.Module):
         return self._bank_cache
 
     def _shared_banks(self) -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
-        """Shared experts fused into one MLP of width S*Is: sum_s MLP_s(x)."""
+        """The shared experts' weights, (w1 [S,2Is,H], w2 [S,H,Is]); the layer
+        computes sum_s MLP_s(x) with K.shared_experts (each expert's output
+        rounded, then summed in order, as the reference harness composes it)."""
         if not self.num_shared_experts:
             return None
-        c = self._shared_cache
-        if c is None:
-            Is = self.shared_intermediate_size
-            w1, w2 = self.shared_w1.detach(), self.shared_w2.detach()
-            w1c = torch.cat([w1[:, :Is].reshape(-1, w1.shape[-1]), w1[:, Is:].reshape(-1, w1.shape[-1])], 0)
-            w2c = torch.cat(list(w2), dim=1)
-            c = self._shared_cache = (w1c.contiguous(), w2c.contiguous())
-        return c
+        return self.shared_w1.detach(), self.shared_w2.detach()
 
     # ------------------------------------------------------------ offload setup
     def build_offload_cache(self, device: torch.device, lru_capacity: int) -> ExpertOffloadCache:
@@ -362,14 +354,14 @@ class FusedMoE(nn.Module):
             side = self._side_stream(x2.device)
             side.wait_stream(cur)
             with torch.cuda.stream(side):
-                shared_y = K.dense_gated_mlp(x2, sb[0], sb[1], self.activation)
+                shared_y = K.shared_experts(x2, sb[0], sb[1], self.activation)
                 shared_done = torch.cuda.Event()
                 shared_done.record(side)
             x2.record_stream(side)
             shared_y.record_stream(cur)
         w, ids32, _, _, sscale = self._router(x2, ids32=True, ids64=False)
         if sb is not None and self.uses_offload:
-            shared_y = K.dense_gated_mlp(x2, sb[0], sb[1], self.activation)
+            shared_y = K.shared_experts(x2, sb[0], sb[1], self.activation)
         if self.cpu_split:
             if shared_y is not None or res2 is not None or norm is not None:
                 raise RfMoeError("the expert split computes the routed experts only (no shared experts, "
@@ -570,4 +562,3 @@ class FusedMoE(nn.Module):
                 key = f"{pre}shared_expert_gate.weight"
                 if self.shared_gate is not None and key in state_dict:
                     self.shared_gate.copy_(state_dict[key].detach().reshape(-1).to(dtype=self.dtype))
-        self._shared_cache = None

@@ -556,7 +556,7 @@ class EPFusedMoE(nn.Module):
             y_back = K.gather_rows(y_back, views[5], torch.empty_like(y_back))
         shared_y = None
         if self._shared is not None:
-            shared_y = K.dense_gated_mlp(x2, self._shared[0], self._shared[1], self.activation)
+            shared_y = K.shared_experts(x2, self._shared[0], self._shared[1], self.activation)
         out = K.combine(y_back, p.row_of_slot, w, out, shared_y=shared_y, shared_scale=sscale, residual=res2,
                         precise=self.precise_combine)
         self._mark("unpermute+shared+combine")
@@ -685,7 +685,7 @@ class EPFusedMoE(nn.Module):
         # reads them through the permute's own row_of_slot (expert order)
         shared_y = None
         if self._shared is not None:
-            shared_y = K.dense_gated_mlp(x2, self._shared[0], self._shared[1], self.activation)
+            shared_y = K.shared_experts(x2, self._shared[0], self._shared[1], self.activation)
         wf = w.contiguous()
         mode = _lib_mod.COMBINE_FP32 if self.precise_combine else _lib_mod.COMBINE_REFERENCE
         check(lib().rf_moe_combine(px.back_ptr(), p.row_of_slot.data_ptr(), wf.data_ptr(), T, Kk, H,
@@ -741,7 +741,7 @@ class EPFusedMoE(nn.Module):
             y_back = keep.data_ptr()
         shared_y = None
         if self._shared is not None:
-            shared_y = K.dense_gated_mlp(x2, self._shared[0], self._shared[1], self.activation)
+            shared_y = K.shared_experts(x2, self._shared[0], self._shared[1], self.activation)
         wf = w.contiguous()
         mode = _lib_mod.COMBINE_FP32 if self.precise_combine else _lib_mod.COMBINE_REFERENCE
         check(lib().rf_moe_combine(y_back, p.row_of_slot.data_ptr(), wf.data_ptr(), T, Kk, H,

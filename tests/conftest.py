@@ -37,7 +37,7 @@ def max_rel(a, r):
 ULP_REL = {torch.bfloat16: 2.0 ** -7, torch.float16: 2.0 ** -10}
 
 
-def routing_mismatches(ids, ids_ref, logits_ref, top_k, round_dtype=None, max_frac=1e-3):
+def routing_mismatches(ids, ids_ref, logits_ref, top_k, round_dtype=None, max_frac=1e-3, max_count=None):
     """Tokens whose routed expert set differs from the reference's.
 
     A difference is accepted only when it is a numerical tie at the top-k
@@ -45,7 +45,8 @@ def routing_mismatches(ids, ids_ref, logits_ref, top_k, round_dtype=None, max_fr
     tolerance of the k-th largest logit — 1e-5 relative for an fp32 router,
     one ulp of the layer dtype when the logits are rounded to it (then the
     reference's own choice among equal values is implementation-defined).
-    Returns the list of such tokens (asserts there are few)."""
+    At most ``max_count`` such tokens (default: max(2, max_frac * T)) are
+    accepted.  Returns the list of such tokens."""
     ids = ids.cpu().long()
     bad = []
     for t in (ids.sort(1).values != ids_ref.sort(1).values).any(1).nonzero().flatten().tolist():
@@ -57,7 +58,8 @@ def routing_mismatches(ids, ids_ref, logits_ref, top_k, round_dtype=None, max_fr
         gaps = [abs(float(lg[e] - kth)) for e in diff]
         assert max(gaps) <= tol, f"token {t}: ids {ids[t].tolist()} vs {ids_ref[t].tolist()}, gaps {gaps}"
         bad.append(t)
-    assert len(bad) <= max(2, int(max_frac * ids.shape[0])), f"{len(bad)} tie-swapped tokens"
+    cap = max(2, int(max_frac * ids.shape[0])) if max_count is None else max_count
+    assert len(bad) <= cap, f"{len(bad)} tie-swapped tokens (at most {cap} accepted)"
     return bad
 
 

@@ -87,7 +87,7 @@ def test_fused_gather_gemm_reports_unsupported_dtype():
      "unknown mode"),
     (lambda L: L.rf_moe_grouped_gemm_gated(None, None, None, None, None, None, None, 0, 8, 8, 64, 64,
                                            64, 2, 9, None), "activation"),
-    (lambda L: L.rf_moe_set_gemm_impl(5), "0 to 4"),
+    (lambda L: L.rf_moe_set_gemm_impl(6), "0 to 5"),
     (lambda L: L.rf_moe_combine_rmsnorm(None, None, None, 4, 2, 64, 2, None, None, None, 0, None, None, -1.0,
                                         None, None, None), "eps"),
     (lambda L: L.rf_moe_int8_quantize(None, 9, None, None, None, 1, 4, 8, 64, None, 1, None, None, None), "dtype"),

@@ -331,3 +331,35 @@ def test_device_plan_too_small_buffers_move_nothing(cuda_ok):
     assert all(not bool(t.any()) for t in recv), "a failed plan moved rows"
     assert all(bool((c[:R] == 5).all()) for c in ctrl), "flags must rise even when nothing moves"
     assert _lib.device_status() == 0
+
+
+def test_bounded_flag_wait_gives_up_and_reports(cuda_ok):
+    """Failure detection on the device without a fault: a stream-ordered wait
+    for a flag that no rank ever raises (the picture of a peer that died
+    between steps) gives up after its 2 s limit, records RF_DEV_WAIT_TIMEOUT in
+    the device error word and returns, so the context and the stream stay
+    usable.  Reference analogue: the per-rank timeout of
+    reframework/parallel/dist.py:173-175."""
+    import time
+    from reframework_b200 import _lib
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    assert _lib.device_status() == 0
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    assert L.rf_moe_ep_wait(flags.data_ptr(), 1, 7, st) == 0
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert 1.5 < waited < 60, f"the wait gave up after {waited:.2f} s"
+    assert _lib.device_status() == 2  # RF_DEV_WAIT_TIMEOUT (read and cleared)
+    # the stream still runs work, and a raised flag ends the same wait at once
+    v = torch.arange(4096, device=dev, dtype=torch.int64).sum()
+    assert int(v) == 4095 * 4096 // 2
+    flags.fill_(7)
+    t0 = time.perf_counter()
+    assert L.rf_moe_ep_wait(flags.data_ptr(), 1, 7, st) == 0
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 1.0
+    assert _lib.device_status() == 0

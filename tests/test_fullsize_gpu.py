@@ -103,3 +103,187 @@ def test_c2_full_size_parity_with_oracle():
     K.grouped_gemm_down(h, w2b, pp.offsets, pp.counts, yv)
     K.combine(yv, pp.row_of_slot, w_half, o_half)
     assert torch.equal(o_half, out * 0.5)
+
+
+def _layer_from(cfg, d):
+    """A resident FusedMoE on the GPU holding the workload's weights (fp32
+    router with the config's bias, shared experts as configured)."""
+    moe = FusedMoE(cfg.experts, cfg.top_k, cfg.hidden, cfg.inter, activation=cfg.activation,
+                   renormalize=cfg.renormalize, dtype=cfg.dtype, router_dtype=torch.float32,
+                   num_shared_experts=cfg.shared_count, shared_intermediate_size=cfg.shared_inter,
+                   shared_expert_gate=cfg.shared_gate, device=DEV)
+    with torch.no_grad():
+        moe.gate.copy_(d["gate"])
+        w1b, w2b = moe._resident_banks()
+        w1b.copy_(d["w1"])
+        w2b.copy_(d["w2"])
+        if cfg.shared_count:
+            moe.shared_w1.copy_(d["shared_w1"])
+            moe.shared_w2.copy_(d["shared_w2"])
+            if cfg.shared_gate:
+                moe.shared_gate.copy_(d["shared_gate"])
+    if d["bias"] is not None:
+        moe.set_router_bias(d["bias"][0])
+    return moe
+
+
+def _oracle_forward(cfg, d):
+    return O.moe_forward(d["x"], d["gate"], d["w1"], d["w2"], top_k=cfg.top_k, renormalize=cfg.renormalize,
+                         bias=d["bias"][0] if d["bias"] is not None else None, router_fp32=True,
+                         activation=cfg.activation,
+                         shared_w1=d.get("shared_w1") if cfg.shared_count else None,
+                         shared_w2=d.get("shared_w2") if cfg.shared_count else None,
+                         shared_gate=d.get("shared_gate") if cfg.shared_gate else None)
+
+
+def _check_full_size(cfg, label):
+    d = generate(cfg)
+    ref = _oracle_forward(cfg, d)
+    moe = _layer_from(cfg, d)
+    x = d["x"].to(DEV)
+    with torch.no_grad():
+        w, ids = moe.route(x)
+        out = moe(x)
+        out2 = moe(x)
+    assert torch.equal(out, out2), "not deterministic"
+    assert routing_mismatches(ids, ref["ids"], ref["logits"], cfg.top_k) == []
+    assert torch.equal(ids.cpu(), ref["ids"]), "fp32 routing must be bit-exact at full size"
+    torch.testing.assert_close(w.cpu(), ref["weights"], rtol=2e-5, atol=2e-6)
+    p = K.permute(ids.to(torch.int32), cfg.experts)
+    counts, order = O.permutation(ids.cpu().numpy(), cfg.experts)
+    off = p.offsets.cpu().numpy()
+    src = p.src_slot.cpu().numpy()
+    assert np.array_equal(p.counts.cpu().numpy(), counts)
+    got = np.concatenate([src[off[e]:off[e] + counts[e]] for e in range(cfg.experts)])
+    assert np.array_equal(got, order), "permutation differs from the reference's selection order"
+    err = max_rel(out, ref["out"])
+    same = float((out.cpu() == ref["out"]).float().mean())
+    print(f"full-size {label}: max-rel {err:.3e}, bit-identical outputs {same:.4f}")
+    assert err < 1e-2, f"max-rel {err:.3e}"
+    return moe, d, out
+
+
+def test_c3_full_size_parity_with_oracle():
+    """Qwen1.5-MoE decode at its benchmark size (H2048 E60 top-4 I1408, 64
+    tokens, Zipf(1.1) router bias, one shared SwiGLU expert of 5632 gated by
+    sigmoid(x.w_s)): fp32-router ids and the permutation bit-exact, output
+    within max-rel 1e-2 of the oracle (reference fused.py:32-87 plus the
+    harness's gated shared expert)."""
+    _check_full_size(CONFIGS["c3_qwen_decode"], "C3")
+
+
+@pytest.mark.parametrize("renormalize", [True, False])
+def test_c4_full_size_parity_with_oracle(renormalize):
+    """DeepSeek-V2-Lite shape at its benchmark size (H2048 E64 top-6 I1408,
+    8192 tokens, two shared experts of 1408), renormalised and not."""
+    from dataclasses import replace
+    cfg = replace(CONFIGS["c4_dsv2lite_ep"], renormalize=renormalize)
+    _check_full_size(cfg, f"C4 renormalize={renormalize}")
+
+
+def _emulated_ep_forward(moe, x, R, placement):
+    """The expert-parallel forward of EPFusedMoE's device-planned path, R ranks
+    emulated on one GPU with separate buffers: every rank's route + compact
+    permute, device plan, dispatch push, regroup, gated GEMM, down GEMM with the
+    return exchange in its epilogue, and combine (+ the shared experts).  The
+    stages run rank by rank in stream order, so each bounded wait starts only
+    after every push it waits for has run.  Returns the concatenated outputs."""
+    import ctypes
+    from reframework_b200.parallel.ep import shard_range  # noqa: F401  (placement built by the caller)
+    L = _lib.lib()
+    T, H = x.shape
+    E, Kk, I = moe.num_experts, moe.top_k, moe.intermediate_size
+    st = torch.cuda.current_stream(DEV).cuda_stream
+    bounds = [(T * r // R, T * (r + 1) // R) for r in range(R)]
+    routed = []
+    for lo, hi in bounds:
+        w, ids32, _, _, sscale = moe._router(x[lo:hi].contiguous(), ids32=True, ids64=False)
+        routed.append((w, ids32, sscale, K.permute(ids32, E, align=1)))
+    cnt = torch.stack([r[3].counts for r in routed]).contiguous()
+    flat = torch.tensor([e for s in placement.slots for e in s], dtype=torch.int32, device=DEV)
+    offs = torch.tensor(np.cumsum([0] + [len(s) for s in placement.slots]), dtype=torch.int32, device=DEV)
+    nslots = int(flat.numel())
+    tmax = max(hi - lo for lo, hi in bounds)
+    recv_cap, back_cap = R * tmax * Kk, tmax * Kk
+    row_bytes = H * x.element_size()
+    recv = [torch.zeros(recv_cap, H, dtype=x.dtype, device=DEV) for _ in range(R)]
+    back = [torch.zeros(back_cap, H, dtype=x.dtype, device=DEV) for _ in range(R)]
+    ctrl = [torch.zeros(2 * R, dtype=torch.int32, device=DEV) for _ in range(R)]
+    done = torch.zeros(R, dtype=torch.int32, device=DEV)
+    ptrs = lambda ts: (ctypes.c_void_p * R)(*[t.data_ptr() for t in ts])  # noqa: E731
+    flags = lambda d_, me: (ctypes.c_void_p * R)(*[ctrl[d].data_ptr() + 4 * (d_ * R + me) for d in range(R)])  # noqa: E731
+    ws, segs = [], []
+    for me in range(R):
+        S = len(placement.slots[me])
+        nb = L.rf_moe_ep_devplan_workspace_size(R, E, S, nslots)
+        lay = np.zeros(_lib.EP_DEVPLAN_LAYOUT_N, np.int64)
+        assert L.rf_moe_ep_devplan_layout(R, E, S, nslots, lay.ctypes.data) == 0
+        wsp = torch.zeros(nb, dtype=torch.uint8, device=DEV)
+        rows_cap = recv_cap + S * (K.ALIGN - 1)
+        assert L.rf_moe_ep_devplan(cnt.data_ptr(), flat.data_ptr(), offs.data_ptr(), R, E, me, S, nslots, K.ALIGN,
+                                   4, recv_cap, back_cap, rows_cap, wsp.data_ptr(), nb, st) == 0
+        ws.append(wsp)
+        segs.append((wsp[lay[0]:lay[0] + 4 * (S + 1)].view(torch.int32), wsp[lay[1]:lay[1] + 4 * S].view(torch.int32),
+                     rows_cap))
+    epoch = 1
+    for me, (lo, hi) in enumerate(bounds):  # dispatch
+        S = len(placement.slots[me])
+        assert L.rf_moe_ep_devplan_push(ws[me].data_ptr(), R, E, S, nslots, 0, x[lo:hi].data_ptr(),
+                                        routed[me][3].src_slot.data_ptr(), Kk, row_bytes, ptrs(recv),
+                                        flags(0, me), epoch, done.data_ptr() + 4 * me, st) == 0
+    w1b, w2b = moe._resident_banks()
+    for me in range(R):  # expert ranks: regroup, gated GEMM, down GEMM + return
+        assert L.rf_moe_ep_wait(ctrl[me].data_ptr(), R, epoch, st) == 0
+        S = len(placement.slots[me])
+        seg_off, seg_cnt, rows_cap = segs[me]
+        xl = torch.empty(rows_cap, H, dtype=x.dtype, device=DEV)
+        assert L.rf_moe_ep_devplan_regroup(ws[me].data_ptr(), R, E, S, nslots, recv[me].data_ptr(), xl.data_ptr(),
+                                           row_bytes, st) == 0
+        sl = torch.tensor(placement.slots[me], dtype=torch.long, device=DEV)
+        b1, b2 = w1b[sl].contiguous(), w2b[sl].contiguous()
+        h = torch.empty(rows_cap, I, dtype=x.dtype, device=DEV)
+        K.grouped_gemm_gated(xl, b1, seg_off, seg_cnt, h, activation=moe.activation)
+        assert L.rf_moe_ep_devplan_down_return(ws[me].data_ptr(), R, E, S, nslots, h.data_ptr(), b2.data_ptr(),
+                                               rows_cap, H, I, _lib.dtype_code(x.dtype), ptrs(back), flags(1, me),
+                                               epoch, done.data_ptr() + 4 * me, st) == 0
+    outs = []
+    sb = moe._shared_banks()
+    for me, (lo, hi) in enumerate(bounds):  # token ranks: shared experts + combine
+        assert L.rf_moe_ep_wait(ctrl[me].data_ptr() + 4 * R, R, epoch, st) == 0
+        w, ids32, sscale, p = routed[me]
+        xr = x[lo:hi].contiguous()
+        shared_y = K.shared_experts(xr, sb[0], sb[1], moe.activation) if sb is not None else None
+        o = torch.empty(hi - lo, H, dtype=x.dtype, device=DEV)
+        K.combine(back[me][:(hi - lo) * Kk], p.row_of_slot, w, o, shared_y=shared_y, shared_scale=sscale)
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0, "an emulated rank timed out or overflowed its plan"
+    return torch.cat(outs)
+
+
+@pytest.mark.parametrize("R,redundant", [(8, 0), (8, 2), (4, 1)])
+def test_c4_full_size_ep_emulated_matches_single_process(R, redundant):
+    """C4 at its benchmark size split over R expert-parallel ranks emulated on
+    one GPU (contiguous expert shards, optionally with hot-expert replicas):
+    the concatenated rank outputs equal the single-process layer bit for bit
+    (reference contract: reframework/parallel/ep.py:120-150 against
+    reframework/moe/moe_layer.py:451-519)."""
+    from reframework_b200.parallel.eplb import Placement, place_experts
+    from reframework_b200.parallel.ep import shard_range
+    cfg = CONFIGS["c4_dsv2lite_ep"]
+    d = generate(cfg)
+    moe = _layer_from(cfg, d)
+    x = d["x"].to(DEV)
+    with torch.no_grad():
+        ref = moe(x)
+        _, ids = moe.route(x)
+    shards = [shard_range(cfg.experts, R, r) for r in range(R)]
+    if redundant:
+        load = torch.bincount(ids.reshape(-1).cpu(), minlength=cfg.experts).numpy()
+        placement = place_experts(load, shards, redundant)
+        assert sum(len(s) for s in placement.slots) > cfg.experts
+    else:
+        placement = Placement(tuple(tuple(range(a, b)) for a, b in shards))
+    with torch.no_grad():
+        got = _emulated_ep_forward(moe, x, R, placement)
+    assert torch.equal(got, ref), f"R={R}: EP output differs from the single-process layer"

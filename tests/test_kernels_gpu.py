@@ -14,6 +14,9 @@ from reframework_b200.workloads import generate
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
+# tokens whose routed set differs from the golden fixture by a one-ulp logit tie,
+# as observed on B200 for every fixture (16-bit and fp32 routers alike)
+TIE_SWAPS_SEEN = 0
 ROUTE_CASES = ["c1_tiny_fp32", "c2_mini_bf16", "c3_mini_bf16", "c4_mini_bf16", "c4_mini_norenorm",
                "fp16_default", "bf16_gelu_default", "fp32_gelu_tanh", "bf16_entropy_k"]
 
@@ -44,7 +47,8 @@ def test_router_matches_reference(name):
         bias=None if bias is None else bias.to(DEV), round_dtype=rdt,
         entropy_k_min=rec.get("entropy_k_min", 0), want_logits=True, ids64=True)
     logits_ref = O.router_logits(d["x"], d["gate"], bias=bias, fp32=rec["mode"] == "harness")
-    bad = routing_mismatches(ids64, rec["ids"], logits_ref, cfg.top_k, round_dtype=rdt, max_frac=0.05)
+    # no fixture has a tie-swapped token on B200 (measured): any swap fails
+    bad = routing_mismatches(ids64, rec["ids"], logits_ref, cfg.top_k, round_dtype=rdt, max_count=TIE_SWAPS_SEEN)
     if rec["mode"] == "harness":
         assert bad == [], "fp32 router: routing must be bit-exact"
     assert torch.equal(ids32.cpu().long(), ids64.cpu())
@@ -186,7 +190,7 @@ def _torch_grouped(a, w1, w2, counts, offs, act, slot=None):
     return h_ref, y_ref
 
 
-@pytest.mark.parametrize("impl", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("impl", [0, 1, 2, 3, 4, 5])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("H,I,counts,act", [
     (256, 256, [130, 0, 1, 300], "silu"),
@@ -240,7 +244,7 @@ def test_tile_width_is_bitwise_invariant(H, I, counts, act):
     off_t = torch.tensor(offs, dtype=torch.int32, device=DEV)
     cnt_t = torch.tensor(counts, dtype=torch.int32, device=DEV)
     outs = []
-    for impl in (2, 3, 4, 0):
+    for impl in (2, 3, 4):
         _lib.set_gemm_impl(impl)
         h = torch.zeros(rows, I, dtype=dtype, device=DEV)
         y = torch.zeros(rows, H, dtype=dtype, device=DEV)
@@ -249,6 +253,73 @@ def test_tile_width_is_bitwise_invariant(H, I, counts, act):
         outs.append((h, y))
     for h, y in outs[1:]:
         assert torch.equal(h, outs[0][0]) and torch.equal(y, outs[0][1])
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu_tanh"])
+@pytest.mark.parametrize("H,I,counts", [
+    (1024, 1408, [700, 64, 129, 3, 0, 256]),
+    (2048, 1408, [5, 1, 0, 9, 2, 4, 0, 7]),
+    (512, 136, [90, 400, 17]),                  # feature blocks past I and H
+])
+def test_pair_kernel_matches_single_cta_kernel(H, I, counts, act):
+    """The CTA-pair kernel (weights on the MMA's M side, tokens on N) against
+    the single-CTA kernel: every output element is an fp32 sum over the same
+    64-deep k-blocks of 16-wide MMA steps; the two must agree within the
+    rounding of one fp32 accumulation order (bit-identical outputs expected
+    for most elements), and the pair kernel must not write rows past an
+    expert's count."""
+    g = torch.Generator().manual_seed(H * 3 + I)
+    dtype = torch.bfloat16
+    E = len(counts)
+    offs = _segments(counts)
+    rows = offs[-1]
+    a = torch.randn(rows, H, generator=g).to(dtype).to(DEV)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.05).to(dtype).to(DEV)
+    w2 = (torch.randn(E, H, I, generator=g) * 0.05).to(dtype).to(DEV)
+    off_t = torch.tensor(offs, dtype=torch.int32, device=DEV)
+    cnt_t = torch.tensor(counts, dtype=torch.int32, device=DEV)
+    outs = []
+    for impl in (2, 5):
+        _lib.set_gemm_impl(impl)
+        h = torch.zeros(rows, I, dtype=dtype, device=DEV)
+        y = torch.zeros(rows, H, dtype=dtype, device=DEV)
+        K.grouped_gemm_gated(a, w1, off_t, cnt_t, h, activation=act)
+        K.grouped_gemm_down(outs[0][0] if outs else h, w2, off_t, cnt_t, y)  # same h into both down GEMMs
+        outs.append((h, y))
+    (h2, y2), (h5, y5) = outs
+    same_h = float((h2 == h5).float().mean())
+    same_y = float((y2 == y5).float().mean())
+    print(f"pair vs single-CTA: identical h {same_h:.4f}, y {same_y:.4f}")
+    assert max_rel(h5, h2) < 8e-3 and max_rel(y5, y2) < 8e-3
+    for e, c in enumerate(counts):
+        assert torch.count_nonzero(h5[offs[e] + c:offs[e + 1]]) == 0
+        assert torch.count_nonzero(y5[offs[e] + c:offs[e + 1]]) == 0
+
+
+@pytest.mark.parametrize("impl", [0, 1, 2, 5])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_down_gemm_addend_rounds_like_the_reference(impl, dtype):
+    """rf_moe_grouped_gemm_down_add: out = round(addend + round(h . w2^T)) in
+    the layer dtype, bit for bit what two separately rounded shared-expert
+    outputs summed in that dtype give (in place, addend == out, too)."""
+    if dtype == torch.float32 and impl not in (0, 1):
+        pytest.skip("fp32 layers run on CUDA cores only")
+    _lib.set_gemm_impl(impl)
+    g = torch.Generator().manual_seed(21)
+    T, H, I = 300, 512, 384
+    h = torch.randn(T, I, generator=g).to(dtype).to(DEV)
+    w2 = (torch.randn(1, H, I, generator=g) * 0.05).to(dtype).to(DEV)
+    add = torch.randn(T, H, generator=g).to(dtype).to(DEV)
+    off, cnt = K.dense_segment(DEV, T)
+    y = torch.empty(T, H, dtype=dtype, device=DEV)
+    K.grouped_gemm_down(h, w2, off, cnt, y)
+    want = (add.float() + y.float()).to(dtype)
+    got = torch.empty_like(y)
+    K.grouped_gemm_down(h, w2, off, cnt, got, addend=add)
+    assert torch.equal(got, want)
+    inplace = add.clone()
+    K.grouped_gemm_down(h, w2, off, cnt, inplace, addend=inplace)
+    assert torch.equal(inplace, want)
 
 
 def test_grouped_gemm_slot_table_and_groups():

@@ -12,6 +12,9 @@ from reframework_b200.workloads import generate
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda")
+# tokens whose routed set differs from the golden fixture by a one-ulp logit tie,
+# as observed on B200 for every fixture (16-bit and fp32 routers alike)
+TIE_SWAPS_SEEN = 0
 
 
 @pytest.fixture(autouse=True)
@@ -68,7 +71,8 @@ def test_layer_matches_reference(name):
     rdt = None if (harness or cfg.dtype == torch.float32) else cfg.dtype
     logits_ref = O.router_logits(d["x"], d["gate"], bias=d["bias"][0] if harness and d["bias"] else None,
                                  fp32=harness)
-    bad = routing_mismatches(ids, rec["ids"], logits_ref, cfg.top_k, round_dtype=rdt, max_frac=0.05)
+    # no fixture has a tie-swapped token on B200 (measured): any swap fails
+    bad = routing_mismatches(ids, rec["ids"], logits_ref, cfg.top_k, round_dtype=rdt, max_count=TIE_SWAPS_SEEN)
     if harness or cfg.dtype == torch.float32:
         assert bad == [] and torch.equal(ids.cpu(), rec["ids"])
     keep = torch.ones(ids.shape[0], dtype=torch.bool)

@@ -230,10 +230,9 @@ def e2e_run(fwd, xh, steps, dev):
 # router x2 (tensor-core logits, top-k), permute x3 (histogram, scatter, gather), gated GEMM, down GEMM, combine
 LAUNCHES_PER_FORWARD = 8
 # EP, exchange planned on the device and carried over peer memory: router x2, permute x2 (histogram,
-# scatter), planner, dispatch push + wait, regroup gather, gated GEMM, down GEMM storing its rows into
-# the token ranks' return buffers + return wait, combine; NCCL's own kernels (the counts all-gather)
-# are not counted
-EP_LAUNCHES_PER_FORWARD = 12
+# scatter), counts push + collect, planner, dispatch push + wait, regroup gather, gated GEMM, down GEMM
+# storing its rows into the token ranks' return buffers + return wait, combine
+EP_LAUNCHES_PER_FORWARD = 14
 
 
 def ep_launches(layer) -> int:

@@ -38,6 +38,8 @@
  *   rf_moe_combine_rmsnorm  the same + the next RMSNorm (norm.py:27-53)
  *   rf_moe_ep_push_rows / rf_moe_ep_wait  reframework/parallel/dist.py:194-206
  *                           (EP dispatch / return all-to-all) as NVLink stores
+ *   rf_moe_ep_counts_push / _collect  the per-step counts all-gather
+ *                           (dist.py:186-191) as NVLink stores
  *   rf_moe_ep_plan / rf_moe_ep_pair_rows  the split of that exchange, replacing
  *                           the replicate-and-all-reduce forward of
  *                           reframework/parallel/ep.py:119-150
@@ -352,6 +354,25 @@ int rf_moe_ep_push_rows(const void *src, int64_t row_bytes, const int32_t *idx1,
                         const int64_t *dst_row0, void *const *dst, int32_t *const *flag, int32_t epoch,
                         uint32_t *done, rf_stream_t stream);
 int rf_moe_ep_wait(const int32_t *flags, int32_t R, int32_t epoch, rf_stream_t stream);
+
+/*
+ * The counts all-gather of the expert-parallel step (reframework/parallel/
+ * dist.py:186-191 as the token-dispatch layer uses it: every rank needs every
+ * rank's routed rows per expert) as one-sided NVLink stores.
+ * rf_moe_ep_counts_push: counts [E] (this rank's) into row `me` of every
+ *   rank's table, dst[d] = rank d's [R][E] int32 table for this step (peer
+ *   mappings or this rank's own), then flag[d] = rank d's counts flag word for
+ *   this rank is set to epoch (st.release.sys) once the rows are visible.
+ * rf_moe_ep_counts_collect: stream-ordered wait (bounded, 2 s) until
+ *   flags[0..R) all equal epoch, then out [R][E] = table.  A source whose flag
+ *   never arrives gets a zero row and sets RF_DEV_WAIT_TIMEOUT.
+ * Callers alternate two tables (by step parity) so that a rank one step ahead
+ * never writes the table a slower rank is reading.
+ */
+int rf_moe_ep_counts_push(const int32_t *counts, int32_t E, int32_t R, int32_t me, int32_t *const *dst,
+                          int32_t *const *flag, int32_t epoch, rf_stream_t stream);
+int rf_moe_ep_counts_collect(const int32_t *flags, const int32_t *table, int32_t R, int32_t E, int32_t epoch,
+                             int32_t *out, rf_stream_t stream);
 
 /*
  * The same exchange planned on the device (no host synchronisation per step).

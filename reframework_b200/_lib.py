@@ -74,6 +74,10 @@ _SIGNATURES = {
                                    _c_void_p, _c_void_p, _c_void_p, _c_void_p, ctypes.c_int32, _c_void_p,
                                    _c_void_p]),
     "rf_moe_ep_wait": (_int, [_c_void_p, ctypes.c_int32, ctypes.c_int32, _c_void_p]),
+    "rf_moe_ep_counts_push": (_int, [_c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_void_p,
+                                     _c_void_p, ctypes.c_int32, _c_void_p]),
+    "rf_moe_ep_counts_collect": (_int, [_c_void_p, _c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                        _c_void_p, _c_void_p]),
     "rf_moe_ep_devplan_workspace_size": (ctypes.c_size_t, [ctypes.c_int32] * 4),
     "rf_moe_ep_devplan_layout": (_int, [ctypes.c_int32] * 4 + [_c_void_p]),
     "rf_moe_ep_devplan": (_int, [_c_void_p, _c_void_p, _c_void_p] + [ctypes.c_int32] * 7 + [_i64, _i64, _i64, _c_void_p,

@@ -14,6 +14,11 @@
 //   rf_moe_ep_wait       one block: waits (ld.acquire.sys, bounded by 2 s of
 //       globaltimer) until every source's flag holds the epoch; on timeout it
 //       sets the device error word and returns instead of hanging.
+//   rf_moe_ep_counts_push / rf_moe_ep_counts_collect  the per-step exchange
+//       of the [R][E] routed-row counts the planner needs (the counts
+//       all-gather), as the same one-sided stores: each rank writes its row
+//       into every rank's table and raises a flag; each rank waits (bounded)
+//       for all R flags and copies its table out.
 // Ordering: a rank pushes into a peer's receive buffer for step n+1 only after
 // that peer's return push of step n reached it, and the peer issues that push
 // after it finished reading its receive buffer, so no buffer is overwritten
@@ -109,6 +114,51 @@ __global__ void wait_flags_kernel(const int32_t *flags, int R, int32_t epoch) {
   }
 }
 
+// One block: this rank's expert counts row into row `me` of every rank's
+// counts table (NVLink stores into the peers' control blocks), then, once all
+// of them are visible system-wide, this rank's counts flag in every rank.
+struct CountsPushArgs {
+  const int32_t *counts;  // [E] this rank's routed rows per expert
+  int R, me, E;
+  int32_t epoch;
+  int32_t *dst[MAX_RANKS];   // rank d's counts table [R][E] for this step
+  int32_t *flag[MAX_RANKS];  // rank d's counts flag word for this rank
+};
+
+__global__ void __launch_bounds__(256) counts_push_kernel(const __grid_constant__ CountsPushArgs a) {
+  for (int d = 0; d < a.R; ++d)
+    for (int e = threadIdx.x; e < a.E; e += blockDim.x) a.dst[d][(int64_t)a.me * a.E + e] = a.counts[e];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // every row stored above, seen by every GPU, before the flags
+    for (int d = 0; d < a.R; ++d) st_release_sys(a.flag[d], a.epoch);
+  }
+}
+
+// One block: warp w takes source rows w, w + 8, ...: every lane waits
+// (acquire, bounded) for that source's flag, then the lanes copy the row.
+__global__ void __launch_bounds__(256) counts_collect_kernel(const int32_t *flags, const int32_t *table, int R,
+                                                             int E, int32_t epoch, int32_t *out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < R; r += 8) {
+    bool ok = ld_acquire_sys(flags + r) == epoch;
+    if (!ok) {
+      const uint64_t t0 = rf::globaltimer_ns();
+      for (uint32_t it = 1; !ok; ++it) {
+        __nanosleep(64);
+        ok = ld_acquire_sys(flags + r) == epoch;
+        if (!ok && (it & 255) == 0 && rf::globaltimer_ns() - t0 > WAIT_LIMIT_NS) break;
+      }
+    }
+    if (!ok) {
+      if (lane == 0) rf_report(RF_DEV_WAIT_TIMEOUT);
+      for (int e = lane; e < E; e += 32) out[(int64_t)r * E + e] = 0;
+      continue;
+    }
+    for (int e = lane; e < E; e += 32) out[(int64_t)r * E + e] = table[(int64_t)r * E + e];
+  }
+}
+
 }  // namespace
 
 extern "C" int rf_moe_peer_alloc(size_t bytes, void **ptr, void *handle) {
@@ -197,4 +247,32 @@ extern "C" int rf_moe_ep_wait(const int32_t *flags, int32_t R, int32_t epoch, rf
   RF_CHECK_ARG(flags && R >= 1 && R <= MAX_RANKS, "rf_moe_ep_wait: bad arguments");
   wait_flags_kernel<<<1, 64, 0, (cudaStream_t)stream>>>(flags, R, epoch);
   return rf::check_launch("rf_moe_ep_wait");
+}
+
+extern "C" int rf_moe_ep_counts_push(const int32_t *counts, int32_t E, int32_t R, int32_t me, int32_t *const *dst,
+                                     int32_t *const *flag, int32_t epoch, rf_stream_t stream) {
+  RF_CHECK_ARG(R >= 1 && R <= MAX_RANKS && me >= 0 && me < R && E >= 1 && E <= 65535,
+               "rf_moe_ep_counts_push: 1 <= R <= 64, 0 <= me < R, 1 <= E <= 65535");
+  RF_CHECK_ARG(counts && dst && flag, "rf_moe_ep_counts_push: null pointer");
+  CountsPushArgs a;
+  a.counts = counts;
+  a.R = R;
+  a.me = me;
+  a.E = E;
+  a.epoch = epoch;
+  for (int d = 0; d < R; ++d) {
+    RF_CHECK_ARG(dst[d] && flag[d], "rf_moe_ep_counts_push: missing peer table or flag");
+    a.dst[d] = dst[d];
+    a.flag[d] = flag[d];
+  }
+  counts_push_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(a);
+  return rf::check_launch("rf_moe_ep_counts_push");
+}
+
+extern "C" int rf_moe_ep_counts_collect(const int32_t *flags, const int32_t *table, int32_t R, int32_t E,
+                                        int32_t epoch, int32_t *out, rf_stream_t stream) {
+  RF_CHECK_ARG(flags && table && out && R >= 1 && R <= MAX_RANKS && E >= 1 && E <= 65535,
+               "rf_moe_ep_counts_collect: bad arguments");
+  counts_collect_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(flags, table, R, E, epoch, out);
+  return rf::check_launch("rf_moe_ep_counts_collect");
 }

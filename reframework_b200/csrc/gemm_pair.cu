@@ -23,7 +23,7 @@
 //
 // Roles (one cluster of 2 CTAs per SM pair, persistent, 320 threads):
 //   warp 0      TMA producer (both CTAs): this CTA's weight rows and token
-//               rows per k-block into a 6-stage ring (128-byte swizzle, each
+//               rows into a 3-stage ring of 128-deep k-blocks (128-byte swizzle, each
 //               CTA copying only its own operands); the copies of both CTAs
 //               complete on the first CTA's stage barrier (.cta_group::2),
 //               which expects the bytes of both.
@@ -53,11 +53,16 @@ RF_DEVICE_ERROR_WORD();
 
 namespace {
 
+// Ring: 3 stages of two 64-deep sub-blocks (64 KB per CTA per stage).  Measured
+// on B200 at C2's shapes: the same 192 KB as 6 stages of one sub-block but one
+// barrier wait and one stage release per 8 MMAs instead of per 4, which was
+// worth 6 % on the gated GEMM (4, 5 or 6 single sub-block stages made no
+// difference: the loop is bound by per-stage work, not by copy latency).
 #ifndef RF_PAIR_KSUB
-#define RF_PAIR_KSUB 1
+#define RF_PAIR_KSUB 2
 #endif
 #ifndef RF_PAIR_STAGES
-#define RF_PAIR_STAGES 6
+#define RF_PAIR_STAGES 3
 #endif
 #ifndef RF_PAIR_EPI_SLEEP_NS
 #define RF_PAIR_EPI_SLEEP_NS 256
@@ -182,6 +187,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
+}
+// Non-blocking probe: has the phase of `parity` completed?
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
 // Named barrier over the epilogue warps that also ANDs a predicate.
 __device__ __forceinline__ bool epi_vote_and(int ok) {
@@ -393,6 +410,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       int stage = 0, it = 0;
       uint32_t phase = 0;
       bool ok = true;
+      bool ready = false;  // the stage about to be consumed was seen complete by the early probe
       for (int t = pair; t < total && ok; t += npairs, ++it) {
         int row0, ntok, fb, s;
         decode(t, row0, ntok, fb, s);
@@ -403,10 +421,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * 256);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!pwait(FULL(stage), phase, 0)) {
+          if (!ready && !pwait(FULL(stage), phase, 0)) {
             ok = false;
             break;
           }
+          // probe the next stage now, so that check overlaps this stage's MMA issue
+          ready = stage + 1 == P_STAGES ? mbar_test(FULL(0), phase ^ 1u) : mbar_test(FULL(stage + 1), phase);
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * P_A_BYTES);
           const uint32_t b0 = smem_u32(sB + stage * P_B_BYTES);

@@ -412,7 +412,8 @@ class EPFusedMoE(nn.Module):
     def _exchange(self):
         if self._px is None:
             from .p2p import PeerExchange
-            self._px = PeerExchange(self.ep_rank, self.ep_size, self.gate.device, self._pg())
+            self._px = PeerExchange(self.ep_rank, self.ep_size, self.gate.device, self._pg(),
+                                    num_experts=self.num_experts)
         return self._px
 
     def close(self) -> None:
@@ -614,8 +615,8 @@ class EPFusedMoE(nn.Module):
 
     def _forward_devplan(self, x2, res2, p, w, sscale, counts) -> torch.Tensor:
         """The EP forward with the exchange planned on the device: counts
-        all-gather (device), planner kernel, peer pushes, bounded waits — no
-        host synchronisation in the step."""
+        exchange over peer memory, planner kernel, peer pushes, bounded waits —
+        no collective and no host synchronisation in the step."""
         import ctypes
         from .p2p import DISPATCH, RETURN
         dev = x2.device
@@ -624,17 +625,17 @@ class EPFusedMoE(nn.Module):
         row_bytes = H * x2.element_size()
         stt, px = self._devplan_state(T, row_bytes)
         S, nslots, ws = stt["S"], stt["nslots"], stt["ws"]
-        cnt = torch.empty(R, E, dtype=torch.int32, device=dev)
-        tdist.all_gather_into_tensor(cnt, counts.contiguous(), group=self._pg())
+        epoch = px.next_epoch()
+        # counts all-gather as peer stores + a bounded flag wait (no collective)
+        cnt = px.exchange_counts(counts.contiguous(), epoch)
         self.last_counts_dev, self.last_counts, self.last_plan = cnt, None, None
-        self._mark("counts all_gather")
+        self._mark("counts exchange")
         st = stream_of(dev)
         check(lib().rf_moe_ep_devplan(cnt.data_ptr(), stt["flat"].data_ptr(), stt["offs"].data_ptr(), R, E,
                                       self.ep_rank, S, nslots, K.ALIGN, self.split_rounds, stt["recv_cap"],
                                       stt["back_cap"], stt["rows_cap"], ws.data_ptr(), ws.numel(), st),
               "rf_moe_ep_devplan")
         self._mark("device plan")
-        epoch = px.next_epoch()
         ctrl = px.peer[2]
         flags0 = (ctypes.c_void_p * R)(*[ctrl[d] + 4 * (DISPATCH * R + self.ep_rank) for d in range(R)])
         flags1 = (ctypes.c_void_p * R)(*[ctrl[d] + 4 * (RETURN * R + self.ep_rank) for d in range(R)])

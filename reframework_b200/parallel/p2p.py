@@ -7,6 +7,7 @@ block of flag words, allocated with CUDA IPC by the rf_moe library and mapped
 by every peer.  ``push`` copies this rank's rows straight into the peers'
 buffers (one kernel, folding in the row gather) and raises this rank's flag in
 every peer; ``wait`` is a stream-ordered, bounded wait for all sources' flags.
+``exchange_counts`` carries the per-step counts all-gather the same way.
 
 Buffer growth is collective: every rank derives the same needed capacity from
 the step's all-to-all matrix, so all ranks grow (and re-exchange handles) in
@@ -51,16 +52,21 @@ class PeerExchange:
 
     GROWTH = 1.25
 
-    def __init__(self, rank: int, world: int, device: torch.device, group=None):
+    def __init__(self, rank: int, world: int, device: torch.device, group=None, num_experts: int = 0):
         if world > 64:
             raise ValueError("peer exchange supports at most 64 ranks")
         self.rank, self.world, self.device, self.group = rank, world, device, group
+        self.num_experts = int(num_experts)
         self.epoch = 0
         self.row_bytes = 0
         self.recv_rows = self.back_rows = 0
         self.own: List[Optional[_Buf]] = [None, None, None]  # recv, back, ctrl
         self.peer: List[List[int]] = [[0] * world for _ in range(3)]
-        self._ctrl_bytes = (2 * world * 4 + 4 + 15) // 16 * 16
+        # control block: dispatch / return flags [2R], the push kernels' block
+        # counter, counts flags [R]; then two [R][E] counts tables (step parity)
+        self._counts_flags_off = (2 * world + 1) * 4
+        self._counts_off = ((3 * world + 1) * 4 + 15) // 16 * 16
+        self._ctrl_bytes = self._counts_off + 2 * world * max(self.num_experts, 1) * 4
 
     # ------------------------------------------------------------ buffers
     def ensure(self, recv_rows: int, back_rows: int, row_bytes: int) -> None:
@@ -139,6 +145,22 @@ class PeerExchange:
             None if idx1 is None else idx1.data_ptr(), None if idx2 is None else idx2.data_ptr(), int(div),
             R, self.rank, c_off, c_row0, c_dst, c_flag, self.epoch, done, stream_of(self.device))
         check(rc, "rf_moe_ep_push_rows")
+
+    def exchange_counts(self, counts: torch.Tensor, epoch: int) -> torch.Tensor:
+        """The step's counts all-gather over peer memory: this rank's routed
+        rows per expert (int32 [E], device) into every rank's table, then a
+        bounded wait for every rank's row; returns the [R, E] table (device)."""
+        R, E = self.world, self.num_experts
+        st = stream_of(self.device)
+        toff = self._counts_off + (epoch & 1) * R * E * 4
+        dst = (ctypes.c_void_p * R)(*[self.peer[2][d] + toff for d in range(R)])
+        flag = (ctypes.c_void_p * R)(*[self.peer[2][d] + self._counts_flags_off + 4 * self.rank for d in range(R)])
+        check(lib().rf_moe_ep_counts_push(counts.data_ptr(), E, R, self.rank, dst, flag, epoch, st),
+              "rf_moe_ep_counts_push")
+        out = torch.empty(R, E, dtype=torch.int32, device=self.device)
+        check(lib().rf_moe_ep_counts_collect(self.own[2].ptr + self._counts_flags_off, self.own[2].ptr + toff, R, E,
+                                             epoch, out.data_ptr(), st), "rf_moe_ep_counts_collect")
+        return out
 
     def wait(self, direction: int) -> None:
         flags = self.own[2].ptr + direction * self.world * 4

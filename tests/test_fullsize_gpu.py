@@ -199,7 +199,20 @@ def _emulated_ep_forward(moe, x, R, placement):
     for lo, hi in bounds:
         w, ids32, _, _, sscale = moe._router(x[lo:hi].contiguous(), ids32=True, ids64=False)
         routed.append((w, ids32, sscale, K.permute(ids32, E, align=1)))
+    # the counts all-gather through the peer-store kernels: every rank's row into
+    # every rank's table, then each rank's bounded collect
     cnt = torch.stack([r[3].counts for r in routed]).contiguous()
+    tables = [torch.zeros(R, E, dtype=torch.int32, device=DEV) for _ in range(R)]
+    cflags = [torch.zeros(R, dtype=torch.int32, device=DEV) for _ in range(R)]
+    for me in range(R):
+        assert L.rf_moe_ep_counts_push(routed[me][3].counts.data_ptr(), E, R, me,
+                                       (ctypes.c_void_p * R)(*[t.data_ptr() for t in tables]),
+                                       (ctypes.c_void_p * R)(*[f.data_ptr() + 4 * me for f in cflags]), 3, st) == 0
+    for me in range(R):
+        got = torch.empty(R, E, dtype=torch.int32, device=DEV)
+        assert L.rf_moe_ep_counts_collect(cflags[me].data_ptr(), tables[me].data_ptr(), R, E, 3, got.data_ptr(),
+                                          st) == 0
+        assert torch.equal(got, cnt), f"rank {me}: collected counts table differs"
     flat = torch.tensor([e for s in placement.slots for e in s], dtype=torch.int32, device=DEV)
     offs = torch.tensor(np.cumsum([0] + [len(s) for s in placement.slots]), dtype=torch.int32, device=DEV)
     nslots = int(flat.numel())

@@ -190,6 +190,9 @@ int rf_moe_permute(const int32_t *topk_ids, int64_t T, int64_t K, int64_t E, int
  * call before any stream capture.  The address is kept per device ordinal
  * for the life of the process: it does not survive cudaDeviceReset (or any
  * other teardown of the device's primary context), after which this entry
+ * point must not be called again in that process.  The address is kept per device ordinal
+ * for the life of the process: it does not survive cudaDeviceReset (or any
+ * other teardown of the device's primary context), after which this entry
  * point must not be called again in that process.  All calls share the one array, which keeps
  * the last call's contents (nothing in it needs to start at zero: each call
  * overwrites the words it reads), so calls that overlap on the same GPU —

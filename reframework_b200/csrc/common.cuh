@@ -116,6 +116,18 @@ __device__ __forceinline__ float act_gate(int act, float g) {
   return act_gate_t<RF_ACT_GELU_TANH>(g);
 }
 
+// The gated activation in IEEE fp32 (reframework/layers/activation.py:15-46
+// on fp32 tensors): every operation correctly rounded, CUDA's expf / erff /
+// tanhf for the transcendental parts.  Used by the int8 expert split.
+__device__ __forceinline__ float act_ieee(int act, float g) {
+  if (act == RF_ACT_SILU) return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+  if (act == RF_ACT_GELU)
+    return __fmul_rn(__fmul_rn(g, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn(g, 0.70710678118654752f))));
+  const float cube = __fmul_rn(__fmul_rn(g, g), g);
+  const float inner = __fmul_rn(0.7978845608028654f, __fadd_rn(g, __fmul_rn(0.044715f, cube)));
+  return __fmul_rn(__fmul_rn(g, 0.5f), __fadd_rn(1.0f, tanhf(inner)));
+}
+
 // Round an fp32 value to the storage type T and back (identity for fp32).
 template <typename T>
 __device__ __forceinline__ float round_to(float v) {

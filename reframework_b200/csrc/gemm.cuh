@@ -63,6 +63,15 @@ bool tma_encode(CUtensorMap *m, int dtype, int rank, const void *base, const cuu
 // The GEMM implementation chosen by rf_moe_set_gemm_impl (0 = automatic).
 int gemm_impl();
 
+// The expert split's int8 grouped GEMMs on the tensor cores (gemm_tc.cu,
+// tcgen05 kind::i8); -1 when the shape is not handled there (the caller runs
+// its CUDA-core kernel), else a status.
+int tc_int8_grouped_gemm(const int8_t *a, const int8_t *w, const int32_t *offsets, const int32_t *counts,
+                         const int32_t *groups, const int32_t *slot, int n_groups, int E, int num_slots,
+                         int64_t rows_capacity, int64_t Kdim, int64_t N, const float *a_scales,
+                         const float *w_scales, int64_t w_stride, bool gated, int act, float *out, float *amax,
+                         const float *row_w, const int32_t *src_slot, cudaStream_t st);
+
 // The grouped GEMM of `g` on CTA pairs (gemm_pair.cu): weight rows on the
 // MMA's M side (256 per pair), token rows on N in steps of 16.  -1 when the
 // shape, dtype or device does not suit it, else a status.

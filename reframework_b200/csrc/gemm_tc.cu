@@ -93,15 +93,35 @@ struct TcArgs {
   const int32_t *gather_src;
   int gather_div;
   const void *addend;  // down only: out = round(addend + round(acc)); may be NULL or out
+  // int8 mode (T = int8_t, kind::i8, exact int32 sums; the expert split):
+  // dequantize with a_scales[listed position] * w_scales[expert * w_stride];
+  // gated: fp32 act(g) * u, per-listed-expert max |.| into i8_amax; down:
+  // times the routing weight row_w[src_slot[row]]; fp32 output rows
+  const float *i8_as, *i8_ws;
+  int64_t i8_wstride;
+  float *i8_amax;
+  const float *i8_rw;
+  const int32_t *i8_src;
 };
 
 // Instruction descriptor of kind::f16: fp32 accumulator, A/B K-major,
 // M = 128, N = BN; operand format 0 = f16, 1 = bf16 (A and B always equal).
 template <typename T, int BN>
 __host__ __device__ constexpr uint32_t instr_desc() {
+  if constexpr (std::is_same<T, int8_t>::value)  // kind::i8: s32 accumulator, signed 8-bit A and B
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   return (1u << 4) | ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 7) |
          ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 10) | ((uint32_t)(BN >> 3) << 17) |
          ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 struct NoRemote {};
@@ -121,6 +141,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const __grid_constant__ CUtensorMap tmB, const TcArgs p,
                     const __grid_constant__ std::conditional_t<REMOTE, rf::RemoteOut, NoRemote> ro) {
   static_assert(!REMOTE || (!GATED && !OUTF32 && !GATHER), "remote stores: plain down GEMM only");
+  constexpr bool I8 = std::is_same<T, int8_t>::value;
+  static_assert(!I8 || (!OUTF32 && !GATHER && !REMOTE), "int8 mode: grouped gated / down only");
+  constexpr int BKE = I8 ? 2 * BK : BK;  // k-block depth in elements: 128 bytes of a row either way
   using C = Cfg<BN_>;
   constexpr int BN = C::BN, STAGES = C::STAGES, B_BYTES = C::B_BYTES, STAGE_BYTES = C::STAGE_BYTES;
   constexpr int NUM_BARS = C::NUM_BARS;
@@ -209,10 +232,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int total = tile_prefix[G];
-  const int num_kb = (p.Kdim + BK - 1) / BK;
+  const int num_kb = (p.Kdim + BKE - 1) / BKE;
 
   // tile -> (group, n-block, m-block); groups with zero tiles are skipped by
   // taking the last group whose prefix is <= t
+  int gi = 0;  // group of the tile decode() last looked at
   auto decode = [&](int t, int &row0, int &rows, int &nb, int &s) {
     int lo = 0, hi = G - 1;
     while (lo < hi) {
@@ -228,6 +252,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     row0 = g_row0[lo] + mb * BM;
     rows = min(BM, cnt - mb * BM);
     s = g_slot[lo];
+    gi = lo;
   };
 
   if (warp == 0) {
@@ -271,12 +296,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t a_bytes =
               GATHER ? (uint32_t)groups4 * 512u : (small ? (uint32_t)(A_BYTES / (BM / BM_SMALL)) : (uint32_t)A_BYTES);
           mbar_expect_tx(FULL(stage), a_bytes + (uint32_t)B_BYTES);
-          if (!GATHER) tma_load_2d(a_dst, small ? &tmA32 : &tmA, FULL(stage), kb * BK, row0);
+          if (!GATHER) tma_load_2d(a_dst, small ? &tmA32 : &tmA, FULL(stage), kb * BKE, row0);
           if (GATED) {
-            tma_load_3d(b_dst, &tmB, FULL(stage), kb * BK, nb * (BN / 2), 2 * s);
-            tma_load_3d(b_dst + B_BYTES / 2, &tmB, FULL(stage), kb * BK, nb * (BN / 2), 2 * s + 1);
+            tma_load_3d(b_dst, &tmB, FULL(stage), kb * BKE, nb * (BN / 2), 2 * s);
+            tma_load_3d(b_dst + B_BYTES / 2, &tmB, FULL(stage), kb * BKE, nb * (BN / 2), 2 * s + 1);
           } else {
-            tma_load_3d(b_dst, &tmB, FULL(stage), kb * BK, nb * BN, s);
+            tma_load_3d(b_dst, &tmB, FULL(stage), kb * BKE, nb * BN, s);
           }
         }
         if (GATHER) {
@@ -320,9 +345,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
           const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            tc_mma(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC,
-                   (kb | k) ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) {  // 32-byte steps: K = 16 (16-bit) or 32 (int8) per MMA
+            if constexpr (I8)
+              tc_mma_i8(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC, (kb | k) ? 1u : 0u);
+            else
+              tc_mma(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC, (kb | k) ? 1u : 0u);
+          }
           tc_commit(EMPTY(stage));  // frees the stage once these MMAs have read it
           if (++stage == STAGES) {
             stage = 0;
@@ -370,7 +398,46 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           orow = reinterpret_cast<T *>(ro.dst[lo]) + (ro.ps[(int64_t)lo * ro.S + s] + (k - cj[lo])) * p.out_ld;
         }
       }
-      if (GATED) {
+      if constexpr (I8) {
+        const int e = p.groups ? p.groups[gi] : gi;
+        const float dq = __fmul_rn(p.i8_as[gi], p.i8_ws[(int64_t)e * p.i8_wstride]);
+        float *orowf = reinterpret_cast<float *>(p.out) + (int64_t)(row0 + r) * p.out_ld;
+        const float rw = (!GATED && row_ok) ? p.i8_rw[p.i8_src[row0 + r]] : 0.f;
+        float m = 0.f;
+        const int n0 = GATED ? nb * (BN / 2) : nb * BN;
+#pragma unroll 1
+        for (int c = part * 32; c < (GATED ? BN / 2 : BN); c += 32 * EPI_SPLIT) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tb + c, g);
+          if (GATED) tmem_ld32(tb + BN / 2 + c, u);
+          tmem_ld_wait();
+          if (row_ok) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const int col = n0 + c + 4 * v;
+              if (col >= p.N) continue;
+              float o[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float gf = __fmul_rn(__int2float_rn((int)g[4 * v + i]), dq);
+                if (GATED) {
+                  const float uf = __fmul_rn(__int2float_rn((int)u[4 * v + i]), dq);
+                  o[i] = __fmul_rn(rf::act_ieee(ACT, gf), uf);
+                  m = fmaxf(m, fabsf(o[i]));
+                } else {
+                  o[i] = __fmul_rn(gf, rw);
+                }
+              }
+              *reinterpret_cast<float4 *>(orowf + col) = make_float4(o[0], o[1], o[2], o[3]);
+            }
+          }
+        }
+        if (GATED) {  // per listed expert max |inter| (non-negative floats order like their bits)
+#pragma unroll
+          for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (lane == 0 && m > 0.f) atomicMax(reinterpret_cast<int *>(p.i8_amax) + gi, __float_as_int(m));
+        }
+      } else if (GATED) {
         const int n0 = nb * (BN / 2);
 #pragma unroll 1
         for (int c = part * 32; c < BN / 2; c += 32 * EPI_SPLIT) {
@@ -505,8 +572,9 @@ bool encode(CUtensorMap *m, int dtype, int rank, const void *base, const cuuint6
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint32_t estr[3] = {1, 1, 1};
-  const CUtensorMapDataType dt =
-      dtype == RF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType dt = dtype == RF_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : dtype == RF_F16  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_UINT8;  // int8 codes: plain bytes
   CUresult r = fn(m, dt, (cuuint32_t)rank, const_cast<void *>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -725,6 +793,79 @@ int tc_dense_f32(const void *a, const void *w, float *out, int64_t M, int64_t N,
   if (bn == 64) return launch_dense<__half, 64>(ma, ma32, mb, p, M, st);
   if (bn == 128) return launch_dense<__half, 128>(ma, ma32, mb, p, M, st);
   return launch_dense<__half, 256>(ma, ma32, mb, p, M, st);
+}
+
+// The int8 grouped GEMMs of the expert split on the tensor cores
+// (tcgen05.mma kind::i8, exact int32 sums), same contract as the CUDA-core
+// kernel of int8_split.cu; -1 when the shape is not handled here.
+int tc_int8_grouped_gemm(const int8_t *a, const int8_t *w, const int32_t *offsets, const int32_t *counts,
+                         const int32_t *groups, const int32_t *slot, int n_groups, int E, int num_slots,
+                         int64_t rows_capacity, int64_t Kdim, int64_t N, const float *a_scales,
+                         const float *w_scales, int64_t w_stride, bool gated, int act, float *out, float *amax,
+                         const float *row_w, const int32_t *src_slot, cudaStream_t st) {
+  if (g_gemm_impl == 1) return -1;
+  if (Kdim % 16 || N % 8 || n_groups < 1 || n_groups > MAX_GROUPS || rows_capacity < 1 ||
+      rows_capacity >= ((int64_t)1 << 31) || Kdim >= (1 << 30) || N >= (1 << 30))
+    return -1;
+  if ((uintptr_t)a % 16 || (uintptr_t)w % 16 || (uintptr_t)out % 16) return -1;
+  if (!encode_fn()) return -1;
+  constexpr int I8D = -1;  // encode(): any code other than the 16-bit ones maps to 8-bit bytes
+  const int64_t groups_est = std::max(1, n_groups);
+  const int bn = rows_capacity - groups_est * (BM - 1) < groups_est * 64 ? 128 : 256;
+  CUtensorMap ma, ma32, mb;
+  const cuuint64_t dA[2] = {(cuuint64_t)Kdim, (cuuint64_t)rows_capacity};
+  const cuuint64_t sAs[1] = {(cuuint64_t)Kdim};
+  const cuuint32_t bA[2] = {2 * BK, BM};
+  const cuuint32_t bA32[2] = {2 * BK, BM_SMALL};
+  bool ok = encode(&ma, I8D, 2, a, dA, sAs, bA) && encode(&ma32, I8D, 2, a, dA, sAs, bA32);
+  if (gated) {
+    const cuuint64_t dB[3] = {(cuuint64_t)Kdim, (cuuint64_t)N, (cuuint64_t)(2 * num_slots)};
+    const cuuint64_t sB[2] = {(cuuint64_t)Kdim, (cuuint64_t)N * Kdim};
+    const cuuint32_t bB[3] = {2 * BK, (cuuint32_t)(bn / 2), 1};
+    ok = ok && encode(&mb, I8D, 3, w, dB, sB, bB);
+  } else {
+    const cuuint64_t dB[3] = {(cuuint64_t)Kdim, (cuuint64_t)N, (cuuint64_t)num_slots};
+    const cuuint64_t sB[2] = {(cuuint64_t)Kdim, (cuuint64_t)N * Kdim};
+    const cuuint32_t bB[3] = {2 * BK, (cuuint32_t)bn, 1};
+    ok = ok && encode(&mb, I8D, 3, w, dB, sB, bB);
+  }
+  if (!ok) return -1;
+  TcArgs p{};
+  p.offsets = offsets;
+  p.counts = counts;
+  p.slot = slot;
+  p.groups = groups;
+  p.n_groups = n_groups;
+  p.E = E;
+  p.num_slots = num_slots;
+  p.Kdim = (int)Kdim;
+  p.N = (int)N;
+  p.n_tiles_n = gated ? (int)((N + bn / 2 - 1) / (bn / 2)) : (int)((N + bn - 1) / bn);
+  p.out = out;
+  p.out_ld = N;
+  p.act = act;
+  p.i8_as = a_scales;
+  p.i8_ws = w_scales;
+  p.i8_wstride = w_stride;
+  p.i8_amax = amax;
+  p.i8_rw = row_w;
+  p.i8_src = src_slot;
+  auto go = [&](auto kern, size_t smem) -> int {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return rf::fail(RF_ERR_CUDA, std::string("int8 tensor-core GEMM: ") + cudaGetErrorString(e));
+    kern<<<rf::num_sms(), NTHREADS, smem, st>>>(ma, ma32, mb, p, NoRemote{});
+    return rf::check_launch(gated ? "int8 tensor-core gated GEMM" : "int8 tensor-core down GEMM");
+  };
+  if (bn == 256) {
+    if (!gated) return go(tc_grouped_gemm<int8_t, false, 0, 256>, Cfg<256>::SMEM_BYTES);
+    if (act == RF_ACT_SILU) return go(tc_grouped_gemm<int8_t, true, RF_ACT_SILU, 256>, Cfg<256>::SMEM_BYTES);
+    if (act == RF_ACT_GELU) return go(tc_grouped_gemm<int8_t, true, RF_ACT_GELU, 256>, Cfg<256>::SMEM_BYTES);
+    return go(tc_grouped_gemm<int8_t, true, RF_ACT_GELU_TANH, 256>, Cfg<256>::SMEM_BYTES);
+  }
+  if (!gated) return go(tc_grouped_gemm<int8_t, false, 0, 128>, Cfg<128>::SMEM_BYTES);
+  if (act == RF_ACT_SILU) return go(tc_grouped_gemm<int8_t, true, RF_ACT_SILU, 128>, Cfg<128>::SMEM_BYTES);
+  if (act == RF_ACT_GELU) return go(tc_grouped_gemm<int8_t, true, RF_ACT_GELU, 128>, Cfg<128>::SMEM_BYTES);
+  return go(tc_grouped_gemm<int8_t, true, RF_ACT_GELU_TANH, 128>, Cfg<128>::SMEM_BYTES);
 }
 
 int tc_down_remote(const GroupedGemmArgs &g, cudaStream_t st) {

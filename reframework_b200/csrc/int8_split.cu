@@ -12,13 +12,14 @@
 //     y = float(iq . w2q[e]^T) * (is * s2[e]) * w (routing weight)    (int8_grouped_gemm, down)
 //   out[t] = (sum of the resident experts' rows, reference rounding in the
 //             layer dtype) + (sum of the int8 rows in fp32), rounded once  (split_combine)
-// The int8 GEMMs accumulate exactly in int32 (dp4a), so they equal
-// torch._int_mm bit for bit; the activation uses IEEE fp32 division with
+// The int8 GEMMs accumulate exactly in int32 (tcgen05.mma kind::i8 on the
+// tensor cores, gemm_tc.cu; dp4a on CUDA cores for shapes TMA cannot
+// describe), so they equal torch._int_mm bit for bit; the activation uses IEEE fp32 division with
 // CUDA's expf / erff / tanhf, within an ulp or two of torch's CPU kernels.
 // The work is bound by the PCIe copy of the int8 weights, not by these kernels.
 #include <string>
 
-#include "common.cuh"
+#include "gemm.cuh"
 
 RF_DEVICE_ERROR_WORD();
 
@@ -155,16 +156,7 @@ struct GemmArgs {
   const int32_t *src_slot;  // down: slot of each permuted row
 };
 
-// The gated activation in IEEE fp32 (reframework/layers/activation.py:15-46
-// on fp32 tensors).
-__device__ __forceinline__ float act_ieee(int act, float g) {
-  if (act == RF_ACT_SILU) return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-  if (act == RF_ACT_GELU)
-    return __fmul_rn(__fmul_rn(g, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn(g, 0.70710678118654752f))));
-  const float cube = __fmul_rn(__fmul_rn(g, g), g);
-  const float inner = __fmul_rn(0.7978845608028654f, __fadd_rn(g, __fmul_rn(0.044715f, cube)));
-  return __fmul_rn(__fmul_rn(g, 0.5f), __fadd_rn(1.0f, tanhf(inner)));
-}
+using rf::act_ieee;
 
 template <bool GATED>
 __global__ void __launch_bounds__(256) int8_gemm_kernel(const GemmArgs p) {
@@ -319,9 +311,14 @@ extern "C" int rf_moe_int8_grouped_gemm(const int8_t *a, const int8_t *w, const 
   p.row_w = row_weights;
   p.src_slot = src_slot;
   const int grid = rf::num_sms() * 4;
+  if (gated && cudaMemsetAsync(amax_out, 0, sizeof(float) * (size_t)n_groups, st) != cudaSuccess)
+    return rf::check_launch("rf_moe_int8_grouped_gemm (amax reset)");
+  // the tensor cores (kind::i8) when the shape allows; the dp4a kernel below otherwise
+  const int tc = rf::tc_int8_grouped_gemm(a, w, offsets, counts, groups, slot, n_groups, E, num_slots, rows_capacity,
+                                          Kdim, N, a_scales, w_scales, w_scale_stride, gated != 0, act, out, amax_out,
+                                          row_weights, src_slot, st);
+  if (tc >= 0) return tc;
   if (gated) {
-    if (cudaMemsetAsync(amax_out, 0, sizeof(float) * (size_t)n_groups, st) != cudaSuccess)
-      return rf::check_launch("rf_moe_int8_grouped_gemm (amax reset)");
     int8_gemm_kernel<true><<<grid, 256, 0, st>>>(p);
   } else {
     int8_gemm_kernel<false><<<grid, 256, 0, st>>>(p);

@@ -322,6 +322,9 @@ static __device__ __align__(256) int32_t g_noalloc_block_counts[kNoAllocScratchW
 // given this address instead.  The cache is keyed by device ordinal and lives
 // as long as the process: after cudaDeviceReset the module may load at
 // another address, so the header tells callers not to use this entry point
+// past a reset.  The cache is keyed by device ordinal and lives
+// as long as the process: after cudaDeviceReset the module may load at
+// another address, so the header tells callers not to use this entry point
 // past a reset.
 int noalloc_scratch(int32_t **out) {
   static std::mutex mu;

@@ -56,6 +56,42 @@ def test_int8_gemm_is_exact(Kdim, N, counts):
         assert torch.equal(out[r0:r0 + counts[e]], ref), f"expert {e}"
 
 
+@pytest.mark.parametrize("gated", [True, False])
+@pytest.mark.parametrize("act", ["silu", "gelu_tanh"])
+@pytest.mark.parametrize("Kdim,N,counts", [(1024, 352, [300, 0, 17, 129]), (272, 200, [130, 1, 0, 64])])
+def test_int8_tensor_core_gemm_equals_dp4a(gated, act, Kdim, N, counts):
+    """tcgen05.mma kind::i8 (exact int32 sums in TMEM) and the dp4a CUDA-core
+    kernel give the same bits: same int32 sums, the same fp32 scale products,
+    activation and routing weight, and (gated) the same per-expert max."""
+    g = torch.Generator().manual_seed(Kdim * 3 + N + gated)
+    E = len(counts)
+    offs, cnt, rows = _segments(counts)
+    a = torch.randint(-127, 128, (rows, Kdim), generator=g, dtype=torch.int8).to(DEV)
+    w = torch.randint(-127, 128, (E + 1, (2 if gated else 1) * N, Kdim), generator=g, dtype=torch.int8).to(DEV)
+    slot = torch.tensor([(e + 1) % (E + 1) for e in range(E)], dtype=torch.int32).to(DEV)
+    groups = torch.tensor([e for e in range(E) if counts[e]][::-1], dtype=torch.int32).to(DEV)
+    a_sc = (torch.rand(len(groups), generator=g) * 1e-3 + 1e-4).to(DEV)
+    w_sc = (torch.rand(E, generator=g) * 1e-3 + 1e-4).to(DEV)
+    rw = torch.rand(rows, generator=g).to(DEV)
+    src = torch.randperm(rows, generator=g).to(torch.int32).to(DEV)
+    res = []
+    for impl in (0, 1):  # 0: tensor cores where the shape allows, 1: CUDA cores only
+        _lib.set_gemm_impl(impl)
+        out = torch.full((rows, N), float("nan"), device=DEV)
+        amax = torch.zeros(len(groups), device=DEV)
+        K.int8_grouped_gemm(a, w, offs.to(DEV), cnt.to(DEV), groups, slot, a_sc, w_sc, 1, out, gated=gated,
+                            activation=act, amax_out=amax if gated else None,
+                            row_weights=None if gated else rw, src_slot=None if gated else src)
+        res.append((out.cpu(), amax.cpu()))
+    _lib.set_gemm_impl(0)
+    for e in range(E):
+        r0 = int(offs[e])
+        seg = slice(r0, r0 + counts[e])
+        assert torch.equal(res[0][0][seg], res[1][0][seg]), f"expert {e}"
+    if gated:
+        assert torch.equal(res[0][1], res[1][1])
+
+
 def test_int8_quantize_matches_the_reference_quantizer():
     g = torch.Generator().manual_seed(1)
     counts = [40, 0, 3, 129]

@@ -78,9 +78,11 @@ int tc_int8_grouped_gemm(const int8_t *a, const int8_t *w, const int32_t *offset
 int launch_pair_grouped_gemm(const GroupedGemmArgs &g, bool gated, cudaStream_t st);
 
 // Dense out[M, ld_out] (fp32) = a[M, K] . w[N, K]^T on the tensor cores
-// (gemm_tc.cu); -1 when the shape or dtype is not handled there.
+// (gemm_tc.cu); -1 when the shape or dtype is not handled there.  With
+// slice_k > 0 (a multiple of 64) K is cut into ceil(K / slice_k) fixed slices
+// and slice j's sums go to out + j * M * ld_out (the caller adds them).
 int tc_dense_f32(const void *a, const void *w, float *out, int64_t M, int64_t N, int64_t Kdim,
-                 int64_t ld_out, int dtype, cudaStream_t st);
+                 int64_t ld_out, int dtype, cudaStream_t st, int64_t slice_k = 0);
 
 // The down GEMM of `g` (g.remote set) on the tensor cores, launched even when
 // no row is routed (the flags must rise); -1 when the shape or dtype is not

@@ -82,6 +82,11 @@ struct TcArgs {
   const int32_t *offsets, *counts, *slot, *groups;  // offsets == counts == NULL: one dense group
   int n_groups, E, num_slots;
   int dense_rows; // rows of the dense group
+  // dense fp32-output mode: K cut into k_slices fixed slices of kb_per_slice
+  // k-blocks, one tile each, slice j's sums written at out + j * slice_stride
+  // (0 or 1 = no slicing)
+  int k_slices, kb_per_slice;
+  int64_t slice_stride;
   int Kdim;       // reduction length
   int N;          // output columns
   int n_tiles_n;  // n-blocks per expert
@@ -231,8 +236,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  const int total = tile_prefix[G];
+  const int base_total = tile_prefix[G];
+  const int nsl = p.k_slices > 1 ? p.k_slices : 1;
+  const int total = base_total * nsl;
   const int num_kb = (p.Kdim + BKE - 1) / BKE;
+  const int kps = nsl > 1 ? p.kb_per_slice : num_kb;
+  // tile t -> (tile of the group table, its k-block range, output offset)
+  auto kspan = [&](int t, int &tt, int &kb0, int &kb1, int64_t &obase) {
+    const int sl = nsl > 1 ? t / base_total : 0;
+    tt = t - sl * base_total;
+    kb0 = sl * kps;
+    kb1 = min(num_kb, kb0 + kps);
+    obase = (int64_t)sl * p.slice_stride;
+  };
 
   // tile -> (group, n-block, m-block); groups with zero tiles are skipped by
   // taking the last group whose prefix is <= t
@@ -266,8 +282,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     bool ok = true;
     // without gather only lane 0 works (no per-k-block warp shuffle)
     for (int t = blockIdx.x; t < total && ok && (GATHER || lane == 0); t += gridDim.x) {
-      int row0, rows, nb, s;
-      decode(t, row0, rows, nb, s);
+      int row0, rows, nb, s, tt, kb0, kb1;
+      int64_t obase;
+      kspan(t, tt, kb0, kb1, obase);
+      decode(tt, row0, rows, nb, s);
       int src[4] = {0, 0, 0, 0};
       int groups4 = 0;
       if (GATHER) {
@@ -279,7 +297,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           src[j] = sl >= 0 ? sl / p.gather_div : 0;  // pad rows read token 0; never stored
         }
       }
-      for (int kb = 0; kb < num_kb; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         int go = 1;
         if (lane == 0) go = mbar_wait(EMPTY(stage), phase ^ 1u, abort_flag) ? 1 : 0;
         if constexpr (GATHER) go = __shfl_sync(0xffffffffu, go, 0);
@@ -331,12 +349,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool ok = true;
       int it = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+        int tt, kb0, kb1;
+        int64_t obase;
+        kspan(t, tt, kb0, kb1, obase);
         const int acc = it & 1;
         const uint32_t aph = (uint32_t)((it >> 1) & 1);
         if (!mbar_wait(TEMPTY(acc), aph ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(FULL(stage), phase, abort_flag)) {
             ok = false;
             break;
@@ -347,9 +368,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 32-byte steps: K = 16 (16-bit) or 32 (int8) per MMA
             if constexpr (I8)
-              tc_mma_i8(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC, (kb | k) ? 1u : 0u);
+              tc_mma_i8(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC, (kb != kb0 || k) ? 1u : 0u);
             else
-              tc_mma(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC, (kb | k) ? 1u : 0u);
+              tc_mma(d, sw128_desc(a0 + k * 32), sw128_desc(b0 + k * 32), IDESC, (kb != kb0 || k) ? 1u : 0u);
           }
           tc_commit(EMPTY(stage));  // frees the stage once these MMAs have read it
           if (++stage == STAGES) {
@@ -371,8 +392,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     T *out = reinterpret_cast<T *>(p.out);
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
-      int row0, rows, nb, s;
-      decode(t, row0, rows, nb, s);
+      int row0, rows, nb, s, tt, kb0, kb1;
+      int64_t obase;
+      kspan(t, tt, kb0, kb1, obase);
+      decode(tt, row0, rows, nb, s);
       const int acc = it & 1;
       const uint32_t aph = (uint32_t)((it >> 1) & 1);
       // one lane waits, the warp re-converges on the broadcast before the
@@ -467,7 +490,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // fp32 rows of out_ld (a multiple of 4) columns; columns in
         // [N, out_ld) hold the zero products of the out-of-range weight rows
         const int n0 = nb * BN;
-        float *orowf = reinterpret_cast<float *>(p.out) + (int64_t)(row0 + r) * p.out_ld;
+        float *orowf = reinterpret_cast<float *>(p.out) + obase + (int64_t)(row0 + r) * p.out_ld;
 #pragma unroll 1
         for (int c = part * 32; c < BN; c += 32 * EPI_SPLIT) {
           uint32_t v32[32];
@@ -607,6 +630,9 @@ int launch_tc_t(const rf::GroupedGemmArgs &g, const CUtensorMap &ma, const CUten
   p.out = g.out;
   p.out_ld = g.N;
   p.dense_rows = 0;
+  p.k_slices = 1;
+  p.kb_per_slice = 0;
+  p.slice_stride = 0;
   p.act = g.act;
   p.gather_src = g.gather_src;
   p.gather_div = g.gather_div;
@@ -732,7 +758,7 @@ int launch_dense(const CUtensorMap &ma, const CUtensorMap &ma32, const CUtensorM
   });
   if (attr_err != cudaSuccess)
     return rf::fail(RF_ERR_CUDA, std::string("tensor-core GEMM: ") + cudaGetErrorString(attr_err));
-  const int64_t tiles = (M + BM - 1) / BM * p.n_tiles_n;
+  const int64_t tiles = (M + BM - 1) / BM * p.n_tiles_n * std::max(1, p.k_slices);
   const int grid = (int)std::min<int64_t>(tiles, rf::num_sms());
   kern<<<grid, NTHREADS, C::SMEM_BYTES, st>>>(ma, ma32, mb, p, NoRemote{});
   return rf::check_launch("tensor-core dense GEMM (fp32 out)");
@@ -754,7 +780,7 @@ int gemm_impl() { return g_gemm_impl; }
 // then runs its CUDA-core code), else a status.  Each output is one fixed
 // sequence of MMAs over k, independent of M and of the other rows.
 int tc_dense_f32(const void *a, const void *w, float *out, int64_t M, int64_t N, int64_t Kdim,
-                 int64_t ld_out, int dtype, cudaStream_t st) {
+                 int64_t ld_out, int dtype, cudaStream_t st, int64_t slice_k) {
   if (g_gemm_impl == 1) return -1;
   if (dtype != RF_BF16 && dtype != RF_F16) return -1;
   if (M <= 0 || N <= 0 || Kdim % 8 || ld_out % 4 || ld_out < N || M >= ((int64_t)1 << 31) ||
@@ -785,6 +811,12 @@ int tc_dense_f32(const void *a, const void *w, float *out, int64_t M, int64_t N,
   p.out = out;
   p.out_ld = ld_out;
   p.act = 0;
+  if (slice_k > 0) {  // fixed slices of K, each a tile of its own; sums at out + j * M * ld_out
+    if (slice_k % BK) return -1;
+    p.kb_per_slice = (int)(slice_k / BK);
+    p.k_slices = (int)((Kdim + slice_k - 1) / slice_k);
+    p.slice_stride = M * ld_out;
+  }
   if (dtype == RF_BF16) {
     if (bn == 64) return launch_dense<__nv_bfloat16, 64>(ma, ma32, mb, p, M, st);
     if (bn == 128) return launch_dense<__nv_bfloat16, 128>(ma, ma32, mb, p, M, st);

@@ -9,8 +9,10 @@
 // Two launches.  The logits come from one of:
 //   the tensor cores (gemm_tc.cu, dense fp32-output mode) when x and the gate
 //       share a 16-bit dtype and a shared gate, if any, is the row right after
-//       the gate's E rows: one fp32 row of round_up(E', 4) logits per token,
-//       each a fixed sequence of MMAs over H (independent of T);
+//       the gate's E rows: one tile per (128 tokens, 256-wide slice of H), each
+//       slice's logits a fixed sequence of MMAs written as fp32 partials of
+//       round_up(E', 4) columns (independent of T; a decode batch still gets a
+//       CTA per slice);
 //   router_logits_kernel  otherwise (fp32 layers): a tiled CUDA-core GEMM.
 //       A block computes a tile of TT tokens x ET experts over one 256-wide
 //       slice of H (the slices give parallelism when there are few tokens);
@@ -389,11 +391,9 @@ extern "C" size_t rf_moe_router_workspace_size(int64_t T, int64_t H, int64_t E, 
   if (T <= 0 || H <= 0 || E <= 0) return 256;
   const int64_t Ec = E + (has_shared_gate ? 1 : 0);
   const size_t slices = (size_t)((H + SLICE - 1) / SLICE);
-  // CUDA-core path: per-slice partials; tensor-core path: one row of
-  // round_up(Ec, 4) logits per token
-  const size_t cuda_core = slices * (size_t)T * (size_t)Ec;
-  const size_t tensor = (size_t)T * (size_t)((Ec + 3) / 4 * 4);
-  return (cuda_core > tensor ? cuda_core : tensor) * sizeof(float) + 256;
+  // per-slice partials: [slices][T][Ec] on CUDA cores, [slices][T][round_up(Ec, 4)]
+  // on the tensor cores
+  return slices * (size_t)T * (size_t)((Ec + 3) / 4 * 4) * sizeof(float) + 256;
 }
 
 extern "C" int rf_moe_router_topk(const void *x, int x_dtype, const void *gate, int gate_dtype,
@@ -449,20 +449,23 @@ extern "C" int rf_moe_router_topk(const void *x, int x_dtype, const void *gate, 
                  "rf_moe_router_topk: workspace too small (see rf_moe_router_workspace_size)");
     RF_CHECK_ARG(p.ttiles <= 0x7fffffff && p.slices <= 65535, "rf_moe_router_topk: too many tokens");
     // Tensor cores when x and the gate share a 16-bit dtype and the shared
-    // gate (if any) is the row right after the gate's E rows: logits as one
-    // fp32 [T, ld] block, each a fixed MMA sequence over H (so, again, the
-    // same bits whatever T is).  Otherwise the CUDA-core slices.
+    // gate (if any) is the row right after the gate's E rows: one tile per
+    // (128 tokens, slice of H), each slice a fixed MMA sequence, partials
+    // [slices][T][ld] summed in slice order by the top-k pass (the same bits
+    // whatever T is; few tokens still get one CTA per slice).  Otherwise the
+    // CUDA-core slices.
     const size_t esz = (size_t)rf::dtype_size(gate_dtype);
     const bool adjacent = !shared_gate ||
                           (const char *)shared_gate == (const char *)gate + (size_t)E * (size_t)H * esz;
     const int64_t ld = (Ec + 3) / 4 * 4;
     int rc = -1;
-    if (x_dtype == gate_dtype && adjacent && workspace_bytes >= (size_t)T * (size_t)ld * sizeof(float))
-      rc = rf::tc_dense_f32(x, gate, reinterpret_cast<float *>(workspace), T, Ec, H, ld, x_dtype, st);
+    if (x_dtype == gate_dtype && adjacent &&
+        workspace_bytes >= (size_t)p.slices * (size_t)T * (size_t)ld * sizeof(float))
+      rc = rf::tc_dense_f32(x, gate, reinterpret_cast<float *>(workspace), T, Ec, H, ld, x_dtype, st, SLICE);
     if (rc > 0) return rc;
     if (rc == 0) {
       b.partial = reinterpret_cast<const float *>(workspace);
-      b.ksplit = 1;
+      b.ksplit = p.slices;
       b.ld = ld;
     } else {
       LogitsArgs a{x, gate, shared_gate, reinterpret_cast<float *>(workspace), T, (int)H, (int)E, Ec};

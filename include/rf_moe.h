@@ -43,7 +43,8 @@
  *   rf_moe_ep_plan / rf_moe_ep_pair_rows  the split of that exchange, replacing
  *                           the replicate-and-all-reduce forward of
  *                           reframework/parallel/ep.py:119-150
- *   rf_moe_ep_devplan, rf_moe_ep_devplan_host, _push, _regroup  the same plan
+ *   rf_moe_ep_devplan, rf_moe_ep_devplan_host, _push, _regroup,
+ *                           _regroup_remote  the same plan
  *                           and exchange driven from the GPU (no host sync)
  *   rf_moe_ep_devplan_down_return  reframework/moe/fused.py:83 on the expert's
  *                           rank + the return all-to-all (dist.py:194-206) in
@@ -397,8 +398,16 @@ int rf_moe_ep_counts_collect(const int32_t *flags, const int32_t *table, int32_t
  *                              token rank's rf_moe_permute layout, align 1), so
  *                              rf_moe_combine reads the return buffer through
  *                              that permute's row_of_slot; then flags as
- *                              rf_moe_ep_push_rows
+ *                              rf_moe_ep_push_rows.  For a dispatch that
+ *                              overlaps the exchange with the GEMM of this
+ *                              rank's own rows: dir 2 is dir 0 without the
+ *                              rows this rank routes to itself (flags as
+ *                              dir 0); dir 3 copies just those rows straight
+ *                              into their slot-major GEMM rows (dst[me] = xl;
+ *                              no flags, `flag`/`done` unused but non-NULL)
  *   rf_moe_ep_devplan_regroup  receive buffer -> slot-major GEMM rows
+ *   rf_moe_ep_devplan_regroup_remote  the same for the rows of the other
+ *                              sources only (after dir 2 + dir 3)
  *   rf_moe_ep_devplan_down_return  dir 1 fused into the down GEMM: the
  *                              tensor-core epilogue stores every row of
  *                              h[rows_capacity, I] . w2[j][H, I]^T straight
@@ -416,10 +425,15 @@ int rf_moe_ep_counts_collect(const int32_t *flags, const int32_t *table, int32_t
  *   below s), [14] int64 pstart [R][S] (source s's permuted row of its first
  *   row for slot j), [15] int64 piece_pos [n_pieces+1], [16] int64 piece_src
  *   [n_pieces] (send positions [piece_pos[k], piece_pos[k+1]) carry permuted
- *   rows from piece_src[k]), [17] int32 n_pieces.  `out` holds
+ *   rows from piece_src[k]), [17] int32 n_pieces, [18] int32 [S] offsets then
+ *   [S] counts: this rank's own rows of each local slot (the grouped-GEMM
+ *   groups of the dir-3 rows), [19] int32 [2S] offsets then [2S] counts: the
+ *   other sources' rows of each slot, those below this rank then those above
+ *   (groups 2j and 2j+1 use slot j's weights), [20] int32 piece_slot
+ *   [n_pieces] (the destination rank's local slot of each send piece).  `out` holds
  *   RF_EP_DEVPLAN_LAYOUT_N entries.
  */
-#define RF_EP_DEVPLAN_LAYOUT_N 18
+#define RF_EP_DEVPLAN_LAYOUT_N 21
 size_t rf_moe_ep_devplan_workspace_size(int32_t R, int32_t E, int32_t S, int32_t n_slots);
 int rf_moe_ep_devplan_layout(int32_t R, int32_t E, int32_t S, int32_t n_slots, int64_t *out);
 int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_experts, const int32_t *slot_offsets,
@@ -439,6 +453,8 @@ int rf_moe_ep_devplan_push(const void *workspace, int32_t R, int32_t E, int32_t 
                            uint32_t *done, rf_stream_t stream);
 int rf_moe_ep_devplan_regroup(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
                               const void *recv, void *xl, int64_t row_bytes, rf_stream_t stream);
+int rf_moe_ep_devplan_regroup_remote(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
+                                     const void *recv, void *xl, int64_t row_bytes, rf_stream_t stream);
 int rf_moe_ep_devplan_down_return(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
                                   const void *h, const void *w2, int64_t rows_capacity, int64_t H, int64_t I,
                                   int32_t dtype, void *const *dst, int32_t *const *flag, int32_t epoch,

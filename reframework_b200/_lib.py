@@ -90,6 +90,7 @@ _SIGNATURES = {
                                                                             _c_void_p, _c_void_p, ctypes.c_int32,
                                                                             _c_void_p, _c_void_p]),
     "rf_moe_ep_devplan_regroup": (_int, [_c_void_p] + [ctypes.c_int32] * 4 + [_c_void_p, _c_void_p, _i64, _c_void_p]),
+    "rf_moe_ep_devplan_regroup_remote": (_int, [_c_void_p] + [ctypes.c_int32] * 4 + [_c_void_p, _c_void_p, _i64, _c_void_p]),
     "rf_moe_ep_devplan_down_return": (_int, [_c_void_p] + [ctypes.c_int32] * 4 + [_c_void_p, _c_void_p, _i64, _i64,
                                                                                _i64, ctypes.c_int32, _c_void_p,
                                                                                _c_void_p, ctypes.c_int32, _c_void_p,
@@ -171,7 +172,7 @@ def device_status() -> int:
 
 _gemm_impl = 0
 RF_ERR_UNSUPPORTED = 2
-EP_DEVPLAN_LAYOUT_N = 18  # entries of rf_moe_ep_devplan_layout's output (RF_EP_DEVPLAN_LAYOUT_N)
+EP_DEVPLAN_LAYOUT_N = 21  # entries of rf_moe_ep_devplan_layout's output (RF_EP_DEVPLAN_LAYOUT_N)
 
 
 def set_gemm_impl(impl: int) -> None:

@@ -46,6 +46,7 @@ struct RfEpDevPlan {
   int64_t back_row0[MAXR];      // rows of s's earlier destinations (the host plan's return offset)
   int64_t piece_pos[MAXP + 1];  // send pieces (send order)
   int64_t piece_src[MAXP];
+  int32_t piece_slot[MAXP];     // the destination rank's local slot of each piece
   int32_t loff32[MAXS + 1];     // int32 copies of loff / lcount for the grouped GEMMs
   int32_t lcount32[MAXS];
   int64_t loff[MAXS + 1];       // local slot segments (aligned) and their row counts
@@ -109,6 +110,10 @@ struct PlannerArgs {
   int64_t *cj_prefix;           // [S][R+1]
   int64_t *pstart;              // [R][S]: permuted row in source s of its first row for slot j
   int64_t *cpre;                // [R][E+1]: rows of source s routed to experts below e
+  // GEMM groups of the overlapped dispatch (int32): this rank's own rows of
+  // each local slot, [S] offsets then [S] counts; the other sources' rows,
+  // [2S] offsets then [2S] counts (rows before and after this rank's, per slot)
+  int32_t *loc, *rem;
   PlanScratch sc;               // quota/lo/sbase [E*R], total [E], load [R], repl [E]
   int64_t *M;                   // [R][R]
   int32_t *hoff, *hlist;        // holders CSR: [E+1], [total slots]
@@ -136,6 +141,12 @@ __host__ __device__ void clear_plan(RfEpDevPlan *P, int S) {
   P->n_send = P->recv_total = P->rows_used = 0;
   P->n_pieces = 0;
   P->overflow = 1;
+}
+
+// A failed plan also gives the overlapped dispatch's GEMM groups no rows.
+__host__ __device__ void clear_groups(const PlannerArgs &a) {
+  for (int j = 0; j < 2 * a.S; ++j) a.loc[j] = 0;
+  for (int j = 0; j < 4 * a.S; ++j) a.rem[j] = 0;
 }
 
 // Runs the planner body: one block on the device (threads meet at barriers and
@@ -271,6 +282,7 @@ __host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
   if (s_bad) {
     if (x.tid() == 0) {
       clear_plan(P, a.S);
+      clear_groups(a);
       x.report(RF_DEV_BAD_EXPERT_ID);
     }
     return;
@@ -301,6 +313,7 @@ __host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
   if (s_bad) {
     if (x.tid() == 0) {
       clear_plan(P, a.S);
+      clear_groups(a);
       x.report(RF_DEV_PLAN_OVERFLOW);
     }
     return;
@@ -332,6 +345,7 @@ __host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
         if (start != pos) identity = 0;
         P->piece_pos[np] = pos;
         P->piece_src[np] = start;
+        P->piece_slot[np] = sl - a.slot_offsets[d];
         ++np;
         pos += ln;
       }
@@ -379,7 +393,18 @@ __host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
   P->overflow = bad;
   if (bad) {
     clear_plan(P, S);
+    clear_groups(a);
     x.report(RF_DEV_PLAN_OVERFLOW);
+  } else {
+    for (int j = 0; j < S; ++j) {
+      const int64_t *cj = a.cj_prefix + (int64_t)j * (R + 1);
+      a.loc[j] = (int32_t)(P->loff[j] + cj[me]);
+      a.loc[S + j] = (int32_t)(cj[me + 1] - cj[me]);
+      a.rem[2 * j] = (int32_t)P->loff[j];
+      a.rem[2 * j + 1] = (int32_t)(P->loff[j] + cj[me + 1]);
+      a.rem[2 * S + 2 * j] = (int32_t)cj[me];
+      a.rem[2 * S + 2 * j + 1] = (int32_t)(P->lcount[j] - cj[me + 1]);
+    }
   }
 }
 
@@ -396,7 +421,7 @@ namespace {
 // One 16-byte-aligned workspace per EP layer: the plan, its two prefix tables
 // and the planner's scratch.
 struct Layout {
-  size_t plan, cs, cj, ps, cpre, quota, lo, sbase, total, load, repl, M, hoff, hlist, bytes;
+  size_t plan, cs, cj, ps, cpre, quota, lo, sbase, total, load, repl, M, hoff, hlist, loc, rem, bytes;
 };
 
 size_t up16(size_t v) { return (v + 15) / 16 * 16; }
@@ -418,6 +443,8 @@ Layout layout_of(int64_t R, int64_t E, int64_t S, int64_t nslots) {
   L.M = o; o = up16(o + (size_t)R * R * 8);
   L.hoff = o; o = up16(o + (size_t)(E + 1) * 4);
   L.hlist = o; o = up16(o + (size_t)(nslots > 0 ? nslots : 1) * 4);
+  L.loc = o; o = up16(o + (size_t)2 * (S > 0 ? S : 1) * 4);
+  L.rem = o; o = up16(o + (size_t)4 * (S > 0 ? S : 1) * 4);
   L.bytes = o;
   return L;
 }
@@ -455,7 +482,8 @@ struct PlanPushArgs {
   const uint8_t *src;
   const int32_t *src_slot;      // dispatch: permuted row -> pair index (t*K+k)
   int64_t div, row_bytes;
-  int R, S, ret;                // ret: 0 dispatch, 1 return
+  int R, S, ret;                // ret (mode): 0 dispatch, 1 return, 2 dispatch to the other ranks only,
+                                // 3 this rank's own dispatch rows straight into its GEMM rows (dst[me])
   int32_t epoch;
   uint32_t *done;
   uint8_t *dst[MAXR];
@@ -473,17 +501,27 @@ __global__ void __launch_bounds__(256) plan_push_kernel(const __grid_constant__ 
   const int lane = threadIdx.x & 31;
   const int R = a.R, S = a.S;
   const int64_t vecs = a.row_bytes / 16;
-  const int64_t n = P->overflow ? 0 : (a.ret ? P->recv_total : P->n_send);
+  const int mode = a.ret, ok = !P->overflow, me = ok ? P->me : 0;  // a failed plan leaves `me` unset
+  // send positions of this rank's own rows: mode 2 skips them, mode 3 moves only them
+  const int64_t own0 = ok ? P->send_off[me] : 0, own = ok ? P->send_off[me + 1] - own0 : 0;
+  const int64_t n = !ok ? 0 : mode == 1 ? P->recv_total : mode == 2 ? P->n_send - own : mode == 3 ? own : P->n_send;
   const int64_t nwarps = (int64_t)gridDim.x * 8;
-  for (int64_t i = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); i < n; i += nwarps) {
+  for (int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); t < n; t += nwarps) {
+    const int64_t i = mode == 3 ? own0 + t : (mode == 2 && t >= own0) ? t + own : t;
     int64_t srow, drow;
     int d;
-    if (!a.ret) {
+    if (mode != 1) {
       const int k = find_le(P->piece_pos, P->n_pieces, i);
       const int64_t j = P->piece_src[k] + (i - P->piece_pos[k]);
       srow = (int64_t)a.src_slot[j] / a.div;
-      d = find_le(P->send_off, R, i);
-      drow = P->dst_row0[d] + (i - P->send_off[d]);
+      if (mode == 3) {  // own rows: the slot's segment, after the rows of the lower-ranked sources
+        const int js = P->piece_slot[k];
+        d = me;
+        drow = P->loff[js] + a.cj[(int64_t)js * (R + 1) + me] + (i - P->piece_pos[k]);
+      } else {
+        d = find_le(P->send_off, R, i);
+        drow = P->dst_row0[d] + (i - P->send_off[d]);
+      }
     } else {
       d = find_le(P->recv_off, R, i);
       const int64_t q2 = i - P->recv_off[d];
@@ -495,6 +533,7 @@ __global__ void __launch_bounds__(256) plan_push_kernel(const __grid_constant__ 
     copy_row(reinterpret_cast<uint4 *>(a.dst[d] + drow * a.row_bytes),
              reinterpret_cast<const uint4 *>(a.src + srow * a.row_bytes), vecs, lane);
   }
+  if (mode == 3) return;  // a local copy: no flags
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
@@ -511,7 +550,7 @@ __global__ void __launch_bounds__(256) plan_push_kernel(const __grid_constant__ 
 // pad rows are left untouched (their GEMM outputs are never stored).
 __global__ void __launch_bounds__(256) plan_regroup_kernel(const RfEpDevPlan *P, const int64_t *cs_all,
                                                            const int64_t *cj_all, const uint8_t *recv, uint8_t *xl,
-                                                           int64_t row_bytes, int R, int S) {
+                                                           int64_t row_bytes, int R, int S, int skip_me) {
   const int lane = threadIdx.x & 31;
   const int64_t vecs = row_bytes / 16;
   const int64_t n = P->overflow ? 0 : P->rows_used;
@@ -522,6 +561,7 @@ __global__ void __launch_bounds__(256) plan_regroup_kernel(const RfEpDevPlan *P,
     if (k >= P->lcount[j]) continue;
     const int64_t *cj = cj_all + (int64_t)j * (R + 1);
     const int s = find_le(cj, R, k);
+    if (skip_me && s == P->me) continue;  // placed by the own-rows push
     const int64_t q = P->recv_off[s] + cs_all[(int64_t)s * (S + 1) + j] + (k - cj[s]);
     copy_row(reinterpret_cast<uint4 *>(xl + r * row_bytes), reinterpret_cast<const uint4 *>(recv + q * row_bytes),
              vecs, lane);
@@ -556,6 +596,9 @@ extern "C" int rf_moe_ep_devplan_layout(int32_t R, int32_t E, int32_t S, int32_t
   out[15] = (int64_t)(L.plan + offsetof(RfEpDevPlan, piece_pos));  // int64 [n_pieces+1] send pieces
   out[16] = (int64_t)(L.plan + offsetof(RfEpDevPlan, piece_src));  // int64 [n_pieces]
   out[17] = (int64_t)(L.plan + offsetof(RfEpDevPlan, n_pieces));   // int32
+  out[18] = (int64_t)L.loc;  // int32 [S] offsets, [S] counts: this rank's own rows per local slot
+  out[19] = (int64_t)L.rem;  // int32 [2S] offsets, [2S] counts: the other sources' rows per local slot
+  out[20] = (int64_t)(L.plan + offsetof(RfEpDevPlan, piece_slot));  // int32 [n_pieces]
   return RF_OK;
 }
 
@@ -601,6 +644,8 @@ int planner_args(PlannerArgs &a, const int32_t *counts, const int32_t *slot_expe
   a.M = reinterpret_cast<int64_t *>(w + L.M);
   a.hoff = reinterpret_cast<int32_t *>(w + L.hoff);
   a.hlist = reinterpret_cast<int32_t *>(w + L.hlist);
+  a.loc = reinterpret_cast<int32_t *>(w + L.loc);
+  a.rem = reinterpret_cast<int32_t *>(w + L.rem);
   return RF_OK;
 }
 
@@ -637,12 +682,14 @@ extern "C" int rf_moe_ep_devplan_host(const int32_t *counts, const int32_t *slot
 }
 
 // dir 0: dispatch (src = token rows x, src_slot/div map send positions to them);
-// dir 1: return (src = the local GEMM output rows).
+// dir 1: return (src = the local GEMM output rows); dir 2: dispatch to the other
+// ranks only; dir 3: this rank's own dispatch rows into its slot-major GEMM rows
+// dst[me] (a local copy, no flags).
 extern "C" int rf_moe_ep_devplan_push(const void *workspace, int32_t R, int32_t E, int32_t S, int32_t n_slots,
                                       int32_t dir, const void *src, const int32_t *src_slot, int64_t div,
                                       int64_t row_bytes, void *const *dst, int32_t *const *flag, int32_t epoch,
                                       uint32_t *done, rf_stream_t stream) {
-  RF_CHECK_ARG(workspace && dst && flag && done && (dir == 0 || dir == 1), "rf_moe_ep_devplan_push: bad arguments");
+  RF_CHECK_ARG(workspace && dst && flag && done && dir >= 0 && dir <= 3, "rf_moe_ep_devplan_push: bad arguments");
   RF_CHECK_ARG(R >= 1 && R <= MAXR && row_bytes > 0 && row_bytes % 16 == 0 && div >= 1,
                "rf_moe_ep_devplan_push: bad sizes");
   RF_CHECK_ARG((uintptr_t)src % 16 == 0, "rf_moe_ep_devplan_push: source must be 16-byte aligned");
@@ -681,8 +728,23 @@ extern "C" int rf_moe_ep_devplan_regroup(const void *workspace, int32_t R, int32
   plan_regroup_kernel<<<rf::num_sms() * 4, 256, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const RfEpDevPlan *>(w + L.plan), reinterpret_cast<const int64_t *>(w + L.cs),
       reinterpret_cast<const int64_t *>(w + L.cj), reinterpret_cast<const uint8_t *>(recv),
-      reinterpret_cast<uint8_t *>(xl), row_bytes, R, S);
+      reinterpret_cast<uint8_t *>(xl), row_bytes, R, S, 0);
   return rf::check_launch("rf_moe_ep_devplan_regroup");
+}
+
+extern "C" int rf_moe_ep_devplan_regroup_remote(const void *workspace, int32_t R, int32_t E, int32_t S,
+                                                int32_t n_slots, const void *recv, void *xl, int64_t row_bytes,
+                                                rf_stream_t stream) {
+  RF_CHECK_ARG(workspace && recv && xl && R >= 1 && R <= MAXR && row_bytes % 16 == 0,
+               "rf_moe_ep_devplan_regroup_remote: bad arguments");
+  const Layout L = layout_of(R, E, S, n_slots);
+  const uint8_t *w = reinterpret_cast<const uint8_t *>(workspace);
+  if (S == 0) return RF_OK;
+  plan_regroup_kernel<<<rf::num_sms() * 4, 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const RfEpDevPlan *>(w + L.plan), reinterpret_cast<const int64_t *>(w + L.cs),
+      reinterpret_cast<const int64_t *>(w + L.cj), reinterpret_cast<const uint8_t *>(recv),
+      reinterpret_cast<uint8_t *>(xl), row_bytes, R, S, 1);
+  return rf::check_launch("rf_moe_ep_devplan_regroup_remote");
 }
 
 // dir 1 fused into the down GEMM: y = h . w2[j]^T per local slot, each row

@@ -223,6 +223,11 @@ class EPFusedMoE(nn.Module):
         # (None: the largest first-step token count over the ranks)
         self.max_tokens_per_rank: Optional[int] = None
         self._dp = None
+        # device plan: push the rows bound for the other ranks on a side stream
+        # while the gated GEMM runs over the rows this rank routed to itself;
+        # False: push everything, wait, then one gated GEMM (same result)
+        self.overlap_dispatch = False
+        self._side_stream = None
         self.last_counts_dev: Optional[torch.Tensor] = None
 
     # --------------------------------------------------------------- build
@@ -599,11 +604,17 @@ class EPFusedMoE(nn.Module):
             lay = np.zeros(_lib_mod.EP_DEVPLAN_LAYOUT_N, dtype=np.int64)
             check(lib().rf_moe_ep_devplan_layout(R, E, S, nslots, lay.ctypes.data), "rf_moe_ep_devplan_layout")
             ws = torch.zeros(nb, dtype=torch.uint8, device=dev)
+            i32 = lambda o, n: ws[o:o + 4 * n].view(torch.int32)  # noqa: E731
             st = self._dp = {
                 "placement": self.placement, "S": S, "nslots": nslots, "ws": ws,
                 "flat": torch.from_numpy(flat).to(dev), "offs": torch.from_numpy(offs).to(dev),
-                "seg_off": ws[lay[0]:lay[0] + 4 * (S + 1)].view(torch.int32),
-                "seg_cnt": ws[lay[1]:lay[1] + 4 * max(S, 1)].view(torch.int32)[:S],
+                "seg_off": i32(lay[0], S + 1),
+                "seg_cnt": i32(lay[1], max(S, 1))[:S],
+                # groups of the overlapped dispatch: own rows per slot, then the
+                # other sources' rows (below / above this rank) per slot
+                "loc_off": i32(lay[18], 2 * S)[:S], "loc_cnt": i32(lay[18], 2 * S)[S:],
+                "rem_off": i32(lay[19], 4 * S)[:2 * S], "rem_cnt": i32(lay[19], 4 * S)[2 * S:],
+                "rem_slot": torch.arange(S, dtype=torch.int32, device=dev).repeat_interleave(2),
             }
         recv_cap = R * self.max_tokens_per_rank * Kk
         st["recv_cap"] = recv_cap
@@ -640,27 +651,62 @@ class EPFusedMoE(nn.Module):
         flags0 = (ctypes.c_void_p * R)(*[ctrl[d] + 4 * (DISPATCH * R + self.ep_rank) for d in range(R)])
         flags1 = (ctypes.c_void_p * R)(*[ctrl[d] + 4 * (RETURN * R + self.ep_rank) for d in range(R)])
         done = px.own[2].ptr + 2 * R * 4
-        check(lib().rf_moe_ep_devplan_push(ws.data_ptr(), R, E, S, nslots, 0, x2.data_ptr() if T else None,
-                                           p.src_slot.data_ptr() if p is not None else None, Kk, row_bytes,
-                                           (ctypes.c_void_p * R)(*px.peer[0]), flags0, epoch, done, st),
-              "rf_moe_ep_devplan_push")
-        self._mark("dispatch push")
-        px.wait(DISPATCH)
-        self._mark("dispatch wait")
+        xsrc = x2.data_ptr() if T else None
+        ssrc = p.src_slot.data_ptr() if p is not None else None
+        peers_recv = (ctypes.c_void_p * R)(*px.peer[0])
         y = None
         back = (ctypes.c_void_p * R)(*px.peer[1])
         returned = False
-        if S > 0:
-            rows = stt["rows_cap"]
+        rows = stt["rows_cap"]
+        I = self.intermediate_size
+        overlap = self.overlap_dispatch and S > 0
+        if overlap:
+            # the rows for the other ranks cross NVLink on a side stream while
+            # this rank's own rows go straight into their GEMM rows and the
+            # gated GEMM runs over them; the other sources' rows follow
+            cur = torch.cuda.current_stream(dev)
+            if self._side_stream is None:
+                self._side_stream = torch.cuda.Stream(device=dev)
+            side = self._side_stream
+            side.wait_stream(cur)
+            check(lib().rf_moe_ep_devplan_push(ws.data_ptr(), R, E, S, nslots, 2, xsrc, ssrc, Kk, row_bytes,
+                                               peers_recv, flags0, epoch, done, side.cuda_stream),
+                  "rf_moe_ep_devplan_push")
             xl = torch.empty(rows, H, dtype=x2.dtype, device=dev)
-            check(lib().rf_moe_ep_devplan_regroup(ws.data_ptr(), R, E, S, nslots, px.recv_ptr(), xl.data_ptr(),
-                                                  row_bytes, st), "rf_moe_ep_devplan_regroup")
-            self._mark("regroup gather")
+            own = (ctypes.c_void_p * R)(*([xl.data_ptr()] * R))
+            check(lib().rf_moe_ep_devplan_push(ws.data_ptr(), R, E, S, nslots, 3, xsrc, ssrc, Kk, row_bytes,
+                                               own, flags0, epoch, done, st), "rf_moe_ep_devplan_push")
+            self._mark("own rows")
             w1b, w2b = self._gemm_banks()
-            I = self.intermediate_size
             h = torch.empty(rows, I, dtype=x2.dtype, device=dev)
-            K.grouped_gemm_gated(xl, w1b, stt["seg_off"], stt["seg_cnt"], h, activation=self.activation)
+            K.grouped_gemm_gated(xl, w1b, stt["loc_off"], stt["loc_cnt"], h, activation=self.activation)
+            self._mark("gated GEMM (own rows)")
+            cur.wait_stream(side)  # every tensor the side stream read outlives this join
+            px.wait(DISPATCH)
+            self._mark("dispatch wait")
+            check(lib().rf_moe_ep_devplan_regroup_remote(ws.data_ptr(), R, E, S, nslots, px.recv_ptr(),
+                                                         xl.data_ptr(), row_bytes, st),
+                  "rf_moe_ep_devplan_regroup_remote")
+            self._mark("regroup gather")
+            K.grouped_gemm_gated(xl, w1b, stt["rem_off"], stt["rem_cnt"], h, slot=stt["rem_slot"],
+                                 activation=self.activation)
             self._mark("gated GEMM")
+        else:
+            check(lib().rf_moe_ep_devplan_push(ws.data_ptr(), R, E, S, nslots, 0, xsrc, ssrc, Kk, row_bytes,
+                                               peers_recv, flags0, epoch, done, st), "rf_moe_ep_devplan_push")
+            self._mark("dispatch push")
+            px.wait(DISPATCH)
+            self._mark("dispatch wait")
+        if S > 0:
+            if not overlap:
+                xl = torch.empty(rows, H, dtype=x2.dtype, device=dev)
+                check(lib().rf_moe_ep_devplan_regroup(ws.data_ptr(), R, E, S, nslots, px.recv_ptr(),
+                                                      xl.data_ptr(), row_bytes, st), "rf_moe_ep_devplan_regroup")
+                self._mark("regroup gather")
+                w1b, w2b = self._gemm_banks()
+                h = torch.empty(rows, I, dtype=x2.dtype, device=dev)
+                K.grouped_gemm_gated(xl, w1b, stt["seg_off"], stt["seg_cnt"], h, activation=self.activation)
+                self._mark("gated GEMM")
             # the down GEMM's epilogue stores every row into its token rank's
             # return buffer (the exchange overlaps the GEMM tile by tile)
             rc = lib().rf_moe_ep_devplan_down_return(ws.data_ptr(), R, E, S, nslots, h.data_ptr(), w2b.data_ptr(),

@@ -338,7 +338,9 @@ def test_device_planner_on_host_matches_host_plan_and_round_trips(seed):
                           loff=i32(lo[0], S + 1).astype(np.int64), lcount=i32(lo[1], S).astype(np.int64),
                           cs=i64(lo[12], R * (S + 1)).reshape(R, S + 1), cj=i64(lo[13], S * (R + 1)).reshape(S, R + 1),
                           ps=i64(lo[14], R * S).reshape(R, S), piece_pos=i64(lo[15], npc + 1),
-                          piece_src=i64(lo[16], npc), n_send=int(i64(lo[4], 1)[0])))
+                          piece_src=i64(lo[16], npc), n_send=int(i64(lo[4], 1)[0]),
+                          piece_slot=i32(lo[20], npc).astype(np.int64), loc=i32(lo[18], 2 * S).astype(np.int64),
+                          rem=i32(lo[19], 4 * S).astype(np.int64)))
     # dispatch: tag = source * 2^20 + its permuted row
     recv = [np.full(max(int(recv_off_d[-1]), 1), -1, np.int64) for recv_off_d in (p["recv_off"] for p in plans)]
     for s, p in enumerate(plans):
@@ -373,6 +375,34 @@ def test_device_planner_on_host_matches_host_plan_and_round_trips(seed):
                 back[ss][drow[s == ss]] = rows[s == ss]
     for s in range(R):
         assert np.array_equal(back[s][:Ts[s] * K], (s << 20) + np.arange(Ts[s] * K)), f"rank {s}: round trip"
+    # the overlapped dispatch: dir 3 puts this rank's own rows straight into its
+    # GEMM rows, the remote-only regroup fills the rest; together they give the
+    # GEMM rows of the plain regroup, and the group tables split each slot's
+    # segment into the rows below / of / above this rank
+    for me, p in enumerate(plans):
+        S, loff, lcount = p["S"], p["loff"], p["lcount"]
+        xl = np.full(max(int(loff[-1]), 1), -1, np.int64)
+        i = np.arange(p["send_off"][me], p["send_off"][me + 1])
+        if i.size:
+            k = _find_le(p["piece_pos"][:-1], i)
+            src_row = p["piece_src"][k] + i - p["piece_pos"][k]
+            js = p["piece_slot"][k]
+            drow = loff[js] + p["cj"][js, me] + i - p["piece_pos"][k]
+            assert (xl[drow] == -1).all(), "an own row placed twice"
+            xl[drow] = (me << 20) + src_row
+        for j in range(S):
+            k = np.arange(lcount[j])
+            s = _find_le(p["cj"][j, :R], k)
+            q = p["recv_off"][s] + p["cs"][s, j] + k - p["cj"][j, s]
+            rem = s != me
+            assert (xl[loff[j] + k[rem]] == -1).all()
+            xl[loff[j] + k[rem]] = recv[me][q[rem]]
+            want = recv[me][q]
+            assert np.array_equal(xl[loff[j]:loff[j] + lcount[j]], want), f"rank {me} slot {j}: overlapped rows"
+            lo_, own, hi = p["cj"][j, me], p["cj"][j, me + 1] - p["cj"][j, me], lcount[j] - p["cj"][j, me + 1]
+            assert (p["rem"][2 * j], p["rem"][2 * S + 2 * j]) == (loff[j], lo_)
+            assert (p["loc"][j], p["loc"][S + j]) == (loff[j] + lo_, own)
+            assert (p["rem"][2 * j + 1], p["rem"][2 * S + 2 * j + 1]) == (loff[j] + lo_ + own, hi)
 
 
 def test_device_planner_on_host_rejects_bad_placements_and_small_buffers():
@@ -390,6 +420,7 @@ def test_device_planner_on_host_rejects_bad_placements_and_small_buffers():
         assert wb[lo[2]:lo[2] + 4].view(np.int32)[0] == 1
         assert not wb[lo[0]:lo[0] + 12].view(np.int32).any() and not wb[lo[1]:lo[1] + 8].view(np.int32).any()
         assert wb[lo[4]:lo[4] + 8].view(np.int64)[0] == 0
+        assert not wb[lo[18]:lo[18] + 16].view(np.int32).any() and not wb[lo[19]:lo[19] + 32].view(np.int32).any()
     st, *_ = _devplan_host(cnt, flat, offs, R, E, 0, 1, 64, 79, 400)  # rank 0's 80 return rows, capacity 79
     assert st == 3
     st, *_ = _devplan_host(cnt, flat, offs, R, E, 0, 128, 64, 80, 64 + 127)  # GEMM rows: 2 x 128 > 191

@@ -241,6 +241,45 @@ def test_device_plan_matches_host_plan_and_round_trips(cuda_ok, seed):
         assert L.rf_moe_ep_devplan_regroup(ws[me].data_ptr(), R, E, S, nslots, recv[me].data_ptr(), xl.data_ptr(),
                                            row_bytes, st) == 0
         ys.append(xl)
+    # the overlapped dispatch (dir 2 to the other ranks into fresh buffers, dir 3
+    # own rows straight into the GEMM rows, remote-only regroup) fills the same
+    # GEMM rows, and its group tables cover exactly the slot segments
+    recv2 = [torch.zeros_like(b) for b in recv]
+    ctrl2 = [torch.zeros(R, dtype=torch.int32, device=dev) for _ in range(R)]
+    xl2 = [torch.zeros_like(y) for y in ys]
+    for me in range(R):
+        S = len(pl.slots[me])
+        flags = (ctypes.c_void_p * R)(*[ctrl2[d].data_ptr() + 4 * me for d in range(R)])
+        src = xs[me] if Ts[me] else recv[me][:0]
+        for mode, dst in ((2, ptrs(recv2)), (3, ptrs([xl2[me]] * R))):
+            assert L.rf_moe_ep_devplan_push(ws[me].data_ptr(), R, E, S, nslots, mode, src.data_ptr(),
+                                            perms[me].src_slot.data_ptr(), topk, row_bytes, dst, flags, 5,
+                                            done.data_ptr() + 4 * me, st) == 0
+    for me in range(R):
+        S = len(pl.slots[me])
+        assert L.rf_moe_ep_devplan_regroup_remote(ws[me].data_ptr(), R, E, S, nslots, recv2[me].data_ptr(),
+                                                  xl2[me].data_ptr(), row_bytes, st) == 0
+    torch.cuda.synchronize()
+    assert all(bool((c == 5).all()) for c in ctrl2), "dir 2 raised its flags in every peer"
+    for me in range(R):
+        S = len(pl.slots[me])
+        wb, lo = ws[me].cpu().numpy(), lay[me]
+        i32 = lambda off, n: wb[off:off + 4 * n].view(np.int32)
+        soff, scnt = i32(lo[0], S + 1), i32(lo[1], S)
+        loc, rem = i32(lo[18], 2 * S), i32(lo[19], 4 * S)
+        covered = []
+        for j in range(S):
+            parts = [(int(rem[2 * j]), int(rem[2 * S + 2 * j])), (int(loc[j]), int(loc[S + j])),
+                     (int(rem[2 * j + 1]), int(rem[2 * S + 2 * j + 1]))]
+            pos = int(soff[j])
+            for a, n in parts:  # below this rank, own, above: contiguous, in that order
+                assert a == pos and n >= 0, f"rank {me} slot {j}: groups {parts} vs segment {soff[j]}+{scnt[j]}"
+                pos += n
+            assert pos == soff[j] + scnt[j]
+            covered.append(torch.arange(int(soff[j]), pos))
+        if covered:
+            idx = torch.cat(covered).to(dev)
+            assert torch.equal(xl2[me][idx], ys[me][idx]), f"rank {me}: overlapped dispatch rows differ"
     for me in range(R):  # return pushes
         S = len(pl.slots[me])
         flags = (ctypes.c_void_p * R)(*[ctrl[d].data_ptr() + 4 * (R + me) for d in range(R)])

@@ -182,13 +182,17 @@ def test_c4_full_size_parity_with_oracle(renormalize):
     _check_full_size(cfg, f"C4 renormalize={renormalize}")
 
 
-def _emulated_ep_forward(moe, x, R, placement):
+def _emulated_ep_forward(moe, x, R, placement, overlap=False):
     """The expert-parallel forward of EPFusedMoE's device-planned path, R ranks
     emulated on one GPU with separate buffers: every rank's route + compact
     permute, device plan, dispatch push, regroup, gated GEMM, down GEMM with the
     return exchange in its epilogue, and combine (+ the shared experts).  The
     stages run rank by rank in stream order, so each bounded wait starts only
-    after every push it waits for has run.  Returns the concatenated outputs."""
+    after every push it waits for has run.  ``overlap``: the overlapped
+    dispatch (rows for the other ranks pushed, own rows placed straight into
+    the GEMM rows and their gated GEMM run before the wait, then the other
+    sources' rows regrouped and their gated GEMM).  Returns the concatenated
+    outputs."""
     import ctypes
     from reframework_b200.parallel.ep import shard_range  # noqa: F401  (placement built by the caller)
     L = _lib.lib()
@@ -226,7 +230,7 @@ def _emulated_ep_forward(moe, x, R, placement):
     done = torch.zeros(R, dtype=torch.int32, device=DEV)
     ptrs = lambda ts: (ctypes.c_void_p * R)(*[t.data_ptr() for t in ts])  # noqa: E731
     flags = lambda d_, me: (ctypes.c_void_p * R)(*[ctrl[d].data_ptr() + 4 * (d_ * R + me) for d in range(R)])  # noqa: E731
-    ws, segs = [], []
+    ws, segs, groups = [], [], []
     for me in range(R):
         S = len(placement.slots[me])
         nb = L.rf_moe_ep_devplan_workspace_size(R, E, S, nslots)
@@ -239,24 +243,43 @@ def _emulated_ep_forward(moe, x, R, placement):
         ws.append(wsp)
         segs.append((wsp[lay[0]:lay[0] + 4 * (S + 1)].view(torch.int32), wsp[lay[1]:lay[1] + 4 * S].view(torch.int32),
                      rows_cap))
+        loc, rem = wsp[lay[18]:lay[18] + 8 * S].view(torch.int32), wsp[lay[19]:lay[19] + 16 * S].view(torch.int32)
+        groups.append((loc[:S], loc[S:], rem[:2 * S], rem[2 * S:],
+                       torch.arange(S, dtype=torch.int32, device=DEV).repeat_interleave(2)))
     epoch = 1
+    w1b, w2b = moe._resident_banks()
+    xls = [torch.empty(segs[me][2], H, dtype=x.dtype, device=DEV) for me in range(R)]
+    hs = [torch.empty(segs[me][2], I, dtype=x.dtype, device=DEV) for me in range(R)]
+    banks = []
+    for me in range(R):
+        sl = torch.tensor(placement.slots[me], dtype=torch.long, device=DEV)
+        banks.append((w1b[sl].contiguous(), w2b[sl].contiguous()))
     for me, (lo, hi) in enumerate(bounds):  # dispatch
         S = len(placement.slots[me])
-        assert L.rf_moe_ep_devplan_push(ws[me].data_ptr(), R, E, S, nslots, 0, x[lo:hi].data_ptr(),
-                                        routed[me][3].src_slot.data_ptr(), Kk, row_bytes, ptrs(recv),
-                                        flags(0, me), epoch, done.data_ptr() + 4 * me, st) == 0
-    w1b, w2b = moe._resident_banks()
+        assert L.rf_moe_ep_devplan_push(ws[me].data_ptr(), R, E, S, nslots, 2 if overlap else 0,
+                                        x[lo:hi].data_ptr(), routed[me][3].src_slot.data_ptr(), Kk, row_bytes,
+                                        ptrs(recv), flags(0, me), epoch, done.data_ptr() + 4 * me, st) == 0
+        if overlap:  # own rows into the GEMM rows, their gated GEMM before the wait
+            assert L.rf_moe_ep_devplan_push(ws[me].data_ptr(), R, E, S, nslots, 3, x[lo:hi].data_ptr(),
+                                            routed[me][3].src_slot.data_ptr(), Kk, row_bytes, ptrs([xls[me]] * R),
+                                            flags(0, me), epoch, done.data_ptr() + 4 * me, st) == 0
+            K.grouped_gemm_gated(xls[me], banks[me][0], groups[me][0], groups[me][1], hs[me],
+                                 activation=moe.activation)
     for me in range(R):  # expert ranks: regroup, gated GEMM, down GEMM + return
         assert L.rf_moe_ep_wait(ctrl[me].data_ptr(), R, epoch, st) == 0
         S = len(placement.slots[me])
         seg_off, seg_cnt, rows_cap = segs[me]
-        xl = torch.empty(rows_cap, H, dtype=x.dtype, device=DEV)
-        assert L.rf_moe_ep_devplan_regroup(ws[me].data_ptr(), R, E, S, nslots, recv[me].data_ptr(), xl.data_ptr(),
-                                           row_bytes, st) == 0
-        sl = torch.tensor(placement.slots[me], dtype=torch.long, device=DEV)
-        b1, b2 = w1b[sl].contiguous(), w2b[sl].contiguous()
-        h = torch.empty(rows_cap, I, dtype=x.dtype, device=DEV)
-        K.grouped_gemm_gated(xl, b1, seg_off, seg_cnt, h, activation=moe.activation)
+        xl, h = xls[me], hs[me]
+        b1, b2 = banks[me]
+        if overlap:
+            assert L.rf_moe_ep_devplan_regroup_remote(ws[me].data_ptr(), R, E, S, nslots, recv[me].data_ptr(),
+                                                      xl.data_ptr(), row_bytes, st) == 0
+            K.grouped_gemm_gated(xl, b1, groups[me][2], groups[me][3], h, slot=groups[me][4],
+                                 activation=moe.activation)
+        else:
+            assert L.rf_moe_ep_devplan_regroup(ws[me].data_ptr(), R, E, S, nslots, recv[me].data_ptr(),
+                                               xl.data_ptr(), row_bytes, st) == 0
+            K.grouped_gemm_gated(xl, b1, seg_off, seg_cnt, h, activation=moe.activation)
         assert L.rf_moe_ep_devplan_down_return(ws[me].data_ptr(), R, E, S, nslots, h.data_ptr(), b2.data_ptr(),
                                                rows_cap, H, I, _lib.dtype_code(x.dtype), ptrs(back), flags(1, me),
                                                epoch, done.data_ptr() + 4 * me, st) == 0
@@ -275,8 +298,9 @@ def _emulated_ep_forward(moe, x, R, placement):
     return torch.cat(outs)
 
 
-@pytest.mark.parametrize("R,redundant", [(8, 0), (8, 2), (4, 1)])
-def test_c4_full_size_ep_emulated_matches_single_process(R, redundant):
+@pytest.mark.parametrize("R,redundant,overlap", [(8, 0, False), (8, 2, False), (4, 1, False), (8, 2, True),
+                                                 (4, 1, True)])
+def test_c4_full_size_ep_emulated_matches_single_process(R, redundant, overlap):
     """C4 at its benchmark size split over R expert-parallel ranks emulated on
     one GPU (contiguous expert shards, optionally with hot-expert replicas):
     the concatenated rank outputs equal the single-process layer bit for bit
@@ -299,5 +323,5 @@ def test_c4_full_size_ep_emulated_matches_single_process(R, redundant):
     else:
         placement = Placement(tuple(tuple(range(a, b)) for a, b in shards))
     with torch.no_grad():
-        got = _emulated_ep_forward(moe, x, R, placement)
-    assert torch.equal(got, ref), f"R={R}: EP output differs from the single-process layer"
+        got = _emulated_ep_forward(moe, x, R, placement, overlap=overlap)
+    assert torch.equal(got, ref), f"R={R} overlap={overlap}: EP output differs from the single-process layer"

@@ -154,16 +154,32 @@ __global__ void __launch_bounds__(NT) simt_grouped_gemm(rf::GroupedGemmArgs p) {
 }
 
 // Skinny variant for experts with few rows (decode-sized groups): a block
-// covers SN output columns for every row of the expert, SR rows at a time;
-// thread (rg, c) owns column n0 + c for the RPT rows rg*RPT...  A 4-stage cp.async ring streams 32-deep k-chunks of the SN weight
-// rows (x2 gated) and of the SR activation rows into shared memory, both kept
-// k-contiguous ([col][k], [row][k]); the multiply reads 16-byte vectors along
-// k (weights: one per thread, activations: warp-wide broadcasts).  Each output
-// is the same ascending-k fp32 FMA chain as in the tiled kernel, so the two
-// kernels give the same bits.
-constexpr int SN = 64, SR = 16, SK = 32, SSTAGES = 4;
-constexpr int RPT = 4;                     // rows per thread
-constexpr int SNT = SN * (SR / RPT);       // threads per block
+// covers SN output columns for every row of the expert, SR rows at a time.
+// Each warp owns 8 columns and all SR rows: lane (c, rg) = (lane % 8, lane / 8)
+// computes column c for the RPT rows rg, rg + 4, rg + 8, ... (interleaved, so the
+// four row groups read different banks).  A 4-stage cp.async ring streams
+// 32-deep k-chunks of the SN weight rows (x2 gated) and of the expert's
+// activation rows into shared memory, both kept k-contiguous ([col][k],
+// [row][k], padded rows); the multiply reads 16-byte vectors along k.  In one
+// warp a weight vector is shared by the 4 row groups and an activation vector
+// by the 8 columns (broadcast reads), so per 16-byte step a warp issues
+// (1 + gated) + RPT loads for 32 * RPT * (1 + gated) * vector-width FMAs.
+// Small blocks (SN = 32, 128 threads, ~55 KB of ring for fp32) give a fine
+// grid: several blocks per SM and a short last wave.  Each output is the same
+// ascending-k fp32 FMA chain as in the tiled kernel, so the two kernels give
+// the same bits.
+#ifndef RF_SKINNY_SK
+#define RF_SKINNY_SK 32
+#endif
+#ifndef RF_SKINNY_STAGES
+#define RF_SKINNY_STAGES 4
+#endif
+constexpr int SN = 32, SR = 32, SK = RF_SKINNY_SK, SSTAGES = RF_SKINNY_STAGES;
+constexpr int RPT = 8;                      // rows per thread
+constexpr int SRG = SR / RPT;               // row groups (4) = lanes per column
+constexpr int SCW = 32 / SRG;               // columns per warp (8)
+constexpr int SNT = (SN / SCW) * 32;        // threads per block (128)
+static_assert(SRG * RPT == SR && SCW * SRG == 32 && RPT == 8, "skinny lane layout (the NR dispatch covers 1..8)");
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool ok) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0)
@@ -183,11 +199,37 @@ struct SkinnyCfg {
   static constexpr int ROW_BYTES = LD * (int)sizeof(T);
 };
 
+// The multiply of one staged chunk for NR rows per thread (NR block-uniform:
+// rows past the expert's are computed on stale shared memory and never stored),
+// branch-free so the compiler interleaves the NR * (1 + gated) FMA chains.
+template <typename T, bool GATED, int NR>
+__device__ __forceinline__ void skinny_chunk(const uint8_t *wg, const uint8_t *wu, const uint8_t *xs,
+                                             float *accg, float *accu) {
+  using C = SkinnyCfg<T>;
+#pragma unroll
+  for (int kv = 0; kv < C::KV; ++kv) {
+    float fg[8], fu[8], fx[NR][8];
+    rf::unpack16<T>(*reinterpret_cast<const uint4 *>(wg + kv * 16), fg);
+    if constexpr (GATED) rf::unpack16<T>(*reinterpret_cast<const uint4 *>(wu + kv * 16), fu);
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+      rf::unpack16<T>(*reinterpret_cast<const uint4 *>(xs + r * SRG * C::ROW_BYTES + kv * 16), fx[r]);
+#pragma unroll
+    for (int j = 0; j < C::E16; ++j)
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        accg[r] = fmaf(fx[r][j], fg[j], accg[r]);
+        if constexpr (GATED) accu[r] = fmaf(fx[r][j], fu[j], accu[r]);
+      }
+  }
+}
+
 template <typename T, bool GATED>
 __global__ void __launch_bounds__(SNT) simt_skinny_gemm(rf::GroupedGemmArgs p) {
   using C = SkinnyCfg<T>;
   constexpr int NW = GATED ? 2 : 1;
   constexpr int STAGE_BYTES = (NW * SN + SR) * C::ROW_BYTES;
+  constexpr int MAXC = ((NW * SN + SR) * C::KV + SNT - 1) / SNT;  // 16-byte copies per thread per chunk
   extern __shared__ __align__(16) uint8_t s_raw[];
   const int g = blockIdx.y;
   const int e = p.groups ? p.groups[g] : g;
@@ -203,7 +245,8 @@ __global__ void __launch_bounds__(SNT) simt_skinny_gemm(rf::GroupedGemmArgs p) {
     return;
   }
   const int n0 = blockIdx.x * SN;
-  const int c = threadIdx.x % SN, rg = threadIdx.x / SN;
+  const int lane = threadIdx.x & 31;
+  const int c = (threadIdx.x >> 5) * SCW + (lane % SCW), rg = lane / SCW;
   const int64_t wstride = (int64_t)NW * p.N * p.Kdim;
   const T *W = reinterpret_cast<const T *>(p.w) + (int64_t)s * wstride;
   T *out = reinterpret_cast<T *>(p.out);
@@ -211,27 +254,41 @@ __global__ void __launch_bounds__(SNT) simt_skinny_gemm(rf::GroupedGemmArgs p) {
   const int nchunks = (p.Kdim + SK - 1) / SK;
   for (int m0 = 0; m0 < cnt; m0 += SR) {
     const int rows = min(SR, cnt - m0);
+    const int nr = (rows + SRG - 1) / SRG;  // rows per thread, the same in the whole block
     const T *A = reinterpret_cast<const T *>(p.a) + ((int64_t)p.offsets[e] + m0) * p.Kdim;
-    // copies of chunk q into ring slot q % SSTAGES: rows [0, NW*SN) weights, then SR activation rows
+    // this thread's copies of every chunk: rows [0, NW*SN) weights, then the
+    // activation rows; the source moves by SK elements per chunk
+    const T *csrc[MAXC];
+    uint32_t cdst[MAXC];
+    int ck[MAXC];  // the copy's first k inside a chunk, or -1 (no copy)
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int v = threadIdx.x + i * SNT;
+      const int row = v / C::KV, kv = v % C::KV;
+      ck[i] = -1;
+      csrc[i] = W;
+      cdst[i] = (uint32_t)(row * C::ROW_BYTES + kv * 16);
+      if (row < NW * SN) {
+        const int m = row / SN, n = n0 + row % SN;
+        if (n < p.N) {
+          ck[i] = kv * C::E16;
+          csrc[i] = W + ((int64_t)m * p.N + n) * p.Kdim + ck[i];
+        }
+      } else if (row - NW * SN < rows) {
+        ck[i] = kv * C::E16;
+        csrc[i] = A + (int64_t)(row - NW * SN) * p.Kdim + ck[i];
+      }
+    }
     auto issue = [&](int q) {
       if (q < nchunks) {
         const int k0 = q * SK;
         const uint32_t st = sbase + (uint32_t)((q % SSTAGES) * STAGE_BYTES);
-        for (int v = threadIdx.x; v < (NW * SN + SR) * C::KV; v += SNT) {
-          const int row = v / C::KV, kv = v % C::KV, k = k0 + kv * C::E16;
-          const T *src;
-          bool ok;
-          if (row < NW * SN) {
-            const int m = row / SN, n = n0 + row % SN;
-            ok = n < p.N && k < p.Kdim;
-            src = ok ? W + ((int64_t)m * p.N + n) * p.Kdim + k : W;
-          } else {
-            const int r = row - NW * SN;
-            ok = r < rows && k < p.Kdim;
-            src = ok ? A + (int64_t)r * p.Kdim + k : A;
+#pragma unroll
+        for (int i = 0; i < MAXC; ++i)
+          if (ck[i] >= 0) {
+            const bool ok = k0 + ck[i] < p.Kdim;
+            cp_async16(st + cdst[i], ok ? csrc[i] + k0 : csrc[i], ok);
           }
-          cp_async16(st + (uint32_t)(row * C::ROW_BYTES + kv * 16), src, ok);
-        }
       }
       cp_async_commit();  // one group per chunk slot, empty past the end
     };
@@ -249,37 +306,32 @@ __global__ void __launch_bounds__(SNT) simt_skinny_gemm(rf::GroupedGemmArgs p) {
       const uint8_t *st = s_raw + (q % SSTAGES) * STAGE_BYTES;
       const uint8_t *wg = st + c * C::ROW_BYTES;
       const uint8_t *wu = st + (SN + c) * C::ROW_BYTES;
-      const uint8_t *xs = st + (NW * SN + rg * RPT) * C::ROW_BYTES;
-#pragma unroll
-      for (int kv = 0; kv < C::KV; ++kv) {
-        float fg[8], fu[8];
-        rf::unpack16<T>(*reinterpret_cast<const uint4 *>(wg + kv * 16), fg);
-        if constexpr (GATED) rf::unpack16<T>(*reinterpret_cast<const uint4 *>(wu + kv * 16), fu);
-#pragma unroll
-        for (int r = 0; r < RPT; ++r) {
-          float fx[8];
-          rf::unpack16<T>(*reinterpret_cast<const uint4 *>(xs + r * C::ROW_BYTES + kv * 16), fx);
-#pragma unroll
-          for (int j = 0; j < C::E16; ++j) {
-            accg[r] = fmaf(fx[j], fg[j], accg[r]);
-            if constexpr (GATED) accu[r] = fmaf(fx[j], fu[j], accu[r]);
-          }
-        }
+      const uint8_t *xs = st + (NW * SN + rg) * C::ROW_BYTES;
+      switch (nr) {  // block-uniform
+        case 1: skinny_chunk<T, GATED, 1>(wg, wu, xs, accg, accu); break;
+        case 2: skinny_chunk<T, GATED, 2>(wg, wu, xs, accg, accu); break;
+        case 3: skinny_chunk<T, GATED, 3>(wg, wu, xs, accg, accu); break;
+        case 4: skinny_chunk<T, GATED, 4>(wg, wu, xs, accg, accu); break;
+        case 5: skinny_chunk<T, GATED, 5>(wg, wu, xs, accg, accu); break;
+        case 6: skinny_chunk<T, GATED, 6>(wg, wu, xs, accg, accu); break;
+        case 7: skinny_chunk<T, GATED, 7>(wg, wu, xs, accg, accu); break;
+        default: skinny_chunk<T, GATED, 8>(wg, wu, xs, accg, accu); break;
       }
     }
     cp_async_wait<0>();
     __syncthreads();  // the ring is reused by the next row chunk
     const int n = n0 + c;
     if (n < p.N) {
-      T *orow = out + ((int64_t)p.offsets[e] + m0 + rg * RPT) * p.N + n;
+      T *ocol = out + ((int64_t)p.offsets[e] + m0) * p.N + n;
 #pragma unroll
       for (int r = 0; r < RPT; ++r) {
-        if (rg * RPT + r >= rows) break;
+        const int row = rg + r * SRG;
+        if (row >= rows) break;
         float v = GATED ? rf::gated_elem<T>(p.act, accg[r], accu[GATED ? r : 0]) : accg[r];
         if (!GATED && p.addend)
-          v = rf::Cvt<T>::to_f(reinterpret_cast<const T *>(p.addend)[(orow - out) + (int64_t)r * p.N]) +
+          v = rf::Cvt<T>::to_f(reinterpret_cast<const T *>(p.addend)[(ocol - out) + (int64_t)row * p.N]) +
               rf::round_to<T>(v);
-        orow[(int64_t)r * p.N] = rf::Cvt<T>::from_f(v);
+        ocol[(int64_t)row * p.N] = rf::Cvt<T>::from_f(v);
       }
     }
   }

@@ -157,24 +157,22 @@ __global__ void __launch_bounds__(NT) simt_grouped_gemm(rf::GroupedGemmArgs p) {
 // covers SN output columns for every row of the expert, SR rows at a time.
 // Each warp owns 8 columns and all SR rows: lane (c, rg) = (lane % 8, lane / 8)
 // computes column c for the RPT rows rg, rg + 4, rg + 8, ... (interleaved, so the
-// four row groups read different banks).  A 4-stage cp.async ring streams
+// four row groups read different banks).  A 3- (gated) or 4-stage (down) cp.async ring streams
 // 32-deep k-chunks of the SN weight rows (x2 gated) and of the expert's
 // activation rows into shared memory, both kept k-contiguous ([col][k],
 // [row][k], padded rows); the multiply reads 16-byte vectors along k.  In one
 // warp a weight vector is shared by the 4 row groups and an activation vector
 // by the 8 columns (broadcast reads), so per 16-byte step a warp issues
 // (1 + gated) + RPT loads for 32 * RPT * (1 + gated) * vector-width FMAs.
-// Small blocks (SN = 32, 128 threads, ~55 KB of ring for fp32) give a fine
-// grid: several blocks per SM and a short last wave.  Each output is the same
+// Small blocks (SN = 32, 128 threads, ~41 KB of ring for fp32, at most 102
+// registers a thread) give a fine grid: five blocks per SM and a short last
+// wave.  Each output is the same
 // ascending-k fp32 FMA chain as in the tiled kernel, so the two kernels give
 // the same bits.
-#ifndef RF_SKINNY_SK
-#define RF_SKINNY_SK 32
-#endif
-#ifndef RF_SKINNY_STAGES
-#define RF_SKINNY_STAGES 4
-#endif
-constexpr int SN = 32, SR = 32, SK = RF_SKINNY_SK, SSTAGES = RF_SKINNY_STAGES;
+constexpr int SN = 32, SR = 32, SK = 32;
+// ring depth: 3 for the gated kernel (five 41 KB blocks per SM for fp32, one
+// wave for C1-sized launches), 4 for the down kernel
+template <bool GATED> constexpr int skinny_stages() { return GATED ? 3 : 4; }
 constexpr int RPT = 8;                      // rows per thread
 constexpr int SRG = SR / RPT;               // row groups (4) = lanes per column
 constexpr int SCW = 32 / SRG;               // columns per warp (8)
@@ -206,29 +204,42 @@ template <typename T, bool GATED, int NR>
 __device__ __forceinline__ void skinny_chunk(const uint8_t *wg, const uint8_t *wu, const uint8_t *xs,
                                              float *accg, float *accu) {
   using C = SkinnyCfg<T>;
+  // vectors of step kv + 1 are loaded while step kv multiplies (shared-memory
+  // latency hidden inside the warp)
+  uint4 vg[2], vu[2], vx[2][NR];
+  auto load = [&](int kv, int b) {
+    vg[b] = *reinterpret_cast<const uint4 *>(wg + kv * 16);
+    if constexpr (GATED) vu[b] = *reinterpret_cast<const uint4 *>(wu + kv * 16);
+#pragma unroll
+    for (int r = 0; r < NR; ++r) vx[b][r] = *reinterpret_cast<const uint4 *>(xs + r * SRG * C::ROW_BYTES + kv * 16);
+  };
+  load(0, 0);
 #pragma unroll
   for (int kv = 0; kv < C::KV; ++kv) {
-    float fg[8], fu[8], fx[NR][8];
-    rf::unpack16<T>(*reinterpret_cast<const uint4 *>(wg + kv * 16), fg);
-    if constexpr (GATED) rf::unpack16<T>(*reinterpret_cast<const uint4 *>(wu + kv * 16), fu);
+    const int b = kv & 1;
+    if (kv + 1 < C::KV) load(kv + 1, b ^ 1);
+    float fg[8], fu[8];
+    rf::unpack16<T>(vg[b], fg);
+    if constexpr (GATED) rf::unpack16<T>(vu[b], fu);
 #pragma unroll
-    for (int r = 0; r < NR; ++r)
-      rf::unpack16<T>(*reinterpret_cast<const uint4 *>(xs + r * SRG * C::ROW_BYTES + kv * 16), fx[r]);
+    for (int r = 0; r < NR; ++r) {
+      float fx[8];
+      rf::unpack16<T>(vx[b][r], fx);
 #pragma unroll
-    for (int j = 0; j < C::E16; ++j)
-#pragma unroll
-      for (int r = 0; r < NR; ++r) {
-        accg[r] = fmaf(fx[r][j], fg[j], accg[r]);
-        if constexpr (GATED) accu[r] = fmaf(fx[r][j], fu[j], accu[r]);
+      for (int j = 0; j < C::E16; ++j) {
+        accg[r] = fmaf(fx[j], fg[j], accg[r]);
+        if constexpr (GATED) accu[r] = fmaf(fx[j], fu[j], accu[r]);
       }
+    }
   }
 }
 
 template <typename T, bool GATED>
-__global__ void __launch_bounds__(SNT) simt_skinny_gemm(rf::GroupedGemmArgs p) {
+__global__ void __launch_bounds__(SNT, GATED ? 5 : 1) simt_skinny_gemm(rf::GroupedGemmArgs p) {
   using C = SkinnyCfg<T>;
   constexpr int NW = GATED ? 2 : 1;
   constexpr int STAGE_BYTES = (NW * SN + SR) * C::ROW_BYTES;
+  constexpr int SSTAGES = skinny_stages<GATED>();
   constexpr int MAXC = ((NW * SN + SR) * C::KV + SNT - 1) / SNT;  // 16-byte copies per thread per chunk
   extern __shared__ __align__(16) uint8_t s_raw[];
   const int g = blockIdx.y;
@@ -340,7 +351,7 @@ __global__ void __launch_bounds__(SNT) simt_skinny_gemm(rf::GroupedGemmArgs p) {
 template <typename T, bool GATED>
 int launch_skinny(const rf::GroupedGemmArgs &p, cudaStream_t st) {
   constexpr int NW = GATED ? 2 : 1;
-  constexpr size_t smem = (size_t)SSTAGES * (NW * SN + SR) * SkinnyCfg<T>::ROW_BYTES;
+  constexpr size_t smem = (size_t)skinny_stages<GATED>() * (NW * SN + SR) * SkinnyCfg<T>::ROW_BYTES;
   auto kern = simt_skinny_gemm<T, GATED>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;

@@ -34,6 +34,15 @@
 //               [token][row], then 16-byte stores of whole token rows.
 // Tiles: per group n_fb feature blocks x ceil(count / 256) token blocks,
 // token-fastest so concurrently running pairs share a weight block in L2.
+// A pair's first tile is its cluster index; later tiles are claimed
+// dynamically (one global atomic counter per launch, the next tile claimed
+// while the current one loads), so a pair that starts late, because another
+// kernel still held its SMs, takes fewer tiles instead of stretching the
+// launch by its whole static share.  The first CTA's producer claims for the
+// pair and publishes each index through a small ring in both CTAs' shared
+// memory (full / empty barriers; read by the MMA issuer, the second producer
+// and one epilogue warp per CTA; the second CTA waits with cluster-scope
+// acquire).
 // Each mbarrier wait is bounded (2 s): on expiry the CTA flags the device
 // error word and both CTAs of the pair stop, let their copies in flight land
 // (a bounded pause: the second CTA's copies signal the first CTA's barrier, so
@@ -43,6 +52,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -81,14 +91,23 @@ constexpr int P_THREADS = 32 * (2 + P_EPI_WARPS);
 constexpr int P_CHUNK = 32;                    // token columns per epilogue round
 constexpr int P_STG_BYTES = P_CHUNK * P_AROWS * 2;  // [32 tokens][128 rows] 16-bit
 constexpr int P_MAX_GROUPS = 512;
-constexpr int P_NUM_BARS = 2 * P_STAGES + 5;   // full, empty, tmem full x2, tmem empty x2, drain
+constexpr int P_TQ = 8;                        // tile-index ring slots
+// Readers that release a ring slot: the MMA issuer and the second CTA's
+// producer (neither stores to global memory, so their release arrives are
+// cheap).  The epilogue reads each index too but does not arrive: it cannot
+// fall more than 2 tiles behind the MMA issuer (two TMEM accumulators), which
+// itself is at most P_STAGES stages behind the producer, so with P_TQ > 6 a
+// slot is never rewritten before the epilogue has read it.
+constexpr int P_TQ_READERS = 2;
+constexpr int P_NUM_BARS = 2 * P_STAGES + 5 + 2 * P_TQ;  // full, empty, tmem full x2, tmem empty x2, drain, tile ring
+constexpr int P_SCHED_SLOTS = 64;              // launches in flight with their own tile counter
 constexpr uint64_t P_ABORT_DRAIN_NS = 1000000;  // pause for copies in flight after an abort (1 ms)
 constexpr uint32_t P_TMEM_COLS = 512;
 constexpr int P_N_BOXES = 5;                   // token boxes of 8, 16, 32, 64, 128 rows
 constexpr unsigned P_EPI_SLEEP_NS = RF_PAIR_EPI_SLEEP_NS;  // epilogue polls of the accumulator barrier
 constexpr size_t P_SMEM_BYTES = 1024 + (size_t)P_STAGES * (P_A_BYTES + P_B_BYTES) + 2 * P_STG_BYTES +
                                 P_NUM_BARS * 8 + 16 + (size_t)(P_MAX_GROUPS + 1) * 4 +
-                                (size_t)3 * P_MAX_GROUPS * 4;
+                                (size_t)3 * P_MAX_GROUPS * 4 + (P_TQ + 2) * 4;
 static_assert(P_SMEM_BYTES <= 227 * 1024, "shared memory");
 
 struct PairArgs {
@@ -99,7 +118,17 @@ struct PairArgs {
   int n_fb;  // feature blocks per group (128 features per pair gated, 256 down)
   void *out;
   const void *addend;  // down only: out = round(addend + round(acc)); may be NULL or out
+  int sched;           // this launch's tile counter (g_pair_sched row)
 };
+
+// Per-launch tile counters.  Every pair claims until it draws an index past
+// the last tile, so a launch makes exactly npairs + max(0, total - npairs)
+// claims; the pair that drew the last of them puts the counter back to zero
+// when it finishes (after a wait timeout the counter may be left nonzero: the
+// device error word then reports RF_DEV_WAIT_TIMEOUT).  The host hands
+// consecutive launches consecutive counters, so up to P_SCHED_SLOTS launches
+// may be in flight at once (several streams, graphs) without sharing one.
+__device__ int g_pair_sched[P_SCHED_SLOTS];
 
 // Token-row maps of one launch: the same 2-D tensor with boxes of 8 << i rows.
 struct TokMaps {
@@ -188,6 +217,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
+// try_wait with cluster-scope acquire: the phase was completed by the other
+// CTA of the pair, which wrote the data it guards into this CTA's memory.
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Non-blocking probe: has the phase of `parity` completed?
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -240,26 +282,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   int *g_row0 = tile_prefix + P_MAX_GROUPS + 1;                   // [G]
   int *g_cnt = g_row0 + P_MAX_GROUPS;                             // [G]
   int *g_slot = g_cnt + P_MAX_GROUPS;                             // [G]
+  volatile int *tq = g_slot + P_MAX_GROUPS;                       // [P_TQ] claimed tile indices
+  volatile int *epi_t = tq + P_TQ;                                // [2] the epilogue's current tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();  // 0: issues the pair's MMAs
-  const int pair = (int)cluster_id_x(), npairs = (int)ncluster_x();
   const int G = p.n_groups;
+  // a pair's first tile is its cluster index; later tiles are claimed
+  // (counter value c -> tile npairs + c) and pass through the ring
+  const int pair = (int)cluster_id_x(), npairs = (int)ncluster_x();
   const uint32_t bar0 = smem_u32(bars);
 #define FULL(s) (bar0 + 8u * (uint32_t)(s))
 #define EMPTY(s) (bar0 + 8u * (uint32_t)(P_STAGES + (s)))
 #define TFULL(a) (bar0 + 8u * (uint32_t)(2 * P_STAGES + (a)))
 #define TEMPTY(a) (bar0 + 8u * (uint32_t)(2 * P_STAGES + 2 + (a)))
   const uint32_t DRAIN = bar0 + 8u * (uint32_t)(2 * P_STAGES + 4);
+#define TQF(i) (bar0 + 8u * (uint32_t)(2 * P_STAGES + 5 + (i)))
+#define TQE(i) (bar0 + 8u * (uint32_t)(2 * P_STAGES + 5 + P_TQ + (i)))
   const uint32_t peer_abort = mapa_shared(smem_u32((const void *)abort_flag), rank ^ 1u);
 
   // bounded wait; on expiry both CTAs of the pair are told to stop
-  auto pwait = [&](uint32_t bar, uint32_t parity, unsigned sleep_ns) -> bool {
-    if (mbar_try(bar, parity)) return true;
+  auto pwait = [&](uint32_t bar, uint32_t parity, unsigned sleep_ns, bool cluster_acq = false) -> bool {
+    auto probe = [&]() { return cluster_acq ? mbar_try_cluster(bar, parity) : mbar_try(bar, parity); };
+    if (probe()) return true;
     const uint64_t t0 = rf::globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
       if (sleep_ns) __nanosleep(sleep_ns);
-      if (mbar_try(bar, parity)) return true;
+      if (probe()) return true;
       if ((it & 63) == 0) {
         if (*abort_flag) return false;
         if (rf::globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
@@ -282,6 +331,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       mbar_init(TEMPTY(a), 2 * P_EPI_WARPS);  // every epilogue warp of both CTAs
     }
     mbar_init(DRAIN, 1);
+    epi_t[0] = epi_t[1] = 0;
+    for (int i = 0; i < P_TQ; ++i) {
+      mbar_init(TQF(i), 1);             // the first CTA's producer publishes
+      mbar_init(TQE(i), P_TQ_READERS);  // used in the first CTA only
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -361,7 +415,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = pair; t < total && ok; t += npairs) {
+      int *claim = &g_pair_sched[p.sched];
+      const int last_claim = npairs + max(0, total - npairs) - 1;
+      auto draw = [&]() { return npairs + atomicAdd(claim, 1); };  // the result is used a tile later
+      const uint32_t tq_peer = mapa_shared(smem_u32((const void *)tq), 1);
+      const uint32_t tqf_peer = mapa_shared(TQF(0), 1);
+      const uint32_t tqe_lead = mapa_shared(TQE(0), 0);
+      // the first CTA publishes each iteration's tile during the iteration
+      // before, so the second CTA's producer never waits for it at a tile
+      // boundary
+      int t_lead = pair;                                            // this iteration's tile
+      int t_next = rank == 0 ? draw() : 0;  // the next one's (claimed)
+      for (int it = 0; ok; ++it) {
+        int t;
+        if (rank == 0) {
+          t = t_lead;
+          if (t >= total) break;  // the sentinel went out one iteration earlier (or t is the first tile)
+        } else if (it == 0) {
+          t = pair;
+          if (t >= total) break;
+        } else {
+          const int slot = (it - 1) % P_TQ;
+          if (!pwait(TQF(slot), (uint32_t)(((it - 1) / P_TQ) & 1), 0, true)) {
+            ok = false;
+            break;
+          }
+          t = tq[slot];
+          mbar_arrive_cluster(tqe_lead + 8u * (uint32_t)slot);
+          if (t >= total) break;
+        }
         int row0, ntok, fb, s;
         decode(t, row0, ntok, fb, s);
         const int half = ((ntok + 15) & ~15) >> 1;  // token rows per CTA: N/2, a multiple of 8
@@ -395,8 +477,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             stage = 0;
             phase ^= 1u;
           }
+          if (rank == 0 && kb == min(P_STAGES - 1, num_kb - 1)) {
+            // once this tile's first stages are in flight (the claim issued
+            // a tile earlier, or at kernel start, has returned by then):
+            // publish the next iteration's tile (ring slot it % P_TQ) and
+            // claim the one after
+            const int slot = it % P_TQ;
+            if (!pwait(TQE(slot), (uint32_t)(((it / P_TQ) & 1) ^ 1), 0)) {
+              ok = false;
+              break;
+            }
+            tq[slot] = t_next;
+            st_cluster_u32(tq_peer + 4u * (uint32_t)slot, (uint32_t)t_next);
+            mbar_arrive(TQF(slot));
+            mbar_arrive_cluster(tqf_peer + 8u * (uint32_t)slot);
+            t_lead = t_next;
+            if (t_next < total) t_next = draw();  // its latency overlaps this tile
+          }
         }
       }
+      // a pair's last draw is past the last tile; the draw that was the
+      // launch's last claim puts the counter back to zero for the next launch
+      if (rank == 0 && t_next - npairs == last_claim) atomicExch(claim, 0);
       if (!ok) {  // let the copies in flight land before this CTA can exit (bounded pause)
         const uint64_t t0 = rf::globaltimer_ns();
         while (rf::globaltimer_ns() - t0 < P_ABORT_DRAIN_NS) __nanosleep(1000);
@@ -411,7 +513,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       bool ready = false;  // the stage about to be consumed was seen complete by the early probe
-      for (int t = pair; t < total && ok; t += npairs, ++it) {
+      for (;; ++it) {
+        int t = pair;
+        if (it > 0) {
+          const int slot = (it - 1) % P_TQ;
+          if (!pwait(TQF(slot), (uint32_t)(((it - 1) / P_TQ) & 1), 0)) break;
+          t = tq[slot];
+          mbar_arrive(TQE(slot));
+        }
+        if (t >= total) break;
         int row0, ntok, fb, s;
         decode(t, row0, ntok, fb, s);
         const uint32_t idesc = IDESC | ((uint32_t)(((ntok + 15) & ~15) >> 3) << 17);
@@ -443,10 +553,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             phase ^= 1u;
           }
         }
-        if (ok) {
-          tc_commit_pair(TFULL(acc));
-          tc_commit_pair(peer_bars + (TFULL(acc) - bar0));
-        }
+        if (!ok) break;
+        tc_commit_pair(TFULL(acc));
+        tc_commit_pair(peer_bars + (TFULL(acc) - bar0));
       }
       // no MMA may still be running when either CTA releases TMEM or exits
       tc_commit_pair(DRAIN);
@@ -460,7 +569,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     const uint32_t tempty0 = mapa_shared(TEMPTY(0), 0);
     T *out = reinterpret_cast<T *>(p.out);
     int it = 0, round = 0;
-    for (int t = pair; t < total; t += npairs, ++it) {
+    for (;; ++it) {
+      // the first epilogue warp reads the ring for all eight (one reader per CTA)
+      int tok_ok = 1;
+      if (it > 0 && warp == 2 && lane == 0) {
+        const int slot = (it - 1) % P_TQ;
+        tok_ok = pwait(TQF(slot), (uint32_t)(((it - 1) / P_TQ) & 1), P_EPI_SLEEP_NS, true) ? 1 : 0;
+        if (tok_ok) epi_t[it & 1] = tq[slot];
+      }
+      tok_ok = __shfl_sync(0xffffffffu, tok_ok, 0);
+      if (!epi_vote_and(tok_ok)) break;  // every epilogue warp takes the same branch
+      const int t = it > 0 ? epi_t[it & 1] : pair;
+      if (t >= total) break;             // the same index in every warp
       int row0, ntok, fb, s;
       decode(t, row0, ntok, fb, s);
       const int np = (ntok + 15) & ~15;
@@ -540,6 +660,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, P_TMEM_COLS);
   }
+#undef TQF
+#undef TQE
 #undef FULL
 #undef EMPTY
 #undef TFULL
@@ -629,6 +751,8 @@ int launch_pair_grouped_gemm(const GroupedGemmArgs &g, bool gated, cudaStream_t 
   p.n_fb = gated ? (g.N + 127) / 128 : (g.N + 255) / 256;
   p.out = g.out;
   p.addend = gated ? nullptr : g.addend;
+  static std::atomic<unsigned> next_sched{0};
+  p.sched = (int)(next_sched.fetch_add(1u) % (unsigned)P_SCHED_SLOTS);
   if (g.dtype == RF_BF16) return launch_pair_dt<__nv_bfloat16>(g, gated, mw, mx, p, st);
   return launch_pair_dt<__half>(g, gated, mw, mx, p, st);
 }

@@ -661,22 +661,22 @@ class EPFusedMoE(nn.Module):
         I = self.intermediate_size
         overlap = self.overlap_dispatch and S > 0
         if overlap:
-            # the rows for the other ranks cross NVLink on a side stream while
-            # this rank's own rows go straight into their GEMM rows and the
-            # gated GEMM runs over them; the other sources' rows follow
+            # this rank's own rows go straight into their GEMM rows; then the
+            # rows for the other ranks cross NVLink on a side stream while the
+            # gated GEMM runs over the own rows; the other sources' rows follow
             cur = torch.cuda.current_stream(dev)
             if self._side_stream is None:
                 self._side_stream = torch.cuda.Stream(device=dev)
             side = self._side_stream
-            side.wait_stream(cur)
-            check(lib().rf_moe_ep_devplan_push(ws.data_ptr(), R, E, S, nslots, 2, xsrc, ssrc, Kk, row_bytes,
-                                               peers_recv, flags0, epoch, done, side.cuda_stream),
-                  "rf_moe_ep_devplan_push")
             xl = torch.empty(rows, H, dtype=x2.dtype, device=dev)
             own = (ctypes.c_void_p * R)(*([xl.data_ptr()] * R))
             check(lib().rf_moe_ep_devplan_push(ws.data_ptr(), R, E, S, nslots, 3, xsrc, ssrc, Kk, row_bytes,
                                                own, flags0, epoch, done, st), "rf_moe_ep_devplan_push")
             self._mark("own rows")
+            side.wait_stream(cur)
+            check(lib().rf_moe_ep_devplan_push(ws.data_ptr(), R, E, S, nslots, 2, xsrc, ssrc, Kk, row_bytes,
+                                               peers_recv, flags0, epoch, done, side.cuda_stream),
+                  "rf_moe_ep_devplan_push")
             w1b, w2b = self._gemm_banks()
             h = torch.empty(rows, I, dtype=x2.dtype, device=dev)
             K.grouped_gemm_gated(xl, w1b, stt["loc_off"], stt["loc_cnt"], h, activation=self.activation)

@@ -296,6 +296,51 @@ def test_pair_kernel_matches_single_cta_kernel(H, I, counts, act):
         assert torch.count_nonzero(y5[offs[e] + c:offs[e + 1]]) == 0
 
 
+def test_pair_kernel_tile_claims_concurrent_launches_and_counter_reuse():
+    """The CTA-pair kernel claims its tiles from a per-launch counter: launches
+    running at the same time on different streams (each holding part of the
+    GPU, so pairs start late) and more launches in a row than there are
+    counters must all give the bits of a lone launch."""
+    g = torch.Generator().manual_seed(77)
+    dtype = torch.bfloat16
+    counts = [300, 17, 0, 256, 90, 5, 128, 40]
+    E, H, I = len(counts), 1024, 704
+    offs = _segments(counts)
+    rows = offs[-1]
+    a = torch.randn(rows, H, generator=g).to(dtype).to(DEV)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.05).to(dtype).to(DEV)
+    w2 = (torch.randn(E, H, I, generator=g) * 0.05).to(dtype).to(DEV)
+    off_t = torch.tensor(offs, dtype=torch.int32, device=DEV)
+    cnt_t = torch.tensor(counts, dtype=torch.int32, device=DEV)
+    _lib.set_gemm_impl(0)
+    h_ref = torch.zeros(rows, I, dtype=dtype, device=DEV)
+    y_ref = torch.zeros(rows, H, dtype=dtype, device=DEV)
+    K.grouped_gemm_gated(a, w1, off_t, cnt_t, h_ref)
+    K.grouped_gemm_down(h_ref, w2, off_t, cnt_t, y_ref)
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(device=DEV) for _ in range(3)]
+    outs = []
+    for rep in range(24):  # 24 x 3 streams x 2 launches: every counter row used more than once
+        hs, ys = [], []
+        for st in streams:
+            st.wait_stream(torch.cuda.current_stream(DEV))
+            with torch.cuda.stream(st):
+                h = torch.zeros(rows, I, dtype=dtype, device=DEV)
+                y = torch.zeros(rows, H, dtype=dtype, device=DEV)
+                K.grouped_gemm_gated(a, w1, off_t, cnt_t, h)
+                K.grouped_gemm_down(h, w2, off_t, cnt_t, y)
+            hs.append(h)
+            ys.append(y)
+        for st in streams:
+            torch.cuda.current_stream(DEV).wait_stream(st)
+        outs.append((hs, ys))
+    torch.cuda.synchronize()
+    for hs, ys in outs:
+        for h, y in zip(hs, ys):
+            assert torch.equal(h, h_ref) and torch.equal(y, y_ref)
+    assert _lib.device_status() == 0
+
+
 @pytest.mark.parametrize("impl", [0, 1, 2, 5])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_down_gemm_addend_rounds_like_the_reference(impl, dtype):

@@ -32,6 +32,21 @@ struct ErrorWordRegistrar {
 int read_clear_all_error_words(int *code);
 
 // -------------------------------------------------------------- device side
+// Work order of the peer push kernels: item t of n goes to position
+// (t * stride + offset) mod n, a permutation when stride is prime to n.
+// Consecutive warps then copy rows for all destinations at once (send order
+// is destination-major, so the plain order would have every rank write to the
+// same few ranks first), and the per-rank offset staggers the ranks.
+__device__ __forceinline__ int64_t scatter_stride(int64_t n) {
+  const int64_t primes[3] = {1009, 1013, 1019};
+  for (int i = 0; i < 3; ++i)
+    if (n % primes[i] != 0) return primes[i];
+  return 1;
+}
+__device__ __forceinline__ int64_t scatter_pos(int64_t t, int64_t n, int64_t stride, int64_t offset) {
+  return (t * stride + offset) % n;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -506,7 +506,11 @@ __global__ void __launch_bounds__(256) plan_push_kernel(const __grid_constant__ 
   const int64_t own0 = ok ? P->send_off[me] : 0, own = ok ? P->send_off[me + 1] - own0 : 0;
   const int64_t n = !ok ? 0 : mode == 1 ? P->recv_total : mode == 2 ? P->n_send - own : mode == 3 ? own : P->n_send;
   const int64_t nwarps = (int64_t)gridDim.x * 8;
-  for (int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); t < n; t += nwarps) {
+  // copies to other ranks interleave all destinations (see rf::scatter_pos)
+  const int64_t stride = mode == 3 || n == 0 ? 1 : rf::scatter_stride(n);
+  const int64_t offset = n == 0 ? 0 : (int64_t)me * (n / (R > 0 ? R : 1));
+  for (int64_t t0 = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); t0 < n; t0 += nwarps) {
+    const int64_t t = mode == 3 ? t0 : rf::scatter_pos(t0, n, stride, offset);
     const int64_t i = mode == 3 ? own0 + t : (mode == 2 && t >= own0) ? t + own : t;
     int64_t srow, drow;
     int d;

@@ -64,7 +64,11 @@ __global__ void __launch_bounds__(256) push_rows_kernel(const __grid_constant__ 
   const int64_t n = a.chunk_off[a.R];
   const int64_t nwarps = (int64_t)gridDim.x * 8;
   const int64_t vecs = a.row_bytes / 16;
-  for (int64_t i = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); i < n; i += nwarps) {
+  // rows for all destinations interleaved, ranks staggered (see rf::scatter_pos)
+  const int64_t stride = n == 0 ? 1 : rf::scatter_stride(n);
+  const int64_t offset = n == 0 ? 0 : (int64_t)a.me * (n / a.R);
+  for (int64_t w = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); w < n; w += nwarps) {
+    const int64_t i = rf::scatter_pos(w, n, stride, offset);
     // destination rank: the chunk holding row i (binary search, R <= 64)
     int lo = 0, hi = a.R - 1;
     while (lo < hi) {

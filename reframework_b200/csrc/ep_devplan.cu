@@ -21,6 +21,7 @@
 // rows in ascending expert order, whichever rank computed them.  Bit-for-bit
 // the same split as the host planner: tests compare the two.
 #include <cstddef>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -414,6 +415,70 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
   planner_body(a, x);
 }
 
+// Shared-memory layout of the planner's inputs and scratch (the planner is
+// one block whose first thread walks these tables sequentially: from shared
+// memory each access costs a few cycles instead of a global round trip).
+struct SmemPlan {
+  size_t counts, sexp, soff, hoff, hlist, quota, lo, sbase, total, load, repl, M, cpre, bytes;
+};
+__host__ __device__ inline SmemPlan smem_plan_layout(int R, int E, int n_slots) {
+  SmemPlan L;
+  size_t o = 0;
+  auto take = [&](size_t n) {
+    const size_t at = o;
+    o = (o + n + 15) / 16 * 16;
+    return at;
+  };
+  L.quota = take((size_t)E * R * 8);
+  L.lo = take((size_t)E * R * 8);
+  L.sbase = take((size_t)E * R * 8);
+  L.total = take((size_t)E * 8);
+  L.load = take((size_t)R * 8);
+  L.M = take((size_t)R * R * 8);
+  L.cpre = take((size_t)R * (E + 1) * 8);
+  L.counts = take((size_t)R * E * 4);
+  L.sexp = take((size_t)(n_slots > 0 ? n_slots : 1) * 4);
+  L.soff = take((size_t)(R + 1) * 4);
+  L.hoff = take((size_t)(E + 1) * 4);
+  L.hlist = take((size_t)(n_slots > 0 ? n_slots : 1) * 4);
+  L.repl = take((size_t)E * 4);
+  L.bytes = o;
+  return L;
+}
+constexpr size_t PLAN_SMEM_MAX = 200 * 1024;
+
+// The planner with its inputs copied to, and its scratch in, shared memory
+// (when they fit in PLAN_SMEM_MAX); the outputs other kernels read (the plan,
+// the prefix tables, the GEMM groups) stay in the workspace.
+__global__ void __launch_bounds__(256) ep_planner_smem_kernel(const PlannerArgs a) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  __shared__ int s_bad;
+  const SmemPlan L = smem_plan_layout(a.R, a.E, a.n_slots);
+  PlannerArgs b = a;
+  int32_t *counts = reinterpret_cast<int32_t *>(sm + L.counts);
+  int32_t *sexp = reinterpret_cast<int32_t *>(sm + L.sexp);
+  int32_t *soff = reinterpret_cast<int32_t *>(sm + L.soff);
+  for (int i = threadIdx.x; i < a.R * a.E; i += blockDim.x) counts[i] = a.counts[i];
+  for (int i = threadIdx.x; i < a.n_slots; i += blockDim.x) sexp[i] = a.slot_experts[i];
+  for (int i = threadIdx.x; i <= a.R; i += blockDim.x) soff[i] = a.slot_offsets[i];
+  __syncthreads();
+  b.counts = counts;
+  b.slot_experts = sexp;
+  b.slot_offsets = soff;
+  b.hoff = reinterpret_cast<int32_t *>(sm + L.hoff);
+  b.hlist = reinterpret_cast<int32_t *>(sm + L.hlist);
+  b.sc.quota = reinterpret_cast<int64_t *>(sm + L.quota);
+  b.sc.lo = reinterpret_cast<int64_t *>(sm + L.lo);
+  b.sc.sbase = reinterpret_cast<int64_t *>(sm + L.sbase);
+  b.sc.total = reinterpret_cast<int64_t *>(sm + L.total);
+  b.sc.load = reinterpret_cast<int64_t *>(sm + L.load);
+  b.sc.repl = reinterpret_cast<int32_t *>(sm + L.repl);
+  b.M = reinterpret_cast<int64_t *>(sm + L.M);
+  b.cpre = reinterpret_cast<int64_t *>(sm + L.cpre);
+  PlanExec x{&s_bad};
+  planner_body(b, x);
+}
+
 }  // namespace
 
 namespace {
@@ -663,7 +728,19 @@ extern "C" int rf_moe_ep_devplan(const int32_t *counts, const int32_t *slot_expe
   const int rc = planner_args(a, counts, slot_experts, slot_offsets, R, E, me, S, n_slots, align, rounds,
                               recv_capacity, back_capacity, rows_capacity, workspace, ws_bytes, "rf_moe_ep_devplan");
   if (rc != RF_OK) return rc;
-  ep_planner_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(a);
+  const size_t smem = smem_plan_layout(R, E, n_slots).bytes;
+  if (smem <= PLAN_SMEM_MAX) {
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+      attr = cudaFuncSetAttribute(ep_planner_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)PLAN_SMEM_MAX);
+    });
+    if (attr != cudaSuccess) return rf::fail(RF_ERR_CUDA, std::string("rf_moe_ep_devplan: ") + cudaGetErrorString(attr));
+    ep_planner_smem_kernel<<<1, 256, smem, (cudaStream_t)stream>>>(a);
+  } else {
+    ep_planner_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(a);
+  }
   return rf::check_launch("rf_moe_ep_devplan");
 }
 

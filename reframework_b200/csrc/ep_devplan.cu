@@ -188,55 +188,67 @@ __host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
   const int R = a.R, E = a.E, me = a.me;
   RfEpDevPlan *P = a.plan;
   int &s_bad = *x.bad;
-  if (x.tid() == 0) {
+  int64_t *quota = a.sc.quota, *lo = a.sc.lo, *sbase = a.sc.sbase, *total = a.sc.total, *load = a.sc.load;
+  const int T0 = x.tid(), NT = x.nthreads();
+  if (T0 == 0) {
     s_bad = 0;
     // the placement: offsets from 0 to n_slots, ascending, this rank's count as laid out
     if (a.slot_offsets[0] != 0 || a.slot_offsets[R] != a.n_slots) s_bad = 1;
     for (int r = 0; r < R; ++r)
       if (a.slot_offsets[r + 1] < a.slot_offsets[r]) s_bad = 1;
     if (!s_bad && a.slot_offsets[me + 1] - a.slot_offsets[me] != a.S) s_bad = 1;
-    int64_t *quota = a.sc.quota, *lo = a.sc.lo, *sbase = a.sc.sbase, *total = a.sc.total, *load = a.sc.load;
-    // holders of every expert, in rank order (CSR)
-    for (int e = 0; e <= E; ++e) a.hoff[e] = 0;
-    for (int r = 0; r < R && !s_bad; ++r)
-      for (int s = a.slot_offsets[r]; s < a.slot_offsets[r + 1]; ++s) {
-        const int e = a.slot_experts[s];
-        if (e < 0 || e >= E) s_bad = 1;
-        else a.hoff[e + 1] += 1;
-      }
-    for (int e = 0; e < E; ++e) a.hoff[e + 1] += a.hoff[e];
-    for (int e = 0; e < E; ++e) total[e] = 0;
-    for (int e = 0; e < E; ++e) a.sc.repl[e] = a.hoff[e];  // fill cursors
-    for (int r = 0; r < R && !s_bad; ++r)
-      for (int s = a.slot_offsets[r]; s < a.slot_offsets[r + 1]; ++s) a.hlist[a.sc.repl[a.slot_experts[s]]++] = r;
-    for (int e = 0; e < E && !s_bad; ++e)  // no rank holds an expert twice
-      for (int h = a.hoff[e] + 1; h < a.hoff[e + 1]; ++h)
-        if (a.hlist[h] == a.hlist[h - 1]) s_bad = 1;
-    for (int r = 0; r < R; ++r)
-      for (int e = 0; e < E; ++e) {
-        const int32_t c = a.counts[(int64_t)r * E + e];
-        if (c < 0) s_bad = 1;
-        total[e] += c;
-      }
-    for (int e = 0; e < E; ++e)
-      if (a.hoff[e + 1] == a.hoff[e] && total[e] != 0) s_bad = 1;
-    // per-holder quota
-    int nrep = 0;
-    for (int64_t i = 0; i < (int64_t)E * R; ++i) quota[i] = 0;
-    for (int r = 0; r < R; ++r) load[r] = 0;
-    for (int e = 0; e < E && !s_bad; ++e) {
-      const int h0 = a.hoff[e], k = a.hoff[e + 1] - h0;
-      if (k == 0) continue;
-      if (k == 1) {
-        quota[(int64_t)e * R + a.hlist[h0]] = total[e];
-      } else {
-        a.sc.repl[nrep++] = e;
-        for (int i = 0; i < k; ++i) quota[(int64_t)e * R + a.hlist[h0 + i]] = total[e] / k + (i < total[e] % k ? 1 : 0);
-      }
+  }
+  x.sync();
+  // per expert (one thread each): holder count, routed total, bad counts
+  for (int s = T0; s < a.n_slots && !s_bad; s += NT)
+    if (a.slot_experts[s] < 0 || a.slot_experts[s] >= E) s_bad = 1;
+  for (int e = T0; e < E; e += NT) {
+    int k = 0;
+    for (int s = 0; s < a.n_slots && !s_bad; ++s) k += a.slot_experts[s] == e;
+    a.hoff[e + 1] = k;
+    int64_t t = 0;
+    for (int r = 0; r < R; ++r) {
+      const int32_t c = a.counts[(int64_t)r * E + e];
+      if (c < 0) s_bad = 1;
+      t += c;
     }
+    total[e] = t;
+  }
+  x.sync();
+  if (T0 == 0) {
+    a.hoff[0] = 0;
+    for (int e = 0; e < E; ++e) a.hoff[e + 1] += a.hoff[e];
+  }
+  x.sync();
+  // holders of every expert, in rank order (CSR); no rank holds an expert
+  // twice; every routed expert has a holder; the initial quotas
+  for (int e = T0; e < E && !s_bad; e += NT) {
+    int h = a.hoff[e];
+    for (int r = 0; r < R; ++r)
+      for (int s = a.slot_offsets[r]; s < a.slot_offsets[r + 1]; ++s)
+        if (a.slot_experts[s] == e) a.hlist[h++] = r;
+    const int h0 = a.hoff[e], k = a.hoff[e + 1] - h0;
+    for (int i = h0 + 1; i < h0 + k; ++i)
+      if (a.hlist[i] == a.hlist[i - 1]) s_bad = 1;
+    if (k == 0 && total[e] != 0) s_bad = 1;
+    for (int r = 0; r < R; ++r) quota[(int64_t)e * R + r] = 0;
+    if (k == 1) quota[(int64_t)e * R + a.hlist[h0]] = total[e];
+    for (int i = 0; k > 1 && i < k; ++i) quota[(int64_t)e * R + a.hlist[h0 + i]] = total[e] / k + (i < total[e] % k ? 1 : 0);
+  }
+  x.sync();
+  for (int r = T0; r < R && !s_bad; r += NT) {
+    int64_t l = 0;
+    for (int e = 0; e < E; ++e) l += quota[(int64_t)e * R + r];
+    load[r] = l;
+  }
+  x.sync();
+  if (T0 == 0 && !s_bad) {
+    // the replicated experts, stable-sorted by total (descending), then the
+    // water-filled split of each, in that order, for `rounds` passes
+    int nrep = 0;
     for (int e = 0; e < E; ++e)
-      for (int r = 0; r < R; ++r) load[r] += quota[(int64_t)e * R + r];
-    for (int i = 1; i < nrep; ++i) {  // stable sort of the replicated experts by total, descending
+      if (a.hoff[e + 1] - a.hoff[e] > 1) a.sc.repl[nrep++] = e;
+    for (int i = 1; i < nrep; ++i) {
       const int v = a.sc.repl[i];
       int j = i;
       while (j > 0 && total[a.sc.repl[j - 1]] < total[v]) {
@@ -268,15 +280,16 @@ __host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
       }
       if (!changed) break;
     }
-    // runs: holder h of expert e covers global rows [lo, lo + quota) (rank order)
-    for (int e = 0; e < E; ++e) {
-      int64_t acc = 0, src = 0;
-      for (int r = 0; r < R; ++r) {
-        lo[(int64_t)e * R + r] = acc;
-        acc += quota[(int64_t)e * R + r];
-        sbase[(int64_t)e * R + r] = src;
-        src += a.counts[(int64_t)r * E + e];
-      }
+  }
+  x.sync();
+  // runs: holder h of expert e covers global rows [lo, lo + quota) (rank order)
+  for (int e = T0; e < E && !s_bad; e += NT) {
+    int64_t acc = 0, src = 0;
+    for (int r = 0; r < R; ++r) {
+      lo[(int64_t)e * R + r] = acc;
+      acc += quota[(int64_t)e * R + r];
+      sbase[(int64_t)e * R + r] = src;
+      src += a.counts[(int64_t)r * E + e];
     }
   }
   x.sync();

@@ -267,9 +267,21 @@ __host__ __device__ constexpr uint32_t pair_idesc_base() {
          ((std::is_same<T, __nv_bfloat16>::value ? 1u : 0u) << 10) | ((uint32_t)(256 >> 4) << 24);
 }
 
-template <typename T, bool GATED, int ACT>
+struct PairNoRemote {};
+
+__device__ __forceinline__ void st_release_sys_pair(int32_t *p, int32_t v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// REMOTE (down GEMM of the expert-parallel layer, groups = this rank's local
+// slots): each output row goes to its token's rank over NVLink, at that
+// rank's permuted row (rf::RemoteOut), and the launch's last CTA raises the
+// return flags in every rank.
+template <typename T, bool GATED, int ACT, bool REMOTE = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
-    tc_pair_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ TokMaps tmX, const PairArgs p) {
+    tc_pair_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ TokMaps tmX, const PairArgs p,
+                 const __grid_constant__ std::conditional_t<REMOTE, rf::RemoteOut, PairNoRemote> ro) {
+  static_assert(!REMOTE || !GATED, "remote stores: down GEMM only");
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t *sA = smem;
@@ -634,6 +646,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             const int k16 = (etid & 7) * 16;
             const int f = fb * 256 + (int)rank * 128 + k16;
             const T *arow = p.addend ? reinterpret_cast<const T *>(p.addend) + (int64_t)(row0 + tok) * p.N : nullptr;
+            if constexpr (REMOTE) {  // source rank of local row k of slot s, and the row there
+              const int64_t k = (int64_t)(row0 + tok) - g_row0[s];
+              const int64_t *cj = ro.cj + (int64_t)s * (ro.R + 1);
+              int lo = 0, hi = ro.R - 1;
+              while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (cj[mid] <= k) lo = mid;
+                else hi = mid - 1;
+              }
+              orow = reinterpret_cast<T *>(ro.dst[lo]) + (ro.ps[(int64_t)lo * ro.S + s] + (k - cj[lo])) * p.N;
+            }
 #pragma unroll
             for (int v = 0; v < 2; ++v) {
               if (f + 8 * v >= p.N) break;
@@ -660,6 +683,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, P_TMEM_COLS);
   }
+  if constexpr (REMOTE) {
+    if (threadIdx.x == 0) {
+      __threadfence_system();  // this CTA's peer stores, visible to every GPU, before the count
+      const uint32_t prev = atomicAdd(ro.done, 1u);
+      if (prev == gridDim.x - 1) {  // last CTA: every row of the launch has landed
+        __threadfence_system();
+        for (int d = 0; d < ro.R; ++d) st_release_sys_pair(ro.flag[d], ro.epoch);
+        *ro.done = 0u;
+      }
+    }
+  }
 #undef TQF
 #undef TQE
 #undef FULL
@@ -668,9 +702,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
 #undef TEMPTY
 }
 
-template <typename T, bool GATED, int ACT>
-int launch_pair_t(const CUtensorMap &mw, const TokMaps &mx, const PairArgs &p, cudaStream_t st) {
-  auto kern = tc_pair_gemm<T, GATED, ACT>;
+template <typename T, bool GATED, int ACT, bool REMOTE = false>
+int launch_pair_t(const CUtensorMap &mw, const TokMaps &mx, const PairArgs &p, cudaStream_t st,
+                  const rf::RemoteOut *remote = nullptr) {
+  auto kern = tc_pair_gemm<T, GATED, ACT, REMOTE>;
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
   static int clusters = 0;
@@ -695,13 +730,19 @@ int launch_pair_t(const CUtensorMap &mw, const TokMaps &mx, const PairArgs &p, c
     return -1;
   }
   if (clusters < 1) return -1;
-  kern<<<2 * clusters, P_THREADS, P_SMEM_BYTES, st>>>(mw, mx, p);
-  return rf::check_launch(GATED ? "tensor-core gated GEMM (CTA pairs)" : "tensor-core down GEMM (CTA pairs)");
+  if constexpr (REMOTE) {
+    kern<<<2 * clusters, P_THREADS, P_SMEM_BYTES, st>>>(mw, mx, p, *remote);
+  } else {
+    kern<<<2 * clusters, P_THREADS, P_SMEM_BYTES, st>>>(mw, mx, p, PairNoRemote{});
+  }
+  return rf::check_launch(REMOTE ? "tensor-core down GEMM with peer stores (CTA pairs)"
+                                 : GATED ? "tensor-core gated GEMM (CTA pairs)" : "tensor-core down GEMM (CTA pairs)");
 }
 
 template <typename T>
 int launch_pair_dt(const rf::GroupedGemmArgs &g, bool gated, const CUtensorMap &mw, const TokMaps &mx,
                    const PairArgs &p, cudaStream_t st) {
+  if (!gated && g.remote) return launch_pair_t<T, false, 0, true>(mw, mx, p, st, g.remote);
   if (!gated) return launch_pair_t<T, false, 0>(mw, mx, p, st);
   if (g.act == RF_ACT_SILU) return launch_pair_t<T, true, RF_ACT_SILU>(mw, mx, p, st);
   if (g.act == RF_ACT_GELU) return launch_pair_t<T, true, RF_ACT_GELU>(mw, mx, p, st);
@@ -714,7 +755,9 @@ namespace rf {
 
 int launch_pair_grouped_gemm(const GroupedGemmArgs &g, bool gated, cudaStream_t st) {
   if (g.dtype != RF_BF16 && g.dtype != RF_F16) return -1;
-  if (g.gather_src || g.remote) return -1;
+  if (g.gather_src) return -1;
+  if (g.remote && (gated || g.slot || g.groups || g.addend || g.remote->R < 1 || g.remote->R > rf::REMOTE_MAX_RANKS))
+    return -1;
   if (g.Kdim % 8 || g.N % 8 || g.n_groups < 1 || g.n_groups > P_MAX_GROUPS || g.rows_capacity < 1) return -1;
   if ((uintptr_t)g.a % 16 || (uintptr_t)g.w % 16 || (uintptr_t)g.out % 16) return -1;
   if (!g.offsets || !g.counts) return -1;

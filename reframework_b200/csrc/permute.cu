@@ -13,7 +13,11 @@
 //   3. gather_rows      x_perm[row] = x[src_slot[row] / K] (zero on pad rows),
 //                       one warp per row with 16-byte vector copies
 // The first two kernels touch only 4-byte ids; the gather is the HBM-bound part
-// (reads and writes T*K*H elements).
+// (reads and writes T*K*H elements).  A decode-sized call with the gather (one
+// block of pairs, at most 256 experts) runs as one launch instead,
+// permute_gather_single: every block ranks the pairs itself and then copies
+// its share of the rows.
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -219,6 +223,138 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint8_t *src, co
   }
 }
 
+// Decode-sized permute with the gather in the same launch (at most CHUNK
+// pairs, at most FUSED_MAX_E experts).  Every block ranks all the pairs in its
+// own shared memory (a few hundred ids: the single-block permute_scatter
+// algorithm, same stable order), block 0 writes the permutation, and then all
+// blocks copy rows: row r of expert e (found by a binary search of the padded
+// offsets) is x[pair / K] for its pair, or zeros on pad rows.  This replaces
+// the scatter + gather pair of launches when a decode step's permute is
+// latency-bound.
+constexpr int FUSED_MAX_E = 256;
+
+__global__ void __launch_bounds__(PT) permute_gather_single(const int32_t *ids, int64_t n, int E, int align,
+                                                            int64_t K, const uint8_t *x, int64_t row_bytes,
+                                                            int32_t *offsets_out, int32_t *counts_out,
+                                                            int32_t *row_of_slot, int32_t *src_slot,
+                                                            uint8_t *x_perm) {
+  __shared__ int s_tot[FUSED_MAX_E];      // expert totals
+  __shared__ int s_off[FUSED_MAX_E + 1];  // padded exclusive offsets; [E] = rows used
+  __shared__ int s_cb[FUSED_MAX_E];       // exclusive prefix of the totals (compact row base)
+  __shared__ int s_wc[PW * FUSED_MAX_E];  // per-warp counts, then per-warp cursors
+  __shared__ int s_tmp[PW];
+  __shared__ int s_src[CHUNK];            // pair of each real row, in compact row order
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool lead = blockIdx.x == 0;
+  const int64_t w0 = (int64_t)warp * SUB;
+  const int64_t w1 = min(n, w0 + SUB);
+  int my_e[PER_LANE];
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    const int64_t i = w0 + j * 32 + lane;
+    int e = -1;
+    if (i < w1) {
+      e = ids[i];
+      if (e < 0 || e >= E) {
+        if (lead) rf_report(RF_DEV_BAD_EXPERT_ID);
+        e = -1;
+      }
+    }
+    my_e[j] = e;
+  }
+  for (int i = threadIdx.x; i < PW * E; i += PT) s_wc[i] = 0;
+  __syncthreads();
+  int *wc = s_wc + warp * E;
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    const int e = my_e[j];
+    const unsigned grp = __match_any_sync(0xffffffffu, e);
+    if (lane == __ffs(grp) - 1 && e >= 0) wc[e] += __popc(grp);
+    __syncwarp();
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += PT) {
+    int tot = 0;
+    for (int w = 0; w < PW; ++w) tot += s_wc[w * E + e];
+    s_tot[e] = tot;
+    s_cb[e] = tot;
+    s_off[e] = (tot + align - 1) / align * align;
+  }
+  __syncthreads();
+  const int used = block_exclusive_scan(s_off, E, s_tmp);
+  block_exclusive_scan(s_cb, E, s_tmp);
+  if (threadIdx.x == 0) s_off[E] = used;
+  if (lead) {
+    for (int e = threadIdx.x; e < E; e += PT) {
+      offsets_out[e] = s_off[e];
+      counts_out[e] = s_tot[e];
+    }
+    if (threadIdx.x == 0) offsets_out[E] = used;
+    for (int e = warp; e < E; e += PW) {  // pad rows of every expert
+      const int p0 = s_off[e] + s_tot[e];
+      const int p1 = s_off[e] + (s_tot[e] + align - 1) / align * align;
+      for (int r = p0 + lane; r < p1; r += 32) src_slot[r] = -1;
+    }
+  }
+  for (int e = threadIdx.x; e < E; e += PT) {
+    int run = s_off[e];
+    for (int w = 0; w < PW; ++w) {
+      const int c = s_wc[w * E + e];
+      s_wc[w * E + e] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int j = 0; j < PER_LANE; ++j) {
+    const int64_t i = w0 + j * 32 + lane;
+    const int e = my_e[j];
+    const unsigned grp = __match_any_sync(0xffffffffu, e);
+    const int leader = __ffs(grp) - 1;
+    int row = -1;
+    if (e >= 0) row = wc[e] + __popc(grp & lt);
+    __syncwarp();
+    if (lane == leader && e >= 0) wc[e] += __popc(grp);
+    __syncwarp();
+    if (i < w1) {
+      if (row >= 0) s_src[s_cb[e] + (row - s_off[e])] = (int)i;
+      if (lead) {
+        row_of_slot[i] = row;
+        if (row >= 0) src_slot[row] = (int32_t)i;
+      }
+    }
+  }
+  __syncthreads();
+  // the gather: one warp per row, 16-byte vectors
+  const int64_t vecs = row_bytes / 16;
+  const int64_t warps = (int64_t)gridDim.x * PW;
+  for (int64_t r = (int64_t)blockIdx.x * PW + warp; r < used; r += warps) {
+    int lo = 0, hi = E - 1;  // the last expert whose segment starts at or before r
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_off[mid] <= r) lo = mid;
+      else hi = mid - 1;
+    }
+    const int64_t jrow = r - s_off[lo];
+    uint4 *d = reinterpret_cast<uint4 *>(x_perm + r * row_bytes);
+    if (jrow >= s_tot[lo]) {
+      for (int64_t v = lane; v < vecs; v += 32) d[v] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const uint4 *q = reinterpret_cast<const uint4 *>(x + (int64_t)(s_src[s_cb[lo] + jrow] / K) * row_bytes);
+    int64_t v = lane;
+    for (; v + 96 < vecs; v += 128) {
+      uint4 t[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) t[u] = __ldg(q + v + 32 * u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) d[v + 32 * u] = t[u];
+    }
+    for (; v < vecs; v += 32) d[v] = __ldg(q + v);
+  }
+}
+
 int launch_gather(const void *src, const int32_t *index, int64_t index_div, int64_t n_max,
                   const int32_t *n_dev, int64_t row_bytes, void *dst, cudaStream_t st) {
   if (n_max <= 0) return RF_OK;
@@ -245,6 +381,17 @@ int launch_permute(const int32_t *topk_ids, int64_t n, int64_t K, int64_t E, int
     return RF_OK;
   }
   const int nblk = (int)((n + CHUNK - 1) / CHUNK);
+  if (nblk == 1 && x_perm && E <= FUSED_MAX_E) {
+    // decode-sized: rank and gather in one launch (grid sized for the padded
+    // rows, at most two blocks per SM; every block ranks the pairs itself)
+    const int64_t rows_cap = n + E * (align - 1);
+    const int64_t blocks = std::min<int64_t>((rows_cap + PW - 1) / PW, (int64_t)rf::num_sms() * 2);
+    permute_gather_single<<<(int)blocks, PT, 0, st>>>(topk_ids, n, (int)E, (int)align, K,
+                                                       (const uint8_t *)x, H * (int64_t)rf::dtype_size(dtype),
+                                                       expert_offsets, expert_counts, row_of_slot, src_slot,
+                                                       (uint8_t *)x_perm);
+    return rf::check_launch((nm + "(rank+gather)").c_str());
+  }
   if (nblk > 1) {
     // permute_hist writes every one of the nblk*E words the scatter reads
     permute_hist<<<nblk, PT, E * sizeof(int), st>>>(topk_ids, n, (int)E, block_counts);
@@ -320,9 +467,6 @@ static __device__ __align__(256) int32_t g_noalloc_block_counts[kNoAllocScratchW
 // Device address of g_noalloc_block_counts, fetched once per device.  In host
 // code the array's name is only a host-side handle, so the kernels must be
 // given this address instead.  The cache is keyed by device ordinal and lives
-// as long as the process: after cudaDeviceReset the module may load at
-// another address, so the header tells callers not to use this entry point
-// past a reset.  The cache is keyed by device ordinal and lives
 // as long as the process: after cudaDeviceReset the module may load at
 // another address, so the header tells callers not to use this entry point
 // past a reset.

@@ -168,6 +168,50 @@ def test_permute_random_stable(T, Kk, E, align):
     assert np.array_equal(got, order)
 
 
+@pytest.mark.parametrize("align", [1, 128])
+@pytest.mark.parametrize("T,Kk,E,dtype", [
+    (1, 1, 1, torch.bfloat16), (37, 3, 5, torch.float32), (64, 4, 60, torch.bfloat16),
+    (256, 4, 256, torch.float16),   # the largest decode-sized case: 1024 pairs, 256 experts
+    (256, 4, 257, torch.bfloat16),  # one expert past it: separate scatter and gather launches
+    (300, 4, 60, torch.bfloat16),   # 1200 pairs: several blocks
+])
+def test_permute_with_gather_random(T, Kk, E, dtype, align):
+    """The permute with its row gather (one launch for decode-sized calls, two
+    or three otherwise): the stable order of the oracle, x_perm rows equal to
+    the token rows, zeros on pad rows, and every pair's row."""
+    g = torch.Generator().manual_seed(T * 7 + E)
+    ids = torch.randint(0, E, (T, Kk), generator=g, dtype=torch.int32)
+    if T > 10:
+        ids[: T // 3, 0] = E - 1  # a heavy expert
+    x = torch.randn(T, 96, generator=g).to(dtype)
+    p = K.permute(ids.to(DEV), E, align=align, x=x.to(DEV))
+    counts, order = O.permutation(ids.numpy(), E)
+    assert np.array_equal(p.counts.cpu().numpy(), counts)
+    off = p.offsets.cpu().numpy()
+    assert np.all(off[:-1] % align == 0) and off[-1] == sum((c + align - 1) // align * align for c in counts)
+    src = p.src_slot.cpu().numpy()
+    ros = p.row_of_slot.cpu().numpy()
+    got = np.concatenate([src[off[e]:off[e] + counts[e]] for e in range(E)])
+    assert np.array_equal(got, order)
+    assert np.array_equal(src[ros], np.arange(T * Kk))
+    used = int(off[-1])
+    rows = torch.from_numpy(src[:used]).long()
+    valid = rows >= 0
+    assert int(valid.sum()) == T * Kk
+    xp = p.x_perm.cpu()[:used]
+    assert torch.equal(xp[valid], x[rows[valid] // Kk])
+    assert torch.count_nonzero(xp[~valid]) == 0
+
+
+def test_bad_expert_id_in_decode_permute_with_gather():
+    ids = torch.tensor([[0, 9], [3, 1]], dtype=torch.int32, device=DEV)  # 9 >= E
+    x = torch.randn(2, 64, dtype=torch.bfloat16, device=DEV)
+    p = K.permute(ids, 4, x=x)
+    assert p.row_of_slot.cpu().tolist()[1] == -1
+    assert p.counts.cpu().tolist() == [1, 1, 0, 1]
+    assert _lib.device_status() == 1
+
+
 def _segments(counts, align=128):
     offs = [0]
     for c in counts:

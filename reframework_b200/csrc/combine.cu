@@ -326,7 +326,7 @@ extern "C" int rf_moe_combine_rmsnorm(const void *y, const int32_t *row_of_slot,
   RF_CHECK_ARG((uintptr_t)y % 16 == 0 && (uintptr_t)residual_out % 16 == 0 && (uintptr_t)normed_out % 16 == 0 &&
                    (uintptr_t)shared_y % 16 == 0 && (uintptr_t)residual % 16 == 0,
                "rf_moe_combine_rmsnorm: buffers must be 16-byte aligned");
-  RF_CHECK_ARG(normed_out != residual_out, "rf_moe_combine_rmsnorm: the two outputs must not alias");
+  RF_CHECK_ARG(T == 0 || normed_out != residual_out, "rf_moe_combine_rmsnorm: the two outputs must not alias");
   if (T == 0) return RF_OK;
   CombineArgs a{y, row_of_slot, topk_weights, shared_y, shared_scale, residual, residual_out, T, (int)K, (int)H,
                 0, mode, normed_out, norm_weight, norm_bias, eps};

@@ -924,7 +924,8 @@ int grouped_gemm(const void *a, const void *w, void *out, const int32_t *offsets
                nm + ": bad sizes");
   RF_CHECK_ARG(Kdim < (1 << 30) && N < (1 << 30) && rows_capacity < ((int64_t)1 << 31),
                nm + ": sizes exceed int32");
-  RF_CHECK_ARG(a && w && out && offsets && counts, nm + ": null pointer");
+  // no rows (an empty batch): the row buffers may be empty, possibly null
+  RF_CHECK_ARG((rows_capacity == 0 || (a && out)) && w && offsets && counts, nm + ": null pointer");
   const int64_t G = groups ? n_groups : E;
   RF_CHECK_ARG(G >= 0 && G <= 65535, nm + ": bad group count");
   if (G == 0 || rows_capacity == 0) return RF_OK;
@@ -1032,7 +1033,7 @@ extern "C" int rf_moe_grouped_gemm_down_add(const void *h, const void *w2, void 
                                             int64_t n_groups, int64_t E, int64_t num_slots,
                                             int64_t rows_capacity, int64_t H, int64_t I, int dtype,
                                             rf_stream_t stream) {
-  RF_CHECK_ARG(addend, "rf_moe_grouped_gemm_down_add: null addend");
+  RF_CHECK_ARG(addend || rows_capacity == 0, "rf_moe_grouped_gemm_down_add: null addend");
   return grouped_gemm(h, w2, y, expert_offsets, expert_counts, expert_slot, groups, n_groups, E,
                       num_slots, rows_capacity, I, H, dtype, RF_ACT_SILU, false, stream,
                       "rf_moe_grouped_gemm_down_add", addend);

@@ -445,8 +445,8 @@ extern "C" int rf_moe_permute(const int32_t *topk_ids, int64_t T, int64_t K, int
                "rf_moe_permute: null output");
   RF_CHECK_ARG(workspace_bytes >= rf_moe_permute_workspace_size(n, E) && workspace,
                "rf_moe_permute: workspace too small");
-  RF_CHECK_ARG(!x_perm || (x && rf::valid_dtype(dtype) && H > 0 &&
-                           (H * (int64_t)rf::dtype_size(dtype)) % 16 == 0),
+  RF_CHECK_ARG(!x_perm || n == 0 || (x && rf::valid_dtype(dtype) && H > 0 &&
+                                      (H * (int64_t)rf::dtype_size(dtype)) % 16 == 0),
                "rf_moe_permute: gather needs x, a dtype and H*elsize % 16 == 0");
   return launch_permute(topk_ids, n, K, E, align, x, dtype, H, expert_offsets, expert_counts,
                         row_of_slot, src_slot, x_perm, reinterpret_cast<int32_t *>(workspace),
@@ -511,8 +511,8 @@ extern "C" int rf_moe_permute_noalloc(const int32_t *topk_ids, int64_t T, int64_
                         std::to_string(kNoAllocScratchWords) + "; use rf_moe_permute with a workspace");
   RF_CHECK_ARG(expert_offsets && expert_counts && (n == 0 || (row_of_slot && src_slot)),
                "rf_moe_permute_noalloc: null output");
-  RF_CHECK_ARG(!x_perm || (x && rf::valid_dtype(dtype) && H > 0 &&
-                           (H * (int64_t)rf::dtype_size(dtype)) % 16 == 0),
+  RF_CHECK_ARG(!x_perm || n == 0 || (x && rf::valid_dtype(dtype) && H > 0 &&
+                                      (H * (int64_t)rf::dtype_size(dtype)) % 16 == 0),
                "rf_moe_permute_noalloc: gather needs x, a dtype and H*elsize % 16 == 0");
   int32_t *block_counts = nullptr;
   int rc = noalloc_scratch(&block_counts);

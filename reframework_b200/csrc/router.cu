@@ -413,9 +413,10 @@ extern "C" int rf_moe_router_topk(const void *x, int x_dtype, const void *gate, 
   RF_CHECK_ARG(gate || (H == E && !shared_gate),
                "rf_moe_router_topk: without a gate, x holds the [T,E] logits (H == E)");
   RF_CHECK_ARG(entropy_k_min <= K, "rf_moe_router_topk: entropy_k_min > K");
-  RF_CHECK_ARG(topk_weights && (topk_ids32 || topk_ids64), "rf_moe_router_topk: missing outputs");
+  // an empty batch (T == 0) has empty, possibly null, outputs and returns at once
+  RF_CHECK_ARG(T == 0 || (topk_weights && (topk_ids32 || topk_ids64)), "rf_moe_router_topk: missing outputs");
   RF_CHECK_ARG(T == 0 || x, "rf_moe_router_topk: null input");
-  RF_CHECK_ARG(!shared_gate || shared_scale, "rf_moe_router_topk: shared_gate needs shared_scale");
+  RF_CHECK_ARG(T == 0 || !shared_gate || shared_scale, "rf_moe_router_topk: shared_gate needs shared_scale");
   RF_CHECK_ARG((!gate || ((uintptr_t)x % 16) == 0) && ((uintptr_t)gate % 16) == 0 &&
                    ((uintptr_t)shared_gate % 16) == 0,
                "rf_moe_router_topk: x / gate must be 16-byte aligned");

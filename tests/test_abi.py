@@ -118,3 +118,25 @@ def test_no_multicast_or_batched_copy_in_sources():
         if f.endswith((".cu", ".cuh", ".h")):
             text = open(os.path.join(csrc, f)).read()
             assert not bad.search(text), f
+
+
+def test_empty_batch_needs_no_row_buffers():
+    """An empty batch (T == 0): the router, the grouped GEMMs (no rows) and the
+    combine accept empty, null row buffers and return at once without a GPU
+    call, as torch does for zero-row tensors in the reference layer."""
+    lib = _lib.lib()
+    dummy = ctypes.create_string_buffer(64)
+    p = ctypes.cast(dummy, ctypes.c_void_p)
+    bf16 = _lib.RF_BF16
+    # router: x, weights and ids all null for T == 0 (with a shared gate, no shared_scale)
+    assert lib.rf_moe_router_topk(None, bf16, p, bf16, None, 0, 64, 8, 2, 1, -1, 0, p, None,
+                                  None, None, None, None, None, 0, None) == 0
+    # grouped GEMMs over zero rows: no activation / output buffers
+    assert lib.rf_moe_grouped_gemm_gated(None, p, None, p, p, None, None, 0, 8, 8, 0, 64, 32, bf16, 0, None) == 0
+    assert lib.rf_moe_grouped_gemm_down_add(None, p, None, None, p, p, None, None, 0, 8, 8, 0, 64, 32,
+                                            bf16, None) == 0
+    # combine of zero tokens
+    assert lib.rf_moe_combine(None, None, None, 0, 2, 64, bf16, None, None, None, 0, 0, None, None) == 0
+    # combine + RMSNorm of zero tokens: both (empty) outputs may be null
+    assert lib.rf_moe_combine_rmsnorm(None, None, None, 0, 2, 64, bf16, None, None, None, 0, p, None, 1e-6,
+                                      None, None, None) == 0

@@ -235,6 +235,31 @@ LAUNCHES_PER_FORWARD = 8
 EP_LAUNCHES_PER_FORWARD = 14
 
 
+def ep_roofline(layer, cfg, traces, maxrank):
+    """Roofline of the dominant kernel of an expert-parallel step: this rank's
+    gated GEMM (its local rows x 2I x H), timed live by the CUDA events the
+    layer records at its phase boundaries in every timed step.  Every rank
+    computes its own; the line reports the slowest rank's launch."""
+    durs = []
+    for tr in traces:
+        marks = {b[0]: a[1].elapsed_time(b[1]) for a, b in zip(tr, tr[1:])}
+        if "gated GEMM" in marks:
+            durs.append(marks["gated GEMM"])
+    st = getattr(layer, "_dp", None) or {}
+    rows = int(st["seg_cnt"].sum().item()) if "seg_cnt" in st else 0
+    ms = statistics.mean(durs) if durs else 0.0
+    flop = 2.0 * rows * cfg.hidden * 2 * cfg.inter
+    ach = flop / (ms / 1e3) / 1e12 if ms > 0 else 0.0
+    # the slowest rank: the lowest achieved rate (max over ranks of its negation)
+    worst = -maxrank(-ach)
+    bf16_peak, _, src = peaks()
+    return {"kernel": "grouped gated GEMM (K3) over this rank's expert rows", "bound": "tensor",
+            "achieved": worst, "peak": bf16_peak, "unit": "TFLOP/s", "frac": worst / bf16_peak,
+            "peak_source": f"{src} bf16 burst (cuBLAS 8192^3, best of 10)",
+            "achieved_rank0": ach, "rows_rank0": rows, "launch_ms_rank0": ms,
+            "traffic": None, "traffic_source": "no ncu capture of the expert-parallel launch"}
+
+
 def ep_launches(layer) -> int:
     """Launches of one EP forward (host-planned exchange: no planner kernel, and
     one more gather when replicas reorder the sent rows)."""
@@ -302,7 +327,7 @@ def run_gpu(args):
         if rank == 0:
             clocks.start()  # before the barrier: no rank may start timing while rank 0 sets up sampling
         barrier()
-        step_ms, stage_ms = [], []
+        step_ms, stage_ms, phase_traces = [], [], []
         for _ in range(args.steps):
             flush.zero_()
             if stage_fn:
@@ -312,11 +337,15 @@ def run_gpu(args):
             else:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
+                layer.trace = []  # phase-boundary events (the gated GEMM's live duration)
                 e0.record()
                 fwd(x)
                 e1.record()
                 stage_ms.append([e0, e1])
+                phase_traces.append(layer.trace)
         barrier()
+        if world > 1:
+            layer.trace = None
         for ev in stage_ms:
             step_ms.append(ev[0].elapsed_time(ev[-1]))
         # ---- e2e through the public API with host buffers (serving-style pipeline)
@@ -394,6 +423,8 @@ def run_gpu(args):
         res["hbm"] = {"permute_gbs": byt_perm / (per["permute"] / 1e3) / 1e9,
                       "combine_gbs": (rows + T) * cfg.hidden * 2 / (per["combine"] / 1e3) / 1e9,
                       "peak_gbs": hbm_peak}
+    if world > 1:
+        res["roofline"] = ep_roofline(layer, cfg, phase_traces, maxrank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(cfg, layer, budget_s=args.cpu_budget)
     if world > 1:

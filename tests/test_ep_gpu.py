@@ -115,6 +115,15 @@ with torch.no_grad():
     assert sum(len(s) for s in pl.slots) > cfg.experts  # at least one replica somewhere
     bal = ep(x[lo:hi])
 assert torch.equal(bal, ref[lo:hi]), "rebalanced EP output differs"
+# an uneven step: the last rank holds every token, the others an empty batch
+ep_un = EPFusedMoE.from_full(full, world, rank, token_sharded=True)
+ep_un.max_tokens_per_rank = T
+mine = x if rank == world - 1 else x[:0]
+with torch.no_grad():
+    un = ep_un(mine)
+assert un.shape == (mine.shape[0], cfg.hidden)
+assert torch.equal(un, ref[:mine.shape[0]]), "EP step with an empty rank differs"
+ep_un.close()
 from reframework_b200 import _lib
 assert _lib.device_status() == 0, "a kernel set the device error word"
 for m in (ep_rep, ep_sh, ep_nc, ep):

@@ -594,7 +594,7 @@ bool encode(CUtensorMap *m, int dtype, int rank, const void *base, const cuuint6
             const cuuint64_t *strides, const cuuint32_t *box) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint32_t estr[3] = {1, 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};  // element strides, one per dimension (rank <= 5)
   const CUtensorMapDataType dt = dtype == RF_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : dtype == RF_F16  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                     : CU_TENSOR_MAP_DATA_TYPE_UINT8;  // int8 codes: plain bytes

@@ -90,6 +90,46 @@ __host__ __device__ void waterfill_dev(int64_t n, const int64_t *base, int m, in
   for (int pos = 0; pos < m; ++pos) out[order[pos]] = give[pos];
 }
 
+#ifdef __CUDA_ARCH__
+// waterfill_dev on one warp, one lane per holder (m <= 32 holders): lane i
+// passes base[i] and gets out[i].  The same integer steps: a stable sort by
+// base (ranks counted with shuffles), the prefix sums of the sorted loads (a
+// warp scan), k = the largest k' in [2, m] with n + P(k') > loads[k'-1] * k'
+// (else 1: the scalar loop's descent from m stops there), level and the
+// remainder handed to the first sorted positions.
+__device__ int64_t waterfill_warp(int64_t n, int64_t b, int m) {
+  const unsigned full = 0xffffffffu;
+  const int lane = (int)(threadIdx.x & 31);
+  const bool act = lane < m;
+  int rank = 0;  // sorted position of this lane's base (ties keep lane order)
+  for (int j = 0; j < m; ++j) {
+    const int64_t bj = __shfl_sync(full, b, j);
+    rank += (bj < b) || (bj == b && j < lane);
+  }
+  int src = 0;  // the lane whose base sits at sorted position `lane`
+  for (int j = 0; j < m; ++j)
+    if (__shfl_sync(full, rank, j) == lane) src = j;
+  const int64_t ld = __shfl_sync(full, b, src);  // loads[lane]
+  int64_t P = act ? ld : 0;                       // P(lane + 1)
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t v = __shfl_up_sync(full, P, o);
+    if (lane >= o) P += v;
+  }
+  const bool stays = act && lane >= 1 && !(n + P <= ld * (int64_t)(lane + 1));
+  const unsigned keep = __ballot_sync(full, stays);
+  const int k = keep ? 32 - __clz(keep) : 1;
+  const int64_t Pk = __shfl_sync(full, P, k - 1);
+  const int64_t level = (n + Pk) / k;
+  int64_t give = 0;
+  if (lane < k) give = level - ld > 0 ? level - ld : 0;
+  int64_t used = give;
+  for (int o = 16; o > 0; o >>= 1) used += __shfl_xor_sync(full, used, o);
+  const int64_t rem = n - used;
+  if (lane < k && rem > 0) give += rem / k + (lane < rem % k ? 1 : 0);
+  return __shfl_sync(full, give, act ? rank : 0);  // out[lane] = give[rank of lane]
+}
+#endif
+
 struct PlanScratch {  // global scratch of the planner (E x R tables)
   int64_t *quota, *lo, *sbase, *total, *load;
   int32_t *repl;
@@ -118,6 +158,11 @@ struct PlannerArgs {
   PlanScratch sc;               // quota/lo/sbase [E*R], total [E], load [R], repl [E]
   int64_t *M;                   // [R][R]
   int32_t *hoff, *hlist;        // holders CSR: [E+1], [total slots]
+  // the first thread's running sums of this rank's receive side (shared
+  // memory when the planner runs there): per local slot the rows so far, the
+  // rows from sources below this rank and up to it, and the segment starts
+  // ([S], [S], [S], [S+1]); the tables above are only written from these
+  int64_t *tail;
 };
 
 __host__ __device__ int64_t piece_dev(const PlannerArgs &a, int e, int src, int h, int64_t *offset) {
@@ -242,6 +287,75 @@ __host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
     load[r] = l;
   }
   x.sync();
+#ifdef __CUDA_ARCH__
+  if (T0 < 32 && !s_bad) {
+    // the replicated experts, stable-sorted by total (descending), then the
+    // water-filled split of each, in that order, for `rounds` passes: warp 0,
+    // the first lane for the bookkeeping, one lane per holder for the split
+    const unsigned full = 0xffffffffu;
+    int nrep = 0;
+    if (T0 == 0) {
+      for (int e = 0; e < E; ++e)
+        if (a.hoff[e + 1] - a.hoff[e] > 1) a.sc.repl[nrep++] = e;
+      for (int i = 1; i < nrep; ++i) {
+        const int v = a.sc.repl[i];
+        int j = i;
+        while (j > 0 && total[a.sc.repl[j - 1]] < total[v]) {
+          a.sc.repl[j] = a.sc.repl[j - 1];
+          --j;
+        }
+        a.sc.repl[j] = v;
+      }
+    }
+    nrep = __shfl_sync(full, nrep, 0);
+    __syncwarp();
+    for (int it = 0; it < a.rounds; ++it) {
+      int changed = 0, stop = 0;
+      for (int ri = 0; ri < nrep; ++ri) {
+        const int e = a.sc.repl[ri], h0 = a.hoff[e], k = a.hoff[e + 1] - h0;
+        if (k > MAXR) {
+          if (T0 == 0) s_bad = 1;
+          stop = 1;
+          break;
+        }
+        if (k <= 32) {
+          const int h = T0 < k ? a.hlist[h0 + T0] : 0;
+          const int64_t b = T0 < k ? load[h] - quota[(int64_t)e * R + h] : 0;
+          const int64_t q_new = waterfill_warp(total[e], b, k);
+          int ch = 0;
+          if (T0 < k) {
+            int64_t &q = quota[(int64_t)e * R + h];
+            if (q != q_new) {
+              load[h] += q_new - q;
+              q = q_new;
+              ch = 1;
+            }
+          }
+          changed |= __any_sync(full, ch);
+        } else {  // more than 32 holders: the scalar split on the first lane
+          int ch = 0;
+          if (T0 == 0) {
+            int64_t base[MAXR], nq[MAXR], loads[MAXR], give[MAXR];
+            int order[MAXR];
+            for (int i = 0; i < k; ++i) base[i] = load[a.hlist[h0 + i]] - quota[(int64_t)e * R + a.hlist[h0 + i]];
+            waterfill_dev(total[e], base, k, nq, order, loads, give);
+            for (int i = 0; i < k; ++i) {
+              int64_t &q = quota[(int64_t)e * R + a.hlist[h0 + i]];
+              if (q != nq[i]) {
+                load[a.hlist[h0 + i]] += nq[i] - q;
+                q = nq[i];
+                ch = 1;
+              }
+            }
+          }
+          changed |= __shfl_sync(full, ch, 0);
+        }
+        __syncwarp();  // this expert's quotas and loads, seen by every lane
+      }
+      if (stop || !changed) break;
+    }
+  }
+#else
   if (T0 == 0 && !s_bad) {
     // the replicated experts, stable-sorted by total (descending), then the
     // water-filled split of each, in that order, for `rounds` passes
@@ -281,6 +395,7 @@ __host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
       if (!changed) break;
     }
   }
+#endif
   x.sync();
   // runs: holder h of expert e covers global rows [lo, lo + quota) (rank order)
   for (int e = T0; e < E && !s_bad; e += NT) {
@@ -379,8 +494,11 @@ __host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
     P->back_row0[d] = back;
   }
   // receive side: c[s][j], source bounds, slot segments and both prefix tables
+  // (running values kept in the scratch `tail`, never read back from the plan)
+  int64_t *lc = a.tail, *cjm = a.tail + S, *cjm1 = a.tail + 2 * S, *lof = a.tail + 3 * S;
   P->recv_off[0] = 0;
-  for (int j = 0; j < S; ++j) P->lcount[j] = 0;
+  for (int j = 0; j < S; ++j) lc[j] = cjm[j] = cjm1[j] = 0;
+  int64_t roff = 0;
   for (int s = 0; s < R && !bad; ++s) {
     int64_t run = 0;
     for (int j = 0; j < S; ++j) {
@@ -389,21 +507,37 @@ __host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
       int64_t off = 0;
       const int64_t c = piece_dev(a, e, s, me, &off);
       a.pstart[(int64_t)s * S + j] = c > 0 ? a.cpre[(int64_t)s * (E + 1) + e] + off : 0;
-      a.cj_prefix[(int64_t)j * (R + 1) + s] = P->lcount[j];
-      P->lcount[j] += c;
+      a.cj_prefix[(int64_t)j * (R + 1) + s] = lc[j];
+      if (s == me) cjm[j] = lc[j];
+      if (s == me + 1) cjm1[j] = lc[j];
+      lc[j] += c;
       run += c;
     }
     a.cs_prefix[(int64_t)s * (S + 1) + S] = run;
-    P->recv_off[s + 1] = P->recv_off[s] + run;
+    roff += run;
+    P->recv_off[s + 1] = roff;
   }
-  for (int j = 0; j < S; ++j) a.cj_prefix[(int64_t)j * (R + 1) + R] = P->lcount[j];
-  P->loff[0] = 0;
-  for (int j = 0; j < S; ++j) P->loff[j + 1] = P->loff[j] + (P->lcount[j] + a.align - 1) / a.align * a.align;
-  for (int j = 0; j <= S; ++j) P->loff32[j] = (int32_t)P->loff[j];
-  for (int j = 0; j < S; ++j) P->lcount32[j] = (int32_t)P->lcount[j];
-  P->recv_total = P->recv_off[R];
-  P->rows_used = P->loff[S];
-  if (P->recv_total > a.recv_capacity || P->rows_used > a.rows_capacity) bad = 1;
+  for (int j = 0; j < S; ++j) {
+    a.cj_prefix[(int64_t)j * (R + 1) + R] = lc[j];
+    if (me + 1 == R) cjm1[j] = lc[j];
+  }
+  int64_t rows = 0;
+  lof[0] = 0;
+  for (int j = 0; j < S; ++j) {
+    rows += (lc[j] + a.align - 1) / a.align * a.align;
+    lof[j + 1] = rows;
+  }
+  for (int j = 0; j <= S; ++j) {
+    P->loff[j] = lof[j];
+    P->loff32[j] = (int32_t)lof[j];
+  }
+  for (int j = 0; j < S; ++j) {
+    P->lcount[j] = lc[j];
+    P->lcount32[j] = (int32_t)lc[j];
+  }
+  P->recv_total = roff;
+  P->rows_used = rows;
+  if (roff > a.recv_capacity || rows > a.rows_capacity) bad = 1;
   P->overflow = bad;
   if (bad) {
     clear_plan(P, S);
@@ -411,13 +545,12 @@ __host__ __device__ void planner_body(const PlannerArgs &a, PlanExec &x) {
     x.report(RF_DEV_PLAN_OVERFLOW);
   } else {
     for (int j = 0; j < S; ++j) {
-      const int64_t *cj = a.cj_prefix + (int64_t)j * (R + 1);
-      a.loc[j] = (int32_t)(P->loff[j] + cj[me]);
-      a.loc[S + j] = (int32_t)(cj[me + 1] - cj[me]);
-      a.rem[2 * j] = (int32_t)P->loff[j];
-      a.rem[2 * j + 1] = (int32_t)(P->loff[j] + cj[me + 1]);
-      a.rem[2 * S + 2 * j] = (int32_t)cj[me];
-      a.rem[2 * S + 2 * j + 1] = (int32_t)(P->lcount[j] - cj[me + 1]);
+      a.loc[j] = (int32_t)(lof[j] + cjm[j]);
+      a.loc[S + j] = (int32_t)(cjm1[j] - cjm[j]);
+      a.rem[2 * j] = (int32_t)lof[j];
+      a.rem[2 * j + 1] = (int32_t)(lof[j] + cjm1[j]);
+      a.rem[2 * S + 2 * j] = (int32_t)cjm[j];
+      a.rem[2 * S + 2 * j + 1] = (int32_t)(lc[j] - cjm1[j]);
     }
   }
 }
@@ -432,7 +565,7 @@ __global__ void __launch_bounds__(256) ep_planner_kernel(const PlannerArgs a) {
 // one block whose first thread walks these tables sequentially: from shared
 // memory each access costs a few cycles instead of a global round trip).
 struct SmemPlan {
-  size_t counts, sexp, soff, hoff, hlist, quota, lo, sbase, total, load, repl, M, cpre, bytes;
+  size_t counts, sexp, soff, hoff, hlist, quota, lo, sbase, total, load, repl, M, cpre, tail, bytes;
 };
 __host__ __device__ inline SmemPlan smem_plan_layout(int R, int E, int n_slots) {
   SmemPlan L;
@@ -449,6 +582,7 @@ __host__ __device__ inline SmemPlan smem_plan_layout(int R, int E, int n_slots) 
   L.load = take((size_t)R * 8);
   L.M = take((size_t)R * R * 8);
   L.cpre = take((size_t)R * (E + 1) * 8);
+  L.tail = take((size_t)(4 * (n_slots > 0 ? n_slots : 1) + 1) * 8);
   L.counts = take((size_t)R * E * 4);
   L.sexp = take((size_t)(n_slots > 0 ? n_slots : 1) * 4);
   L.soff = take((size_t)(R + 1) * 4);
@@ -488,6 +622,7 @@ __global__ void __launch_bounds__(256) ep_planner_smem_kernel(const PlannerArgs 
   b.sc.repl = reinterpret_cast<int32_t *>(sm + L.repl);
   b.M = reinterpret_cast<int64_t *>(sm + L.M);
   b.cpre = reinterpret_cast<int64_t *>(sm + L.cpre);
+  b.tail = reinterpret_cast<int64_t *>(sm + L.tail);
   PlanExec x{&s_bad};
   planner_body(b, x);
 }
@@ -499,7 +634,7 @@ namespace {
 // One 16-byte-aligned workspace per EP layer: the plan, its two prefix tables
 // and the planner's scratch.
 struct Layout {
-  size_t plan, cs, cj, ps, cpre, quota, lo, sbase, total, load, repl, M, hoff, hlist, loc, rem, bytes;
+  size_t plan, cs, cj, ps, cpre, quota, lo, sbase, total, load, repl, M, hoff, hlist, loc, rem, tail, bytes;
 };
 
 size_t up16(size_t v) { return (v + 15) / 16 * 16; }
@@ -523,6 +658,7 @@ Layout layout_of(int64_t R, int64_t E, int64_t S, int64_t nslots) {
   L.hlist = o; o = up16(o + (size_t)(nslots > 0 ? nslots : 1) * 4);
   L.loc = o; o = up16(o + (size_t)2 * (S > 0 ? S : 1) * 4);
   L.rem = o; o = up16(o + (size_t)4 * (S > 0 ? S : 1) * 4);
+  L.tail = o; o = up16(o + (size_t)(4 * S + 1) * 8);
   L.bytes = o;
   return L;
 }
@@ -728,6 +864,7 @@ int planner_args(PlannerArgs &a, const int32_t *counts, const int32_t *slot_expe
   a.hlist = reinterpret_cast<int32_t *>(w + L.hlist);
   a.loc = reinterpret_cast<int32_t *>(w + L.loc);
   a.rem = reinterpret_cast<int32_t *>(w + L.rem);
+  a.tail = reinterpret_cast<int64_t *>(w + L.tail);
   return RF_OK;
 }
 

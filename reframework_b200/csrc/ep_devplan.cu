@@ -92,41 +92,36 @@ __host__ __device__ void waterfill_dev(int64_t n, const int64_t *base, int m, in
 
 #ifdef __CUDA_ARCH__
 // waterfill_dev on one warp, one lane per holder (m <= 32 holders): lane i
-// passes base[i] and gets out[i].  The same integer steps: a stable sort by
-// base (ranks counted with shuffles), the prefix sums of the sorted loads (a
-// warp scan), k = the largest k' in [2, m] with n + P(k') > loads[k'-1] * k'
-// (else 1: the scalar loop's descent from m stops there), level and the
-// remainder handed to the first sorted positions.
+// passes base[i] and gets out[i].  The same integer steps, each lane working
+// at its own sorted position: its stable rank r (ties keep lane order) and the
+// sum of the sorted loads up to and including it, P(r + 1), come from one
+// pass of shuffles; k = the largest k' in [2, m] with n + P(k') > loads[k'-1]
+// * k' (else 1: where the scalar loop's descent from m stops), then the level
+// and the remainder for the first sorted positions.
 __device__ int64_t waterfill_warp(int64_t n, int64_t b, int m) {
   const unsigned full = 0xffffffffu;
   const int lane = (int)(threadIdx.x & 31);
   const bool act = lane < m;
-  int rank = 0;  // sorted position of this lane's base (ties keep lane order)
+  int rank = 0;
+  int64_t upto = 0;  // P(rank + 1)
   for (int j = 0; j < m; ++j) {
     const int64_t bj = __shfl_sync(full, b, j);
-    rank += (bj < b) || (bj == b && j < lane);
+    const bool before = (bj < b) || (bj == b && j < lane);
+    rank += before;
+    if (before || j == lane) upto += bj;
   }
-  int src = 0;  // the lane whose base sits at sorted position `lane`
-  for (int j = 0; j < m; ++j)
-    if (__shfl_sync(full, rank, j) == lane) src = j;
-  const int64_t ld = __shfl_sync(full, b, src);  // loads[lane]
-  int64_t P = act ? ld : 0;                       // P(lane + 1)
-  for (int o = 1; o < 32; o <<= 1) {
-    const int64_t v = __shfl_up_sync(full, P, o);
-    if (lane >= o) P += v;
-  }
-  const bool stays = act && lane >= 1 && !(n + P <= ld * (int64_t)(lane + 1));
-  const unsigned keep = __ballot_sync(full, stays);
-  const int k = keep ? 32 - __clz(keep) : 1;
-  const int64_t Pk = __shfl_sync(full, P, k - 1);
+  const bool stays = act && rank >= 1 && !(n + upto <= b * (int64_t)(rank + 1));
+  const int k = max(1, (int)__reduce_max_sync(full, stays ? (unsigned)(rank + 1) : 0u));
+  const unsigned at = __ballot_sync(full, act && rank == k - 1);  // the lane at sorted position k - 1
+  const int64_t Pk = __shfl_sync(full, upto, __ffs(at) - 1);
   const int64_t level = (n + Pk) / k;
   int64_t give = 0;
-  if (lane < k) give = level - ld > 0 ? level - ld : 0;
+  if (act && rank < k) give = level - b > 0 ? level - b : 0;
   int64_t used = give;
   for (int o = 16; o > 0; o >>= 1) used += __shfl_xor_sync(full, used, o);
   const int64_t rem = n - used;
-  if (lane < k && rem > 0) give += rem / k + (lane < rem % k ? 1 : 0);
-  return __shfl_sync(full, give, act ? rank : 0);  // out[lane] = give[rank of lane]
+  if (act && rank < k && rem > 0) give += rem / k + (rank < rem % k ? 1 : 0);
+  return give;
 }
 #endif
 

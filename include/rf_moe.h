@@ -8,6 +8,11 @@
  * exception crosses this boundary.  rf_moe_last_error() returns the message
  * of the calling thread's most recent failure.
  *
+ * An empty batch is valid: with T == 0 (or no rows, for the grouped GEMMs) the
+ * router, permute, grouped GEMMs and combines accept null pointers for the
+ * zero-size token and row buffers (what a zero-row tensor hands over) and
+ * return RF_OK; the permute still writes its (all-zero) offsets and counts.
+ *
  * Row layout shared by the stages: the T*K (token, slot) pairs are grouped by
  * expert ("permuted rows").  Expert e owns rows
  *     [expert_offsets[e], expert_offsets[e] + expert_counts[e])

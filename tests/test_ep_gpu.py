@@ -155,6 +155,69 @@ def test_ep_two_ranks_match_single_process(cuda_ok):
     assert not bad, f"ranks {bad} failed:\n{report}"
 
 
+@pytest.mark.parametrize("R", [40, 64])
+def test_device_plan_with_many_holders_matches_host_plan(cuda_ok, R):
+    """The device planner splits a replicated expert's rows on one warp (one
+    lane per holder) and falls back to its first thread past 32 holders: with
+    an expert on every rank, one on 21 ranks and one on 6 (and ranks that hold
+    no primary expert), every rank's plan tables equal the host planner's."""
+    import numpy as np
+    from reframework_b200 import _lib
+    from reframework_b200.parallel.ep import shard_range
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    E = 8
+    rng = np.random.default_rng(R)
+    slots = [list(range(*shard_range(E, R, r))) for r in range(R)]
+    for r in range(R):
+        if 0 not in slots[r]:
+            slots[r].append(0)
+        if 8 <= r < 29 and 1 not in slots[r]:
+            slots[r].append(1)
+        if 30 <= r < 36 and 2 not in slots[r]:
+            slots[r].append(2)
+    p = np.exp(rng.normal(size=E))
+    cnt_np = np.stack([rng.multinomial(int(rng.integers(0, 3000)), p / p.sum()) for _ in range(R)]).astype(np.int32)
+    flat = np.ascontiguousarray([e for s in slots for e in s], dtype=np.int32)
+    offs = np.ascontiguousarray(np.cumsum([0] + [len(s) for s in slots]), dtype=np.int32)
+    cnt = torch.from_numpy(cnt_np).to(dev)
+    flat_d, offs_d = torch.from_numpy(flat).to(dev), torch.from_numpy(offs).to(dev)
+    M = np.zeros(R * R, np.int64)
+    assert L.rf_moe_ep_pair_rows(cnt_np.ctypes.data, R, E, flat.ctypes.data, offs.ctypes.data, 4, M.ctypes.data) == 0
+    M = M.reshape(R, R)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    nslots = int(flat.size)
+    cap_recv = int(cnt_np.sum()) + 1
+    back_cap = int(cnt_np.sum(1).max()) + 1
+    for me in (0, 7, 8, 29, 33, R - 1):
+        S = len(slots[me])
+        nb = L.rf_moe_ep_devplan_workspace_size(R, E, S, nslots)
+        w = torch.zeros(nb, dtype=torch.uint8, device=dev)
+        lo = np.zeros(_lib.EP_DEVPLAN_LAYOUT_N, np.int64)
+        assert L.rf_moe_ep_devplan_layout(R, E, S, nslots, lo.ctypes.data) == 0
+        assert L.rf_moe_ep_devplan(cnt.data_ptr(), flat_d.data_ptr(), offs_d.data_ptr(), R, E, me, S, nslots, 128, 4,
+                                   cap_recv, back_cap, cap_recv + S * 128, w.data_ptr(), nb, st) == 0
+        torch.cuda.synchronize()
+        wb = w.cpu().numpy()
+        i64 = lambda off, n: wb[off:off + 8 * n].view(np.int64)  # noqa: E731
+        i32 = lambda off, n: wb[off:off + 4 * n].view(np.int32)  # noqa: E731
+        send = np.zeros(R, np.int64)
+        recvs = np.zeros(R, np.int64)
+        hl = np.zeros(15, np.int64)
+        buf = np.zeros(4 * int(cnt_np.sum()) + 4096, np.int32)
+        assert L.rf_moe_ep_plan(cnt_np.ctypes.data, R, E, me, flat.ctypes.data, offs.ctypes.data, 128, 4,
+                                send.ctypes.data, recvs.ctypes.data, buf.ctypes.data, buf.size, hl.ctypes.data) == 0
+        assert i32(lo[2], 1)[0] == 0, "device plan overflowed"
+        assert np.array_equal(i64(lo[6], R + 1), np.concatenate([[0], np.cumsum(send)]))
+        assert np.array_equal(i64(lo[8], R + 1), np.concatenate([[0], np.cumsum(recvs)]))
+        assert np.array_equal(i64(lo[7], R), M[:me].sum(0) if me else np.zeros(R))
+        assert np.array_equal(i64(lo[9], R), M[:, :me].sum(1) if me else np.zeros(R))
+        seg = lambda i: buf[hl[2 * i]:hl[2 * i] + hl[2 * i + 1]]  # noqa: E731
+        assert np.array_equal(i32(lo[0], S + 1), seg(2)) and np.array_equal(i32(lo[1], S), seg(3))
+        assert i32(lo[10], 1)[0] == hl[13] and i64(lo[11], 1)[0] == hl[12]
+    assert _lib.device_status() == 0
+
+
 @pytest.mark.parametrize("seed", range(4))
 def test_device_plan_matches_host_plan_and_round_trips(cuda_ok, seed):
     """rf_moe_ep_devplan == rf_moe_ep_plan / rf_moe_ep_pair_rows for every rank,

@@ -1,6 +1,7 @@
-"""Parity at the benchmark's full size (Mixtral-8x7B shape, 4096 tokens) and a
-GEMM case where every CTA runs many tiles (accumulator double buffering and
-barrier phase wrap-around)."""
+"""Parity at the benchmark configurations' full sizes (C2 Mixtral-8x7B, C3
+decode, C4 DeepSeek-V2-Lite with its expert-parallel split emulated, C5 with the
+offload cache) and a GEMM case where every CTA runs many tiles (accumulator
+double buffering and barrier phase wrap-around)."""
 
 import numpy as np
 import pytest
@@ -325,3 +326,44 @@ def test_c4_full_size_ep_emulated_matches_single_process(R, redundant, overlap):
     with torch.no_grad():
         got = _emulated_ep_forward(moe, x, R, placement, overlap=overlap)
     assert torch.equal(got, ref), f"R={R} overlap={overlap}: EP output differs from the single-process layer"
+
+
+def test_c5_full_size_offload_equals_resident():
+    """Mixtral-8x22B shape at its benchmark size (H6144 E8 top-2 I16384, 2048
+    tokens per step, per-step Dirichlet(0.3) router bias) with the expert
+    offload cache of 4 device slots: six steps of the exact streaming forward
+    (experts copied from the pinned host pool into evicted slots on the copy
+    stream while earlier experts compute) give the resident layer's outputs bit
+    for bit — the same kernels over the same rows; the resident layer's parity
+    with the reference is checked at full size above (C2) and on the fixtures.
+    The cache counts one hit or miss per routed expert and step."""
+    cfg = CONFIGS["c5_mixtral22b_offload"]
+    d = generate(cfg, device=str(DEV), with_x=False)
+
+    def layer():
+        m = FusedMoE(cfg.experts, cfg.top_k, cfg.hidden, cfg.inter, dtype=cfg.dtype,
+                     router_dtype=torch.float32, device=DEV)
+        with torch.no_grad():
+            m.gate.copy_(d["gate"])
+            w1b, w2b = m._resident_banks()
+            w1b.copy_(d["w1"])
+            w2b.copy_(d["w2"])
+        return m
+
+    resident, offloaded = layer(), layer()
+    cache = offloaded.build_offload_cache(DEV, lru_capacity=4)
+    torch.cuda.empty_cache()
+    g = torch.Generator(device=DEV).manual_seed(cfg.seed + 101)
+    x = torch.randn(cfg.tokens, cfg.hidden, generator=g, device=DEV, dtype=cfg.dtype)
+    routed = 0
+    with torch.no_grad():
+        for s in range(6):
+            resident.set_router_bias(d["bias"][s])
+            offloaded.set_router_bias(d["bias"][s])
+            a = resident(x)
+            b = offloaded(x)
+            routed += int((torch.bincount(resident.route(x)[1].reshape(-1), minlength=cfg.experts) > 0).sum())
+            assert torch.equal(a, b), f"step {s}: offloaded output differs from the resident layer"
+    st = cache.stats
+    assert st.hits + st.misses == routed
+    assert st.misses > 0 and st.hits > 0

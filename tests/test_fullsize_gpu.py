@@ -367,3 +367,37 @@ def test_c5_full_size_offload_equals_resident():
     st = cache.stats
     assert st.hits + st.misses == routed
     assert st.misses > 0 and st.hits > 0
+
+
+@pytest.mark.parametrize("name", ["c2_mixtral_bf16", "c3_qwen_decode"])
+def test_full_size_graph_replay_equals_eager(name):
+    """The bench configurations' forwards captured in a CUDA graph (the decode
+    path's form) replay to the eager forward's bits, twice in a row (the tile
+    counters and permute scratch are reused across replays)."""
+    from reframework_b200.moe.graph import capture_forward
+    cfg = CONFIGS[name]
+    d = generate(cfg, device=str(DEV), with_x=False)
+    moe = FusedMoE(cfg.experts, cfg.top_k, cfg.hidden, cfg.inter, dtype=cfg.dtype, router_dtype=torch.float32,
+                   num_shared_experts=cfg.shared_count, shared_intermediate_size=cfg.shared_inter,
+                   shared_expert_gate=cfg.shared_gate, device=DEV)
+    with torch.no_grad():
+        moe.gate.copy_(d["gate"])
+        w1b, w2b = moe._resident_banks()
+        w1b.copy_(d["w1"])
+        w2b.copy_(d["w2"])
+        if cfg.shared_count:
+            moe.shared_w1.copy_(d["shared_w1"])
+            moe.shared_w2.copy_(d["shared_w2"])
+            if cfg.shared_gate:
+                moe.shared_gate.copy_(d["shared_gate"])
+    if d["bias"] is not None:
+        moe.set_router_bias(d["bias"][0])
+    del d
+    g = torch.Generator(device=DEV).manual_seed(cfg.seed + 101)
+    x = torch.randn(cfg.tokens, cfg.hidden, generator=g, device=DEV, dtype=cfg.dtype)
+    with torch.no_grad():
+        eager = moe(x).clone()
+        graphed = capture_forward(moe, x)
+        first = graphed(x).clone()
+        second = graphed(x).clone()
+    assert torch.equal(first, eager) and torch.equal(second, eager)

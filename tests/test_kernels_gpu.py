@@ -168,7 +168,7 @@ def test_permute_random_stable(T, Kk, E, align):
     assert np.array_equal(got, order)
 
 
-@pytest.mark.parametrize("align", [1, 128])
+@pytest.mark.parametrize("align", [1, 64, 128, 256])
 @pytest.mark.parametrize("T,Kk,E,dtype", [
     (1, 1, 1, torch.bfloat16), (37, 3, 5, torch.float32), (64, 4, 60, torch.bfloat16),
     (256, 4, 256, torch.float16),   # the largest decode-sized case: 1024 pairs, 256 experts

@@ -438,3 +438,59 @@ def test_device_planner_on_host_rejects_bad_placements_and_small_buffers():
         st, wb, lo = _devplan_host(cnt, fl, of, R, E, 0, 1, 64, 80, 400, S=S)
         assert st == 1, (fl, of, S)
         assert wb[lo[2]:lo[2] + 4].view(np.int32)[0] == 1
+
+
+def _waterfill_scalar(n, base):
+    """The planner's split of n rows over holders with current loads `base`
+    (waterfill_dev in csrc/ep_devplan.cu, the host planner's steps)."""
+    m = len(base)
+    order = sorted(range(m), key=lambda i: (base[i], i))
+    loads = [base[o] for o in order]
+    k = m
+    while k > 1 and n + sum(loads[:k]) <= loads[k - 1] * k:
+        k -= 1
+    level = (n + sum(loads[:k])) // k
+    give = [max(level - loads[i], 0) if i < k else 0 for i in range(m)]
+    rem = n - sum(give)
+    i = 0
+    while rem > 0:
+        give[i % k] += 1
+        i += 1
+        rem -= 1
+    out = [0] * m
+    for pos in range(m):
+        out[order[pos]] = give[pos]
+    return out
+
+
+def _waterfill_by_rank(n, base):
+    """The same split in the per-holder form the device planner's warp uses
+    (waterfill_warp): each holder's stable rank and the sorted-load prefix up
+    to it, the cut-off as the largest position whose holder still takes rows,
+    then the level and the remainder for the first sorted positions."""
+    m = len(base)
+    rank = [sum(1 for j in range(m) if base[j] < base[i] or (base[j] == base[i] and j < i)) for i in range(m)]
+    upto = [sum(base[j] for j in range(m) if rank[j] <= rank[i]) for i in range(m)]
+    k = max([rank[i] + 1 for i in range(m) if rank[i] >= 1 and not (n + upto[i] <= base[i] * (rank[i] + 1))],
+            default=1)
+    pk = next(upto[i] for i in range(m) if rank[i] == k - 1)
+    level = (n + pk) // k
+    give = [max(level - base[i], 0) if rank[i] < k else 0 for i in range(m)]
+    rem = n - sum(give)
+    if rem > 0:
+        give = [g + (rem // k + (1 if rank[i] < rem % k else 0)) if rank[i] < k else g for i, g in enumerate(give)]
+    return give
+
+
+def test_warp_split_formulation_equals_the_scalar_water_filling():
+    """The device planner splits a replicated expert's rows with one warp lane
+    per holder; its per-holder formulation gives the scalar split's rows on
+    random loads with ties, zeros and large values (the GPU tests then compare
+    the device plans with the host planner's)."""
+    rng = np.random.default_rng(5)
+    for _ in range(20000):
+        m = int(rng.integers(1, 33))
+        hi = int(rng.choice([3, 10, 1000, 10 ** 9]))
+        base = [int(v) for v in rng.integers(0, hi + 1, size=m)]
+        n = int(rng.integers(0, int(rng.choice([5, 100, 10 ** 6, 10 ** 10])) + 1))
+        assert _waterfill_by_rank(n, base) == _waterfill_scalar(n, base), (n, base)
